@@ -1,0 +1,178 @@
+/* libshahd_b200 — B200 (sm_100a) backend for the Shahd KV-cached decode path.
+ *
+ * A C-ABI shared library the Bun/TypeScript host loads through bun:ffi, as it loads
+ * GoKernels/matmul.dll today. Two surfaces:
+ *   1. the matmul-level seam of the Go FFI library (same symbol names and signatures), so the
+ *      reference's GoFfiBackend loader path (Brain/ComputeBackend/GoFfiBackend.ts:92-151) works as is;
+ *   2. a decode-level session API (device-resident weights, paged KV cache, batched cached steps,
+ *      on-device greedy / seeded sampling) that takes over CachedDecoder / CachedGenerate.
+ * All host buffers are caller-owned and only read or written during a call; the library never keeps a
+ * host pointer. Device memory behind a session is owned by the session.
+ *
+ * Reference paths below are relative to the reference repository (Khaymah/shahd-llm-stack).
+ */
+#ifndef SHAHD_B200_H
+#define SHAHD_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes of the int-returning entry points ------------------------------------------ */
+#define SHAHD_OK 0
+#define SHAHD_EINVAL (-1)   /* bad argument (the message names it, like ValidateMatMulArgs does) */
+#define SHAHD_ENODEV (-2)   /* no usable sm_100 device */
+#define SHAHD_ENOMEM (-3)   /* device allocation failed or KV pool exhausted */
+#define SHAHD_ECUDA (-4)    /* a CUDA call failed */
+#define SHAHD_ESTATE (-5)   /* call not valid in the session's current state */
+#define SHAHD_ETIMEOUT (-6) /* a bounded device-side wait gave up (kernel reported it) */
+
+/* ================================================================================================
+ * 1. Matmul-level seam: drop-in for the Go FFI exports (GoKernels/ffi/matmul.go:96-118,218-395).
+ *    Host pointers, row-major, i32 dims, synchronous. They return void like the Go exports; a bad
+ *    argument or a device failure leaves `out` untouched and records ShahdLastError().
+ * ============================================================================================== */
+
+/* out[M,N] = a[M,K] @ b[K,N] (overwrite).                       replaces MatMulF64, matmul.go:218-235 */
+void MatMulF64(const double* a, const double* b, double* out, int m, int k, int n);
+/* out[M,N] (+)= a[M,K] @ btᵀ, bt stored [N,K]; acc!=0 adds.      replaces MatMulNTF64, matmul.go:242-245 */
+void MatMulNTF64(const double* a, const double* bt, double* out, int m, int k, int n, int acc);
+/* db[K,N] (+)= aᵀ @ dout, a [M,K], dout [M,N].                   replaces MatMulTNF64, matmul.go:252-289 */
+void MatMulTNF64(const double* a, const double* dout, double* db, int m, int k, int n, int acc);
+/* f32 twins (fp32 FMA accumulation on the GPU).                  replace matmul.go:329-395 */
+void MatMulF32(const float* a, const float* b, float* out, int m, int k, int n);
+void MatMulNTF32(const float* a, const float* bt, float* out, int m, int k, int n, int acc);
+void MatMulTNF32(const float* a, const float* dout, float* db, int m, int k, int n, int acc);
+/* Accepted for loader compatibility (matmul.go:96-99); the GPU path has no CPU fan-out to cap. */
+void SetKernelThreads(int n);
+/* 1 when the fast kernels can run. For this library that means a usable sm_100 device, so the
+ * reference selector's probe (BackendSelector.ts:74-93, matmul.go:106-109) keeps working unchanged. */
+int ShahdCpuSupportsAvx2Fma(void);
+/* Test hook with the meaning of matmul.go:111-118: force != 0 makes every decode projection run the
+ * CUDA-core (SIMT) kernels whatever the row count, so the tensor-core tiles can be parity-checked
+ * against them; 0 restores the row-count rule. Process-wide. */
+void SetScalarKernels(int force);
+
+/* ---- additions of this library ---------------------------------------------------------------- */
+/* 1 when device 0 is an sm_100 GPU this build can run on, else 0 (the "Gpu" slot probe,
+ * BackendSelector.ts:134-137). */
+int ShahdGpuAvailable(void);
+/* Thread-local message of the last failure on this thread ("" when none). */
+const char* ShahdLastError(void);
+/* Row count from which decode projections use tcgen05 tiles instead of the SIMT kernel (default 32;
+ * 1 forces tensor cores everywhere). Process-wide tuning/test hook; no counterpart in the reference. */
+void ShahdSetTensorCoreMinRows(int rows);
+/* First error code a kernel recorded for a bounded device-side wait that gave up (0 = none). */
+int ShahdDeviceErrorFlag(void);
+/* Device-pointer MatMulNT on the tensor cores: out[M,N] (+)= a[M,K] @ btᵀ with a, bt bf16 row-major
+ * on the device, out fp32; tcgen05/TMEM tiles fed by TMA. K must be a multiple of 8 and the three
+ * pointers 16-byte aligned. stream may be 0. Returns a status code.  (MatMulNtInto/MatMulNtAcc of
+ * ComputeBackend.ts:29-36 for device-resident operands.) */
+int ShahdMatMulNTBF16Device(const void* a, const void* bt, float* out, int m, int k, int n, int acc, void* stream);
+
+/* ================================================================================================
+ * 2. Decode-level session API (new surface; nothing in the reference plays this role — its decode
+ *    row math is inline TS, Brain/Sampling/CachedRowMath.ts).
+ * ============================================================================================== */
+
+/* Model knobs of Brain/Config/Constants.ts:11-26 with Derived values resolved (DeriveConfig.ts:8-20). */
+typedef struct ShahdModelCfg {
+  int32_t embed_dim;
+  int32_t num_layers;
+  int32_t num_heads;
+  int32_t kv_heads;        /* Derived.KvHeads (NumHeads for MHA) */
+  int32_t block_size;      /* context window = KV capacity */
+  int32_t vocab_size;
+  int32_t mlp_hidden;      /* Derived.MlpHidden = round(EmbedDim * MlpRatio) */
+  int32_t position_scheme; /* 0 = Learned, 1 = Rope */
+  int32_t norm_kind;       /* 0 = LayerNorm, 1 = RmsNorm */
+  int32_t mlp_kind;        /* 0 = Relu, 1 = SwiGlu, 2 = GeGlu */
+  int32_t weight_tying;    /* 1 = LM head is Wteᵀ */
+  int32_t reserved;        /* 0 */
+  double layer_norm_eps;   /* Model.LayerNormEps */
+  double rope_base;        /* RoPE theta; the reference always uses 10000 (RotaryEmbedding.ts:13) */
+} ShahdModelCfg;
+
+/* SamplingOptions (Brain/Sampling/Distribution.ts:11-15). */
+typedef struct ShahdSampling {
+  double temperature; /* <= 0 => greedy argmax */
+  int32_t top_k;      /* 0 => disabled */
+  int32_t reserved;
+  double top_p;       /* 1 => disabled */
+} ShahdSampling;
+
+typedef struct ShahdSessionOpts {
+  int32_t max_seqs; /* sequences held at once (slots 0..max_seqs-1) */
+  int32_t kv_pages; /* KV pool size in pages of 64 positions; 0 = max_seqs * ceil(block_size / 64) */
+  int32_t device;   /* CUDA device ordinal */
+  int32_t flags;    /* 0 */
+} ShahdSessionOpts;
+
+typedef struct ShahdSession ShahdSession;
+
+/* Number of parameters of Shahd.Parameters() (Brain/Nn/Shahd.ts:87-94) for cfg, or -1. */
+int64_t shahd_param_count(const ShahdModelCfg* cfg);
+
+/* The reference's weight initialization: new Shahd(Config, CreateRngStreams(seed).InitRng)
+ * (Shahd.ts:30-39, InitPolicy.ts:15-24, SeededRng.ts) with InitScale 0.02 and UseScaledResidualInit,
+ * written as f32 in Parameters() order. count must equal shahd_param_count(cfg). */
+int shahd_init_params(const ShahdModelCfg* cfg, uint32_t seed, float* params, int64_t count);
+
+/* Copies the parameters (Parameters() order; params_f64 = 0: float, 1: double) to the device,
+ * repacked to BF16 [out,in] tiles plus fp32 norms/embeddings, and allocates the paged KV pool. */
+int shahd_session_create(const ShahdModelCfg* cfg, const void* params, int32_t params_f64, int64_t params_count,
+                         const ShahdSessionOpts* opts, ShahdSession** out);
+int shahd_session_destroy(ShahdSession* s);
+
+/* Forget the cached tokens of the listed slots (KvCache.Reset, KvCache.ts:62-64); frees their pages. */
+int shahd_reset(ShahdSession* s, const int32_t* slots, int32_t n);
+/* Cached length of one slot (KvCache.Length, KvCache.ts:52-54), or a negative status. */
+int32_t shahd_seq_length(ShahdSession* s, int32_t slot);
+
+/* PrefillCache (Brain/Sampling/CachedForward.ts:100-110) for n slots at once: slot i is reset and
+ * filled with ids[offsets[i] .. offsets[i+1]) at window positions 0..len-1. offsets has n+1 entries. */
+int shahd_prefill(ShahdSession* s, const int32_t* slots, const int32_t* ids, const int32_t* offsets, int32_t n);
+
+/* CachedForwardStep (CachedForward.ts:94-96) for n slots at once: token i enters slot i at position
+ * == its cached length. logits (nullable) receives [n, vocab] fp32; next_ids (nullable) receives the
+ * greedy argmax of each row (ArgmaxOf, Distribution.ts:19-30). */
+int shahd_step(ShahdSession* s, const int32_t* slots, const int32_t* tokens, int32_t n, float* logits,
+               int32_t* next_ids);
+
+/* CachedGenerate (CachedForward.ts:153-171) for n independent sequences, slots 0..n-1 (reset first).
+ * prompts packed with offsets (n+1 entries); out_ids receives [n, max_new] new ids; rng_states [n]
+ * (SeededRng states, one per sequence; read and written back; unused when greedy). */
+int shahd_generate(ShahdSession* s, const int32_t* prompts, const int32_t* offsets, int32_t n, int32_t max_new,
+                   const ShahdSampling* opts, uint32_t* rng_states, int32_t* out_ids);
+
+/* Device-pointer twin of shahd_generate: prompts/offsets/out_ids/rng_states are device buffers and the
+ * call is asynchronous on `stream` (0 = the session's stream). offsets must also be given on the host
+ * (host_offsets) because the host plans pages and window slides from the lengths. */
+int shahd_generate_device(ShahdSession* s, const int32_t* d_prompts, const int32_t* host_offsets, int32_t n,
+                          int32_t max_new, const ShahdSampling* opts, uint32_t* d_rng_states, int32_t* d_out_ids,
+                          void* stream);
+
+/* Wait for the session's outstanding device work; returns the first recorded device error, if any. */
+int shahd_sync(ShahdSession* s);
+
+/* Kernel launches of one decode step of n rows (embed, 5 per layer, head, finish). */
+int32_t shahd_step_launches(ShahdSession* s, int32_t n);
+/* Every kernel this session has launched so far. */
+int64_t shahd_kernel_launches(ShahdSession* s);
+/* Measurement hook (no counterpart in the reference): while enabled, every kernel launch of the session
+ * is bracketed by CUDA events on its own stream and tagged with its class and algorithmic bytes.
+ * Enabling (or disabling) clears the records. */
+int shahd_profile(ShahdSession* s, int32_t enable);
+/* Totals over the records of one class: 0 = decode attention, 1 = projections (GEMV/GEMM incl. the
+ * LM head), 2 = embed/finish. total_ms sums the launches' event times; bytes sums their algorithmic
+ * bytes (weights once + activations + KV rows read). */
+int shahd_profile_read(ShahdSession* s, int32_t kind, double* total_ms, int64_t* launches, double* bytes);
+
+const char* shahd_last_error(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

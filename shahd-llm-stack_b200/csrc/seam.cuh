@@ -1,0 +1,409 @@
+// Matmul-level seam of libshahd_b200: the Go FFI exports (GoKernels/ffi/matmul.go:96-395) on the GPU,
+// and the device-pointer bf16 MatMulNT on the tensor cores.
+#include <cstdarg>
+#include <cstring>
+#include <mutex>
+#include <string>
+
+#include "../../include/shahd_b200.h"
+#include "common.cuh"
+#include "umma_linear.cuh"
+
+namespace shahd {
+
+int g_umma_min_rows = 32;
+
+// ---- thread-local last error --------------------------------------------------------------------
+static thread_local std::string t_error;
+
+void SetError(const char* fmt, ...) {
+  char buf[1024];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof buf, fmt, ap);
+  va_end(ap);
+  t_error = buf;
+}
+const char* GetError() { return t_error.c_str(); }
+void ClearError() { t_error.clear(); }
+
+// ---- SIMT GEMM for the f32/f64 seam: C[i,j] (+)= sum_p A(i,p) B(p,j) with generic strides ---------
+
+constexpr int kGT = 64, kGK = 16;
+
+template <typename T>
+__global__ void __launch_bounds__(256) GemmSimtKernel(const T* __restrict__ A, long long sai, long long sap,
+                                                      const T* __restrict__ B, long long sbp, long long sbj,
+                                                      T* __restrict__ C, int M, int N, int K, int acc) {
+  __shared__ T As[kGK][kGT + 1];
+  __shared__ T Bs[kGK][kGT + 1];
+  const int tx = threadIdx.x % 16, ty = threadIdx.x / 16;
+  const int i0 = blockIdx.y * kGT, j0 = blockIdx.x * kGT;
+  T accv[4][4];
+#pragma unroll
+  for (int a = 0; a < 4; a++)
+#pragma unroll
+    for (int b = 0; b < 4; b++) accv[a][b] = 0;
+  for (int p0 = 0; p0 < K; p0 += kGK) {
+    for (int e = threadIdx.x; e < kGK * kGT; e += 256) {
+      // A tile: element (i, p) with p fastest when A is K-contiguous, else i fastest
+      int pi, ii;
+      if (sap == 1) { pi = e % kGK; ii = e / kGK; } else { ii = e % kGT; pi = e / kGT; }
+      const int gi = i0 + ii, gp = p0 + pi;
+      As[pi][ii] = (gi < M && gp < K) ? A[gi * sai + gp * sap] : T(0);
+      int pj, jj;
+      if (sbj == 1) { jj = e % kGT; pj = e / kGT; } else { pj = e % kGK; jj = e / kGK; }
+      const int gj = j0 + jj, gq = p0 + pj;
+      Bs[pj][jj] = (gj < N && gq < K) ? B[gq * sbp + gj * sbj] : T(0);
+    }
+    __syncthreads();
+#pragma unroll
+    for (int p = 0; p < kGK; p++) {
+      T a[4], b[4];
+#pragma unroll
+      for (int q = 0; q < 4; q++) {
+        a[q] = As[p][ty + 16 * q];
+        b[q] = Bs[p][tx + 16 * q];
+      }
+#pragma unroll
+      for (int x = 0; x < 4; x++)
+#pragma unroll
+        for (int y = 0; y < 4; y++) accv[x][y] = fma(a[x], b[y], accv[x][y]);
+    }
+    __syncthreads();
+  }
+#pragma unroll
+  for (int x = 0; x < 4; x++)
+#pragma unroll
+    for (int y = 0; y < 4; y++) {
+      const int i = i0 + ty + 16 * x, j = j0 + tx + 16 * y;
+      if (i < M && j < N) {
+        T* c = C + (size_t)i * N + j;
+        *c = acc ? *c + accv[x][y] : accv[x][y];
+      }
+    }
+}
+
+// ---- per-device workspace for the host-pointer seam ---------------------------------------------
+struct Workspace {
+  std::mutex mu;
+  void* buf = nullptr;
+  size_t cap = 0;
+  cudaStream_t stream = nullptr;
+};
+
+static Workspace& WorkspaceFor(int dev) {
+  static Workspace ws[64];
+  return ws[dev & 63];
+}
+
+static int DeviceOk() {
+  int n = 0;
+  if (cudaGetDeviceCount(&n) != cudaSuccess || n < 1) return 0;
+  cudaDeviceProp p;
+  if (cudaGetDeviceProperties(&p, 0) != cudaSuccess) return 0;
+  return p.major == 10 ? 1 : 0;
+}
+
+static bool CheckDims(const char* op, long long m, long long k, long long n) {
+  const char* names[3] = {"M", "K", "N"};
+  long long v[3] = {m, k, n};
+  for (int i = 0; i < 3; i++)
+    if (v[i] < 1 || v[i] > 2147483647LL) {
+      SetError("%s: dimension %s must be an integer in [1, 2147483647], got %lld", op, names[i], v[i]);
+      return false;
+    }
+  return true;
+}
+
+enum Layout { kNN, kNT, kTN };
+
+template <typename T>
+static void RunSeam(const char* op, Layout lay, const T* a, const T* b, T* out, int m, int k, int n, int acc) {
+  ClearError();
+  if (!CheckDims(op, m, k, n)) return;
+  if (!a || !b || !out) {
+    SetError("%s: null buffer (a native kernel cannot take a pointer to zero-length memory)", op);
+    return;
+  }
+  if (!DeviceOk()) {
+    SetError("%s: no usable sm_100 device", op);
+    return;
+  }
+  int dev = 0;
+  cudaGetDevice(&dev);
+  Workspace& w = WorkspaceFor(dev);
+  std::lock_guard<std::mutex> g(w.mu);
+  const size_t na = (size_t)m * k, nb = lay == kTN ? (size_t)m * n : (size_t)k * n;
+  const size_t no = lay == kTN ? (size_t)k * n : (size_t)m * n;
+  const size_t need = (na + nb + no) * sizeof(T) + 256;
+  if (w.cap < need) {
+    if (w.buf) cudaFree(w.buf);
+    w.buf = nullptr;
+    w.cap = 0;
+    if (cudaMalloc(&w.buf, need) != cudaSuccess) {
+      SetError("%s: cudaMalloc of %zu bytes failed", op, need);
+      return;
+    }
+    w.cap = need;
+  }
+  if (!w.stream) cudaStreamCreateWithFlags(&w.stream, cudaStreamNonBlocking);
+  T* da = static_cast<T*>(w.buf);
+  T* db = da + na;
+  T* dc = db + nb;
+  cudaMemcpyAsync(da, a, na * sizeof(T), cudaMemcpyHostToDevice, w.stream);
+  cudaMemcpyAsync(db, b, nb * sizeof(T), cudaMemcpyHostToDevice, w.stream);
+  if (acc) cudaMemcpyAsync(dc, out, no * sizeof(T), cudaMemcpyHostToDevice, w.stream);
+  int M = m, N = n, K = k;
+  long long sai, sap, sbp, sbj;
+  if (lay == kNN) { sai = k; sap = 1; sbp = n; sbj = 1; }
+  else if (lay == kNT) { sai = k; sap = 1; sbp = 1; sbj = k; }
+  else { M = k; K = m; sai = 1; sap = k; sbp = n; sbj = 1; }  // db[K,N] = aᵀ @ dout
+  dim3 grid(CeilDiv(N, kGT), CeilDiv(M, kGT));
+  GemmSimtKernel<T><<<grid, 256, 0, w.stream>>>(da, sai, sap, db, sbp, sbj, dc, M, N, K, acc);
+  cudaMemcpyAsync(out, dc, no * sizeof(T), cudaMemcpyDeviceToHost, w.stream);
+  cudaError_t e = cudaStreamSynchronize(w.stream);
+  if (e == cudaSuccess) e = cudaGetLastError();
+  if (e != cudaSuccess) SetError("%s: device error: %s", op, cudaGetErrorString(e));
+}
+
+// ---- tcgen05 GEMM, both operands by TMA, warp-specialized, persistent ---------------------------
+
+constexpr int kGemmBN = 128;
+constexpr int kGemmStages = 4;
+constexpr int kGemmThreads = 192;  // warp 0 TMA, warp 1 MMA, warps 2..5 epilogue
+constexpr int kGemmStageBytes = (kUmmaBM + kGemmBN) * kUmmaBK * 2;
+constexpr int kGemmSmem = kGemmStages * kGemmStageBytes + 1024 + 256;
+
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    GemmNtBf16Kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tb, float* out, int M,
+                     int N, int K, int acc) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kGemmStages * kGemmStageBytes);
+  uint64_t* empty = full + kGemmStages;
+  uint64_t* tfull = empty + kGemmStages;  // [2]
+  uint64_t* tempty = tfull + 2;           // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+  volatile int* s_abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int tiles_n = CeilDiv(N, kGemmBN), tiles = tiles_n * CeilDiv(M, kUmmaBM);
+  const int nk = CeilDiv(K, kUmmaBK);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kGemmStages; s++) {
+      MbarInit(&full[s], 1);
+      MbarInit(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; b++) {
+      MbarInit(&tfull[b], 1);
+      MbarInit(&tempty[b], 4);
+    }
+    *s_abort = 0;
+    FenceMbarInit();
+    PrefetchTmaDesc(&ta);
+    PrefetchTmaDesc(&tb);
+  }
+  __syncwarp();
+  if (warp == 1) {
+    TmemAlloc(tmem_slot, 2 * kGemmBN);
+    TmemRelinquish();
+  }
+  TcgenFenceBefore();
+  __syncthreads();
+  TcgenFenceAfter();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int it = 0;
+      for (int t = blockIdx.x; t < tiles && !*s_abort; t += gridDim.x) {
+        const int m0 = (t / tiles_n) * kUmmaBM, n0 = (t % tiles_n) * kGemmBN;
+        for (int kb = 0; kb < nk; kb++, it++) {
+          const int s = it % kGemmStages;
+          if (!MbarWaitBounded(&empty[s], ((it / kGemmStages) & 1) ^ 1, kWaitLimit)) {
+            atomicCAS(&g_shahd_device_error, 0, kDevErrGemmTimeout);
+            *s_abort = 1;
+            break;
+          }
+          uint8_t* sa = smem + s * kGemmStageBytes;
+          MbarArriveExpectTx(&full[s], kGemmStageBytes);
+          TmaLoad2D(sa, &ta, &full[s], kb * kUmmaBK, m0);
+          TmaLoad2D(sa + kUmmaBM * kUmmaBK * 2, &tb, &full[s], kb * kUmmaBK, n0);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t idesc = UmmaIdescBf16(kUmmaBM, kGemmBN);
+      int it = 0, tc = 0;
+      for (int t = blockIdx.x; t < tiles && !*s_abort; t += gridDim.x, tc++) {
+        const int buf = tc & 1;
+        if (!MbarWaitBounded(&tempty[buf], ((tc >> 1) & 1) ^ 1, kWaitLimit)) {
+          atomicCAS(&g_shahd_device_error, 0, kDevErrGemmTimeout);
+          *s_abort = 1;
+          break;
+        }
+        TcgenFenceAfter();
+        const uint32_t d = tmem + (uint32_t)(buf * kGemmBN);
+        for (int kb = 0; kb < nk; kb++, it++) {
+          const int s = it % kGemmStages;
+          if (!MbarWaitBounded(&full[s], (it / kGemmStages) & 1, kWaitLimit)) {
+            atomicCAS(&g_shahd_device_error, 0, kDevErrGemmTimeout);
+            *s_abort = 1;
+            break;
+          }
+          TcgenFenceAfter();
+          uint8_t* sa = smem + s * kGemmStageBytes;
+          const uint64_t ad = SmemDescSw128(SmemAddr(sa));
+          const uint64_t bd = SmemDescSw128(SmemAddr(sa + kUmmaBM * kUmmaBK * 2));
+#pragma unroll
+          for (int kk = 0; kk < kUmmaBK / 16; kk++)
+            UmmaBf16(d, ad + (uint64_t)(kk * 2), bd + (uint64_t)(kk * 2), idesc, (kb > 0 || kk > 0) ? 1u : 0u);
+          UmmaCommit(&empty[s]);
+        }
+        if (*s_abort) break;
+        UmmaCommit(&tfull[buf]);
+      }
+    }
+  } else {
+    // epilogue warps 2..5 own TMEM lane quadrants (warp % 4)
+    const int quad = warp & 3;
+    int tc = 0;
+    for (int t = blockIdx.x; t < tiles; t += gridDim.x, tc++) {
+      const int buf = tc & 1;
+      if (!MbarWaitBounded(&tfull[buf], (tc >> 1) & 1, kWaitLimit)) {
+        if (lane == 0) atomicCAS(&g_shahd_device_error, 0, kDevErrGemmTimeout);
+        *s_abort = 1;
+        break;
+      }
+      TcgenFenceAfter();
+      const int m0 = (t / tiles_n) * kUmmaBM, n0 = (t % tiles_n) * kGemmBN;
+      const int row = m0 + quad * 32 + lane;
+#pragma unroll 1
+      for (int c = 0; c < kGemmBN; c += 16) {
+        uint32_t u[16];
+        TmemLoad16(tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)(buf * kGemmBN + c), u);
+        TmemWaitLd();
+        if (row < M) {
+          float* o = out + (size_t)row * N + n0 + c;
+          if (n0 + c + 16 <= N && (N & 3) == 0) {
+#pragma unroll
+            for (int j = 0; j < 16; j += 4) {
+              float4 v = make_float4(__uint_as_float(u[j]), __uint_as_float(u[j + 1]), __uint_as_float(u[j + 2]),
+                                     __uint_as_float(u[j + 3]));
+              if (acc) {
+                const float4 p = *reinterpret_cast<const float4*>(o + j);
+                v.x += p.x; v.y += p.y; v.z += p.z; v.w += p.w;
+              }
+              *reinterpret_cast<float4*>(o + j) = v;
+            }
+          } else {
+            for (int j = 0; j < 16; j++)
+              if (n0 + c + j < N) o[j] = acc ? o[j] + __uint_as_float(u[j]) : __uint_as_float(u[j]);
+          }
+        }
+      }
+      TcgenFenceBefore();
+      __syncwarp();
+      if (lane == 0) MbarArrive(&tempty[buf]);
+    }
+  }
+  TcgenFenceBefore();
+  __syncthreads();
+  __syncwarp();
+  if (warp == 1) TmemDealloc(tmem, 2 * kGemmBN);
+}
+
+static int NumSMs(int dev) {
+  static int cache[64] = {0};
+  if (!cache[dev & 63]) cudaDeviceGetAttribute(&cache[dev & 63], cudaDevAttrMultiProcessorCount, dev);
+  return cache[dev & 63];
+}
+
+int GemmNtBf16(const void* a, const void* bt, float* out, int m, int k, int n, int acc, cudaStream_t st) {
+  if ((reinterpret_cast<uintptr_t>(a) | reinterpret_cast<uintptr_t>(bt) | reinterpret_cast<uintptr_t>(out)) & 15) {
+    SetError("ShahdMatMulNTBF16Device: pointers must be 16-byte aligned");
+    return SHAHD_EINVAL;
+  }
+  if (k % 8 != 0) {
+    SetError("ShahdMatMulNTBF16Device: K=%d must be a multiple of 8 (16-byte rows for TMA)", k);
+    return SHAHD_EINVAL;
+  }
+  CUtensorMap ta, tb;
+  if (!MakeTmaBf16(a, m, k, k, kUmmaBM, &ta) || !MakeTmaBf16(bt, n, k, k, kGemmBN, &tb)) {
+    SetError("ShahdMatMulNTBF16Device: cuTensorMapEncodeTiled failed");
+    return SHAHD_ECUDA;
+  }
+  static bool configured = false;
+  if (!configured) {
+    cudaFuncSetAttribute(GemmNtBf16Kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemmSmem);
+    configured = true;
+  }
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const int tiles = CeilDiv(n, kGemmBN) * CeilDiv(m, kUmmaBM);
+  const int grid = tiles < NumSMs(dev) ? tiles : NumSMs(dev);
+  GemmNtBf16Kernel<<<grid, kGemmThreads, kGemmSmem, st>>>(ta, tb, out, m, n, k, acc);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    SetError("ShahdMatMulNTBF16Device: launch failed: %s", cudaGetErrorString(e));
+    return SHAHD_ECUDA;
+  }
+  return SHAHD_OK;
+}
+
+}  // namespace shahd
+
+using namespace shahd;
+
+extern "C" {
+
+void MatMulF64(const double* a, const double* b, double* out, int m, int k, int n) {
+  RunSeam<double>("MatMulF64", kNN, a, b, out, m, k, n, 0);
+}
+void MatMulNTF64(const double* a, const double* bt, double* out, int m, int k, int n, int acc) {
+  RunSeam<double>("MatMulNTF64", kNT, a, bt, out, m, k, n, acc != 0);
+}
+void MatMulTNF64(const double* a, const double* dout, double* db, int m, int k, int n, int acc) {
+  RunSeam<double>("MatMulTNF64", kTN, a, dout, db, m, k, n, acc != 0);
+}
+void MatMulF32(const float* a, const float* b, float* out, int m, int k, int n) {
+  RunSeam<float>("MatMulF32", kNN, a, b, out, m, k, n, 0);
+}
+void MatMulNTF32(const float* a, const float* bt, float* out, int m, int k, int n, int acc) {
+  RunSeam<float>("MatMulNTF32", kNT, a, bt, out, m, k, n, acc != 0);
+}
+void MatMulTNF32(const float* a, const float* dout, float* db, int m, int k, int n, int acc) {
+  RunSeam<float>("MatMulTNF32", kTN, a, dout, db, m, k, n, acc != 0);
+}
+
+void SetKernelThreads(int n) { (void)n; }
+
+int ShahdCpuSupportsAvx2Fma(void) { return DeviceOk(); }
+
+void SetScalarKernels(int force) { g_umma_min_rows = force ? 0x7fffffff : 32; }
+
+int ShahdGpuAvailable(void) { return DeviceOk(); }
+
+const char* ShahdLastError(void) { return GetError(); }
+
+void ShahdSetTensorCoreMinRows(int rows) { g_umma_min_rows = rows < 1 ? 1 : rows; }
+
+int ShahdDeviceErrorFlag(void) {
+  int v = 0;
+  if (cudaMemcpyFromSymbol(&v, g_shahd_device_error, sizeof(int)) != cudaSuccess) return -1;
+  return v;
+}
+
+int ShahdMatMulNTBF16Device(const void* a, const void* bt, float* out, int m, int k, int n, int acc, void* stream) {
+  ClearError();
+  if (!CheckDims("ShahdMatMulNTBF16Device", m, k, n)) return SHAHD_EINVAL;
+  if (!a || !bt || !out) {
+    SetError("ShahdMatMulNTBF16Device: null pointer");
+    return SHAHD_EINVAL;
+  }
+  return GemmNtBf16(a, bt, out, m, k, n, acc, static_cast<cudaStream_t>(stream));
+}
+
+}  // extern "C"

@@ -1,0 +1,921 @@
+// Decode-level session: device-resident weights, paged KV pool, batched cached steps and the
+// on-device CachedGenerate loop (Brain/Sampling/CachedForward.ts:94-199) behind the C ABI of
+// include/shahd_b200.h.
+#include <algorithm>
+#include <cmath>
+#include <cstdarg>
+#include <cstring>
+#include <map>
+#include <mutex>
+#include <numeric>
+#include <vector>
+
+#include "../../include/shahd_b200.h"
+#include "decode_kernels.cuh"
+#include "params.h"
+#include "umma_linear.cuh"
+
+namespace shahd {
+
+struct Layer {
+  bf16 *w_qkv, *w_o, *w_up, *w_down;
+  float *ln1_g, *ln1_b, *ln2_g, *ln2_b, *b_fc, *b_proj;
+};
+
+struct GraphKey {
+  int n;
+  int mode;
+  bool operator<(const GraphKey& o) const { return n != o.n ? n < o.n : mode < o.mode; }
+};
+
+}  // namespace shahd
+
+struct ShahdSession {
+  ShahdModelCfg cfg;
+  int E, L, H, Hk, d, F, C, V, G;
+  int Ep, Fp, HDp;  // reduction lengths padded to multiples of 8
+  int Nqkv, Nup;
+  int device;
+  int max_seqs;
+  cudaStream_t stream;
+  std::mutex mu;
+  std::vector<void*> allocs;
+
+  std::vector<shahd::Layer> layers;
+  shahd::bf16* w_head;
+  float *head_bias, *lnf_g, *lnf_b, *wte, *wpe, *rope_cos, *rope_sin;
+
+  // paged KV pool
+  shahd::bf16* kv_pool;
+  size_t page_elems;
+  int kv_pages, max_blocks;
+  int* d_block_table;
+  int* h_block_table;  // pinned mirror
+  std::vector<int> free_pages;
+  std::vector<int> h_len;
+  int* d_seq_len;
+
+  // per-row scratch (capacity max_seqs rows)
+  float *x, *q, *ctx, *act, *logits, *am_val;
+  int* am_idx;
+  int am_stride;
+  float *part_o, *part_m, *part_l;
+  int* attn_counter;
+  int *d_slot, *d_tok, *d_pos, *d_next, *d_gen_count, *d_poff, *d_pf_slot, *d_pf_poff;
+  int* d_prompt;
+  size_t prompt_cap;
+  int* d_window;
+  int* d_out;
+  size_t out_cap;
+  int* h_pinned_rows;  // pinned staging for per-call row arrays
+  float* d_logits_full;
+
+  std::map<shahd::GraphKey, cudaGraphExec_t> graphs;
+
+  // measurement: kernel launch count, and optional CUDA-event timing per kernel class
+  long long launches = 0;
+  bool prof = false;
+  std::vector<cudaEvent_t> ev_pool;
+  size_t ev_used = 0;
+  struct ProfRec {
+    int kind;
+    size_t ev0, ev1;
+    double bytes;
+  };
+  std::vector<ProfRec> prof_recs;
+};
+
+namespace shahd {
+
+namespace {
+
+template <class T>
+int DevAlloc(ShahdSession* s, T** p, size_t count) {
+  void* v = nullptr;
+  if (count == 0) count = 1;
+  cudaError_t e = cudaMalloc(&v, count * sizeof(T));
+  if (e != cudaSuccess) {
+    SetError("cudaMalloc of %zu bytes failed: %s", count * sizeof(T), cudaGetErrorString(e));
+    return e == cudaErrorMemoryAllocation ? SHAHD_ENOMEM : SHAHD_ECUDA;
+  }
+  s->allocs.push_back(v);
+  *p = static_cast<T*>(v);
+  return SHAHD_OK;
+}
+
+#define SHAHD_TRY(expr)        \
+  do {                         \
+    int rc_ = (expr);          \
+    if (rc_ != SHAHD_OK) return rc_; \
+  } while (0)
+
+// ---- linear launcher: SIMT (few rows) or tcgen05 tiles (batched rows) ----------------------------
+
+template <int MT, int NORM, class Epi>
+void LaunchSimt(const LinearArgs& la, const Epi& epi, cudaStream_t st) {
+  const size_t smem = (size_t)MT * la.Kp * sizeof(float);
+  static bool configured = false;  // per template instance; the attribute is per function
+  if (!configured) {
+    cudaFuncSetAttribute(LinearSimtKernel<MT, NORM, Epi>, cudaFuncAttributeMaxDynamicSharedMemorySize, 224 * 1024);
+    configured = true;
+  }
+  dim3 grid(CeilDiv(la.N, kSimtCols), CeilDiv(la.M, MT));
+  LinearSimtKernel<MT, NORM, Epi><<<grid, kSimtWarps * 32, smem, st>>>(la, epi);
+}
+
+template <int NORM, class Epi>
+void LaunchLinearNorm(const LinearArgs& la, const Epi& epi, cudaStream_t st) {
+  if (la.M >= kUmmaMinRows && UmmaLinearSupported(la)) {
+    LaunchUmmaLinear<NORM, Epi>(la, epi, st);
+  } else if (la.M <= 1) {
+    LaunchSimt<1, NORM, Epi>(la, epi, st);
+  } else if (la.M <= 4) {
+    LaunchSimt<4, NORM, Epi>(la, epi, st);
+  } else {
+    LaunchSimt<16, NORM, Epi>(la, epi, st);
+  }
+}
+
+template <class Epi>
+void LaunchLinear(int norm, const LinearArgs& la, const Epi& epi, cudaStream_t st) {
+  if (norm == kNormRms) LaunchLinearNorm<kNormRms, Epi>(la, epi, st);
+  else if (norm == kNormLayer) LaunchLinearNorm<kNormLayer, Epi>(la, epi, st);
+  else LaunchLinearNorm<kNormNone, Epi>(la, epi, st);
+}
+
+// Number of argmax partial blocks the head launch produces per row.
+int HeadBlocks(const ShahdSession* s, int M) {
+  LinearArgs la{};
+  la.M = M;
+  la.K = s->E;
+  la.Kp = s->Ep;
+  la.N = s->V;
+  if (M >= kUmmaMinRows && UmmaLinearSupported(la)) return CeilDiv(la.N, UmmaBN(M, la.N));
+  return CeilDiv(s->V, kSimtCols);
+}
+
+struct StepPlan {
+  int M;
+  const int* slot;   // device [M]
+  const int* tok;    // device [M] (direct tokens) or nullptr
+  const int* poff;   // device [M] prompt gather offsets, or nullptr
+  const int* prompt; // device packed ids for the gather
+  bool head;         // run final norm + LM head + argmax
+  float* logits;     // device [M, V] or nullptr
+  int* next_ids;     // device [M] or nullptr
+  int* cur_tok;      // device [M] or nullptr
+  int* out_ids;      // device [M, out_ld] or nullptr
+  int out_ld;
+  long long attended;  // sum over rows of (position + 1): cached positions the attention reads
+};
+
+// ---- measurement hooks: kernel classes timed with CUDA events on the launching stream ---------------
+enum ProfKind { kProfAttention = 0, kProfLinear = 1, kProfOther = 2, kProfKinds = 3 };
+
+size_t ProfEvent(ShahdSession* s, cudaStream_t st) {
+  if (s->ev_used == s->ev_pool.size()) {
+    cudaEvent_t e;
+    cudaEventCreate(&e);
+    s->ev_pool.push_back(e);
+  }
+  cudaEventRecord(s->ev_pool[s->ev_used], st);
+  return s->ev_used++;
+}
+
+template <class F>
+void Timed(ShahdSession* s, cudaStream_t st, int kind, double bytes, F&& launch) {
+  s->launches++;
+  if (!s->prof) {
+    launch();
+    return;
+  }
+  const size_t e0 = ProfEvent(s, st);
+  launch();
+  const size_t e1 = ProfEvent(s, st);
+  s->prof_recs.push_back({kind, e0, e1, bytes});
+}
+
+// Algorithmic bytes of one projection: bf16 weights once, fp32 activations in, fp32 results out.
+double LinearBytes(int M, int K, int Kp, int N) { return 2.0 * N * Kp + 4.0 * M * K + 4.0 * M * N; }
+
+// Enqueue one batched cached step (AdvanceOneToken + HeadLogitsRow for M rows) on `st`.
+void EnqueueStep(ShahdSession* s, const StepPlan& p, cudaStream_t st) {
+  const int M = p.M;
+  const int norm = s->cfg.norm_kind == 1 ? kNormRms : kNormLayer;
+  Timed(s, st, kProfOther, 8.0 * M * s->E, [&] {
+    EmbedArgs e{p.slot, p.tok, p.prompt, p.poff, s->d_seq_len, s->d_pos, s->wte, s->wpe, s->x, s->E};
+    EmbedKernel<<<M, 128, 0, st>>>(e);
+  });
+  KvView kv{s->kv_pool, s->d_block_table, s->max_blocks, s->Hk, s->d, s->page_elems};
+  const int hd = s->H * s->d;
+  // K and V rows read (bf16) + q read and ctx written (fp32)
+  const double attn_bytes = 4.0 * s->Hk * s->d * (double)p.attended + 8.0 * M * hd;
+  for (int l = 0; l < s->L; l++) {
+    const Layer& Ly = s->layers[l];
+    // norm1 + QKV + RoPE + KV append (CachedForward.ts:66-73, :78-79)
+    LinearArgs la{s->x, s->E, M, s->E, s->Ep, Ly.w_qkv, s->Nqkv, Ly.ln1_g, Ly.ln1_b, (float)s->cfg.layer_norm_eps,
+                  nullptr, nullptr};
+    EpiQKV eq{s->q, kv, l, s->d_pos, p.slot, s->rope_cos, s->rope_sin, s->H, s->Hk, s->d};
+    Timed(s, st, kProfLinear, LinearBytes(M, s->E, s->Ep, s->Nqkv), [&] { LaunchLinear(norm, la, eq, st); });
+    // attention over the cache (CachedForward.ts:76-80)
+    AttnArgs aa{s->q, s->ctx, kv, l, s->d_pos, p.slot, s->H, s->Hk, s->G, s->d, (float)(1.0 / std::sqrt((double)s->d)),
+                s->max_blocks, s->part_o, s->part_m, s->part_l, s->attn_counter};
+    dim3 ag(s->max_blocks, s->Hk, M);
+    Timed(s, st, kProfAttention, attn_bytes, [&] {
+      if (s->d == 64) AttnDecodeKernel<64><<<ag, kAttnThreads, 0, st>>>(aa);
+      else if (s->d == 32) AttnDecodeKernel<32><<<ag, kAttnThreads, 0, st>>>(aa);
+      else if (s->d == 128) AttnDecodeKernel<128><<<ag, kAttnThreads, 0, st>>>(aa);
+      else AttnDecodeGenericKernel<<<ag, kAttnThreads, 0, st>>>(aa);
+    });
+    // summed per-head Wo + residual (CachedForward.ts:81-84)
+    LinearArgs lo{s->ctx, hd, M, hd, s->HDp, Ly.w_o, s->E, nullptr, nullptr, 0.f, nullptr, nullptr};
+    Timed(s, st, kProfLinear, LinearBytes(M, hd, s->HDp, s->E),
+          [&] { LaunchLinear(kNormNone, lo, EpiResid{s->x, s->E, nullptr}, st); });
+    // norm2 + MLP + residual (CachedForward.ts:86-87)
+    LinearArgs lu{s->x, s->E, M, s->E, s->Ep, Ly.w_up, s->Nup, Ly.ln2_g, Ly.ln2_b, (float)s->cfg.layer_norm_eps,
+                  nullptr, nullptr};
+    Timed(s, st, kProfLinear, LinearBytes(M, s->E, s->Ep, s->Nup), [&] {
+      if (s->cfg.mlp_kind == 0) LaunchLinear(norm, lu, EpiReluFc{s->act, s->F, Ly.b_fc}, st);
+      else LaunchLinear(norm, lu, EpiGated{s->act, s->F, s->cfg.mlp_kind == 2}, st);
+    });
+    LinearArgs ld{s->act, s->F, M, s->F, s->Fp, Ly.w_down, s->E, nullptr, nullptr, 0.f, nullptr, nullptr};
+    Timed(s, st, kProfLinear, LinearBytes(M, s->F, s->Fp, s->E),
+          [&] { LaunchLinear(kNormNone, ld, EpiResid{s->x, s->E, Ly.b_proj}, st); });
+  }
+  int nblk = 0;
+  if (p.head) {
+    // final norm + LM head + argmax partials (HeadLogitsRow, CachedRowMath.ts:117-137)
+    nblk = HeadBlocks(s, M);
+    LinearArgs lh{s->x, s->E, M, s->E, s->Ep, s->w_head, s->V, s->lnf_g, s->lnf_b, (float)s->cfg.layer_norm_eps,
+                  s->am_val, s->am_idx};
+    Timed(s, st, kProfLinear, LinearBytes(M, s->E, s->Ep, s->V),
+          [&] { LaunchLinear(norm, lh, EpiLogits{p.logits, s->head_bias}, st); });
+  }
+  FinishArgs f{M, p.slot, s->d_pos, s->d_seq_len, p.head ? s->am_val : nullptr, s->am_idx, nblk, p.next_ids,
+               p.cur_tok, p.out_ids, p.out_ld, s->d_gen_count, nullptr};
+  Timed(s, st, kProfOther, 16.0 * M, [&] { FinishKernel<<<CeilDiv(M, 128), 128, 0, st>>>(f); });
+}
+
+int CheckLaunch(const char* what) {
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    SetError("%s: kernel launch failed: %s", what, cudaGetErrorString(e));
+    return SHAHD_ECUDA;
+  }
+  return SHAHD_OK;
+}
+
+// ---- KV page management (host mirror of the block table) ---------------------------------------
+
+void ResetSlot(ShahdSession* s, int slot) {
+  for (int b = 0; b < s->max_blocks; b++) {
+    int& e = s->h_block_table[slot * s->max_blocks + b];
+    if (e >= 0) {
+      s->free_pages.push_back(e);
+      e = -1;
+    }
+  }
+  s->h_len[slot] = 0;
+}
+
+// Pages for positions [0, upto) of `slot`.
+int EnsurePages(ShahdSession* s, int slot, int upto) {
+  const int need = std::min(CeilDiv(upto, kPageTokens), s->max_blocks);
+  for (int b = 0; b < need; b++) {
+    int& e = s->h_block_table[slot * s->max_blocks + b];
+    if (e < 0) {
+      if (s->free_pages.empty()) {
+        SetError("KV pool exhausted: no free page for slot %d position %d (kv_pages=%d)", slot, b * kPageTokens,
+                 s->kv_pages);
+        return SHAHD_ENOMEM;
+      }
+      e = s->free_pages.back();
+      s->free_pages.pop_back();
+    }
+  }
+  return SHAHD_OK;
+}
+
+int UploadTables(ShahdSession* s) {
+  SHAHD_CUDA_TRY(cudaMemcpyAsync(s->d_block_table, s->h_block_table, sizeof(int) * (size_t)s->max_seqs * s->max_blocks,
+                                 cudaMemcpyHostToDevice, s->stream));
+  // Synchronous on purpose: the pinned mirror may change right after this call returns.
+  SHAHD_CUDA_TRY(cudaStreamSynchronize(s->stream));
+  return SHAHD_OK;
+}
+
+int UploadLengths(ShahdSession* s) {
+  std::vector<int> tmp(s->h_len);
+  SHAHD_CUDA_TRY(cudaMemcpy(s->d_seq_len, tmp.data(), sizeof(int) * tmp.size(), cudaMemcpyHostToDevice));
+  return SHAHD_OK;
+}
+
+__global__ void GatherLastTokens(const int* prompt, const int* ends, int n, int* cur) {
+  int r = blockIdx.x * blockDim.x + threadIdx.x;
+  if (r < n) cur[r] = prompt[ends[r] - 1];
+}
+
+// Window rebuild input: the last (C-1) tokens of prompt_r ++ out_r[0..gen) (CachedForward.ts:133-141).
+__global__ void GatherWindow(const int* prompt, const int* pstart, const int* plen, const int* out, int out_ld,
+                             const int* rows, int nrows, int gen, int keep, int* window) {
+  int i = blockIdx.x;
+  if (i >= nrows) return;
+  int r = rows[i];
+  int total = plen[r] + gen;
+  int start = total - keep;
+  for (int k = threadIdx.x; k < keep; k += blockDim.x) {
+    int idx = start + k;
+    window[(size_t)i * keep + k] = idx < plen[r] ? prompt[pstart[r] + idx] : out[(size_t)r * out_ld + (idx - plen[r])];
+  }
+}
+
+__global__ void SetLengths(int* seq_len, const int* slots, int n, int value) {
+  int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) seq_len[slots[i]] = value;
+}
+
+// Prefill rows (already reset, lengths 0) by cached steps over their contexts: row i of the plan takes
+// ids[poff_i + t] at step t while t < len_i. Rows must be ordered by descending length.
+int PrefillBySteps(ShahdSession* s, const int* d_slots, const int* d_poff, const int* d_prompt,
+                   const std::vector<int>& lens_desc, const std::vector<int>& slots_desc) {
+  if (lens_desc.empty() || lens_desc[0] == 0) return SHAHD_OK;
+  for (size_t i = 0; i < slots_desc.size(); i++) SHAHD_TRY(EnsurePages(s, slots_desc[i], lens_desc[i]));
+  SHAHD_TRY(UploadTables(s));
+  for (int t = 0; t < lens_desc[0]; t++) {
+    int M = 0;
+    while (M < (int)lens_desc.size() && lens_desc[M] > t) M++;
+    StepPlan p{M, d_slots, nullptr, d_poff, d_prompt, false, nullptr, nullptr, nullptr, nullptr, 0, (long long)M * (t + 1)};
+    EnqueueStep(s, p, s->stream);
+  }
+  for (size_t i = 0; i < slots_desc.size(); i++) s->h_len[slots_desc[i]] = lens_desc[i];
+  return CheckLaunch("prefill");
+}
+
+int ValidateSlots(ShahdSession* s, const int32_t* slots, int n, const char* op) {
+  std::vector<char> seen(s->max_seqs, 0);
+  for (int i = 0; i < n; i++) {
+    if (slots[i] < 0 || slots[i] >= s->max_seqs) {
+      SetError("%s: slot %d out of range [0,%d)", op, slots[i], s->max_seqs);
+      return SHAHD_EINVAL;
+    }
+    if (seen[slots[i]]) {
+      SetError("%s: slot %d listed twice", op, slots[i]);
+      return SHAHD_EINVAL;
+    }
+    seen[slots[i]] = 1;
+  }
+  return SHAHD_OK;
+}
+
+int ValidateIds(ShahdSession* s, const int32_t* ids, size_t n, const char* op) {
+  for (size_t i = 0; i < n; i++)
+    if (ids[i] < 0 || ids[i] >= s->V) {
+      SetError("%s: token id %d out of range [0,%d) — likely a tokenizer/vocab mismatch", op, ids[i], s->V);
+      return SHAHD_EINVAL;
+    }
+  return SHAHD_OK;
+}
+
+int GrowPrompt(ShahdSession* s, size_t count) {
+  if (count <= s->prompt_cap) return SHAHD_OK;
+  size_t cap = std::max(count, s->prompt_cap * 2);
+  int* p = nullptr;
+  SHAHD_TRY(DevAlloc(s, &p, cap));
+  s->d_prompt = p;
+  s->prompt_cap = cap;
+  return SHAHD_OK;
+}
+
+int GrowOut(ShahdSession* s, size_t count) {
+  if (count <= s->out_cap) return SHAHD_OK;
+  size_t cap = std::max(count, s->out_cap * 2);
+  int* p = nullptr;
+  SHAHD_TRY(DevAlloc(s, &p, cap));
+  s->d_out = p;
+  s->out_cap = cap;
+  return SHAHD_OK;
+}
+
+// Core of shahd_generate / shahd_generate_device. d_prompt_packed holds the packed prompts on the
+// device; offs their host offsets. Output ids land in d_out [n, max_new].
+int GenerateCore(ShahdSession* s, const int* d_prompt_packed, const std::vector<int>& offs, int n, int max_new,
+                 const ShahdSampling* o, int* d_out, cudaStream_t st) {
+  if (o && o->temperature > 0) {
+    SetError("shahd_generate: stochastic sampling (temperature > 0) is not supported by this build");
+    return SHAHD_EINVAL;
+  }
+  const int C = s->C;
+  // CachedDecoder constructor: Context = prompt.slice(-BlockSize); prefill all but its last id.
+  std::vector<int> plen(n), pstart(n), full_len(n);
+  for (int i = 0; i < n; i++) {
+    full_len[i] = offs[i + 1] - offs[i];
+    int ctx = std::min(full_len[i], C);
+    pstart[i] = offs[i + 1] - ctx;
+    plen[i] = ctx - 1;
+  }
+  SHAHD_CUDA_TRY(cudaStreamSynchronize(s->stream));
+  for (int i = 0; i < n; i++) ResetSlot(s, i);
+  // Pages for the whole run up front: positions reach min(plen + max_new, C).
+  for (int i = 0; i < n; i++) SHAHD_TRY(EnsurePages(s, i, std::min(plen[i] + max_new, C)));
+  SHAHD_TRY(UploadTables(s));
+  SHAHD_TRY(UploadLengths(s));
+
+  // prefill-by-steps in descending-length order
+  std::vector<int> order(n);
+  std::iota(order.begin(), order.end(), 0);
+  std::stable_sort(order.begin(), order.end(), [&](int a, int b) { return plen[a] > plen[b]; });
+  int* h = s->h_pinned_rows;
+  std::vector<int> lens_desc(n), slots_desc(n);
+  for (int i = 0; i < n; i++) {
+    h[i] = order[i];                 // slot
+    h[s->max_seqs + i] = pstart[order[i]];  // gather offset
+    lens_desc[i] = plen[order[i]];
+    slots_desc[i] = order[i];
+  }
+  SHAHD_CUDA_TRY(cudaMemcpyAsync(s->d_pf_slot, h, sizeof(int) * n, cudaMemcpyHostToDevice, st));
+  SHAHD_CUDA_TRY(cudaMemcpyAsync(s->d_pf_poff, h + s->max_seqs, sizeof(int) * n, cudaMemcpyHostToDevice, st));
+  // decode-order rows: slot r = row r
+  for (int i = 0; i < n; i++) {
+    h[2 * s->max_seqs + i] = i;
+    h[3 * s->max_seqs + i] = offs[i + 1];
+    h[4 * s->max_seqs + i] = offs[i];
+    h[5 * s->max_seqs + i] = full_len[i];
+  }
+  SHAHD_CUDA_TRY(cudaMemcpyAsync(s->d_slot, h + 2 * s->max_seqs, sizeof(int) * n, cudaMemcpyHostToDevice, st));
+  SHAHD_CUDA_TRY(cudaMemcpyAsync(s->d_poff, h + 3 * s->max_seqs, sizeof(int) * n, cudaMemcpyHostToDevice, st));
+  SHAHD_CUDA_TRY(cudaMemsetAsync(s->d_gen_count, 0, sizeof(int) * n, st));
+  SHAHD_CUDA_TRY(cudaStreamSynchronize(st));  // pinned staging reused below
+  if (st != s->stream) {
+    // all work of this call is ordered on the caller's stream
+  }
+  cudaStream_t saved = s->stream;
+  s->stream = st;
+  int rc = PrefillBySteps(s, s->d_pf_slot, s->d_pf_poff, d_prompt_packed, lens_desc, slots_desc);
+  if (rc == SHAHD_OK) {
+    GatherLastTokens<<<CeilDiv(n, 128), 128, 0, st>>>(d_prompt_packed, s->d_poff, n, s->d_tok);
+    s->launches++;
+    // the decode loop: step k consumes the last context id (k = 0) or the id sampled at k-1
+    StepPlan p{n, s->d_slot, s->d_tok, nullptr, nullptr, true, nullptr, nullptr, s->d_tok, d_out, max_new, 0};
+    for (int k = 0; k < max_new && rc == SHAHD_OK; k++) {
+      // rows whose window is full rebuild it from their last C-1 ids first (CachedForward.ts:135-141)
+      std::vector<int> slide;
+      for (int i = 0; i < n; i++)
+        if (s->h_len[i] >= C) slide.push_back(i);
+      if (!slide.empty()) {
+        const int keep = C - 1;
+        const int ns = (int)slide.size();
+        for (int i = 0; i < ns; i++) h[6 * s->max_seqs + i] = slide[i];
+        int* d_rows = s->d_next;  // scratch [ns]
+        cudaMemcpyAsync(d_rows, h + 6 * s->max_seqs, sizeof(int) * ns, cudaMemcpyHostToDevice, st);
+        cudaMemcpyAsync(s->d_pf_slot, h + 5 * s->max_seqs, sizeof(int) * n, cudaMemcpyHostToDevice, st);  // full lengths
+        // GatherWindow needs per-row prompt start/length and the output so far: rows are slots here
+        cudaMemcpyAsync(s->d_pf_poff, h + 4 * s->max_seqs, sizeof(int) * n, cudaMemcpyHostToDevice, st);  // prompt starts
+        GatherWindow<<<ns, 128, 0, st>>>(d_prompt_packed, s->d_pf_poff, s->d_pf_slot, d_out, max_new, d_rows, ns, k - 1,
+                                         keep, s->d_window);
+        SetLengths<<<CeilDiv(ns, 128), 128, 0, st>>>(s->d_seq_len, d_rows, ns, 0);
+        s->launches += 2;
+        for (int i = 0; i < ns; i++) {
+          h[7 * s->max_seqs + i] = i * keep;  // gather offsets into the window buffer
+          s->h_len[slide[i]] = 0;
+        }
+        cudaMemcpyAsync(s->d_pf_poff, h + 7 * s->max_seqs, sizeof(int) * ns, cudaMemcpyHostToDevice, st);
+        cudaMemcpyAsync(s->d_pf_slot, h + 6 * s->max_seqs, sizeof(int) * ns, cudaMemcpyHostToDevice, st);
+        std::vector<int> lens(ns, keep);
+        rc = PrefillBySteps(s, s->d_pf_slot, s->d_pf_poff, s->d_window, lens, slide);
+        cudaStreamSynchronize(st);  // pinned staging reused next step
+        if (rc != SHAHD_OK) break;
+      }
+      p.attended = 0;
+      for (int i = 0; i < n; i++) p.attended += s->h_len[i] + 1;
+      EnqueueStep(s, p, st);
+      for (int i = 0; i < n; i++) s->h_len[i] += 1;
+      rc = CheckLaunch("generate step");
+    }
+  }
+  s->stream = saved;
+  return rc;
+}
+
+}  // namespace
+}  // namespace shahd
+
+using namespace shahd;
+
+// ================================================================================================
+// C ABI
+// ================================================================================================
+
+extern "C" int64_t shahd_param_count(const ShahdModelCfg* cfg) {
+  ClearError();
+  ParamLayout lay;
+  if (!cfg || BuildParamLayout(*cfg, &lay) != SHAHD_OK) return -1;
+  return lay.total;
+}
+
+extern "C" int shahd_session_create(const ShahdModelCfg* cfg, const void* params, int32_t params_f64,
+                                    int64_t params_count, const ShahdSessionOpts* opts, ShahdSession** out) {
+  ClearError();
+  if (!cfg || !params || !opts || !out) {
+    SetError("shahd_session_create: null argument");
+    return SHAHD_EINVAL;
+  }
+  *out = nullptr;
+  ParamLayout lay;
+  if (BuildParamLayout(*cfg, &lay) != SHAHD_OK) return SHAHD_EINVAL;
+  if (params_count != lay.total) {
+    SetError("shahd_session_create: params hold %lld values but the model needs %lld", (long long)params_count,
+             (long long)lay.total);
+    return SHAHD_EINVAL;
+  }
+  if (opts->max_seqs < 1) {
+    SetError("shahd_session_create: max_seqs must be >= 1, got %d", opts->max_seqs);
+    return SHAHD_EINVAL;
+  }
+  const int d = cfg->embed_dim / cfg->num_heads;
+  if (d % 2 != 0 || d > kMaxHeadDimGeneric) {
+    SetError("shahd_session_create: head dim %d must be even and <= %d", d, kMaxHeadDimGeneric);
+    return SHAHD_EINVAL;
+  }
+  if (cfg->num_heads / cfg->kv_heads > kMaxGroup) {
+    SetError("shahd_session_create: query group %d exceeds %d", cfg->num_heads / cfg->kv_heads, kMaxGroup);
+    return SHAHD_EINVAL;
+  }
+  int ndev = 0;
+  if (cudaGetDeviceCount(&ndev) != cudaSuccess || opts->device < 0 || opts->device >= ndev) {
+    SetError("shahd_session_create: CUDA device %d not available", opts->device);
+    return SHAHD_ENODEV;
+  }
+  cudaDeviceProp prop;
+  SHAHD_CUDA_TRY(cudaGetDeviceProperties(&prop, opts->device));
+  if (prop.major != 10) {
+    SetError("shahd_session_create: device %d is sm_%d%d, this build runs on sm_100", opts->device, prop.major, prop.minor);
+    return SHAHD_ENODEV;
+  }
+  SHAHD_CUDA_TRY(cudaSetDevice(opts->device));
+
+  ShahdSession* s = new ShahdSession();
+  s->cfg = *cfg;
+  s->E = cfg->embed_dim; s->L = cfg->num_layers; s->H = cfg->num_heads; s->Hk = cfg->kv_heads; s->d = d;
+  s->F = cfg->mlp_hidden; s->C = cfg->block_size; s->V = cfg->vocab_size; s->G = s->H / s->Hk;
+  s->Ep = RoundUp(s->E, 8); s->Fp = RoundUp(s->F, 8); s->HDp = RoundUp(s->H * d, 8);
+  s->Nqkv = (s->H + 2 * s->Hk) * d;
+  s->Nup = cfg->mlp_kind == 0 ? s->F : 2 * s->F;
+  s->device = opts->device;
+  s->max_seqs = opts->max_seqs;
+  s->max_blocks = CeilDiv(s->C, kPageTokens);
+  s->kv_pages = opts->kv_pages > 0 ? opts->kv_pages : s->max_seqs * s->max_blocks;
+  s->page_elems = (size_t)s->L * s->Hk * 2 * kPageTokens * d;
+  auto fail = [&](int rc) {
+    shahd_session_destroy(s);
+    return rc;
+  };
+  if (cudaStreamCreateWithFlags(&s->stream, cudaStreamNonBlocking) != cudaSuccess) {
+    SetError("cudaStreamCreate failed");
+    delete s;
+    return SHAHD_ECUDA;
+  }
+
+  // ---- weights: repack on the host, one copy each ----
+  HostWeights hw;
+  if (RepackWeights(*cfg, lay, params, params_f64 != 0, &hw) != SHAHD_OK) return fail(SHAHD_EINVAL);
+  auto up_bf = [&](const std::vector<bf16>& v, bf16** dst) -> int {
+    SHAHD_TRY(DevAlloc(s, dst, v.size()));
+    SHAHD_CUDA_TRY(cudaMemcpy(*dst, v.data(), v.size() * sizeof(bf16), cudaMemcpyHostToDevice));
+    return SHAHD_OK;
+  };
+  auto up_f = [&](const std::vector<float>& v, float** dst) -> int {
+    if (v.empty()) {
+      *dst = nullptr;
+      return SHAHD_OK;
+    }
+    SHAHD_TRY(DevAlloc(s, dst, v.size()));
+    SHAHD_CUDA_TRY(cudaMemcpy(*dst, v.data(), v.size() * sizeof(float), cudaMemcpyHostToDevice));
+    return SHAHD_OK;
+  };
+  int rc = SHAHD_OK;
+  s->layers.resize(s->L);
+  for (int l = 0; l < s->L && rc == SHAHD_OK; l++) {
+    Layer& Ly = s->layers[l];
+    const HostLayer& hl = hw.layers[l];
+    rc = up_bf(hl.w_qkv, &Ly.w_qkv);
+    if (rc == SHAHD_OK) rc = up_bf(hl.w_o, &Ly.w_o);
+    if (rc == SHAHD_OK) rc = up_bf(hl.w_up, &Ly.w_up);
+    if (rc == SHAHD_OK) rc = up_bf(hl.w_down, &Ly.w_down);
+    if (rc == SHAHD_OK) rc = up_f(hl.ln1_g, &Ly.ln1_g);
+    if (rc == SHAHD_OK) rc = up_f(hl.ln1_b, &Ly.ln1_b);
+    if (rc == SHAHD_OK) rc = up_f(hl.ln2_g, &Ly.ln2_g);
+    if (rc == SHAHD_OK) rc = up_f(hl.ln2_b, &Ly.ln2_b);
+    if (rc == SHAHD_OK) rc = up_f(hl.b_fc, &Ly.b_fc);
+    if (rc == SHAHD_OK) rc = up_f(hl.b_proj, &Ly.b_proj);
+  }
+  if (rc == SHAHD_OK) rc = up_bf(hw.w_head, &s->w_head);
+  if (rc == SHAHD_OK) rc = up_f(hw.head_bias, &s->head_bias);
+  if (rc == SHAHD_OK) rc = up_f(hw.lnf_g, &s->lnf_g);
+  if (rc == SHAHD_OK) rc = up_f(hw.lnf_b, &s->lnf_b);
+  if (rc == SHAHD_OK) rc = up_f(hw.wte, &s->wte);
+  if (rc == SHAHD_OK) rc = up_f(hw.wpe, &s->wpe);
+  if (rc == SHAHD_OK) rc = up_f(hw.rope_cos, &s->rope_cos);
+  if (rc == SHAHD_OK) rc = up_f(hw.rope_sin, &s->rope_sin);
+  if (rc != SHAHD_OK) return fail(rc);
+
+  // ---- KV pool + tables ----
+  const int R = s->max_seqs;
+  if ((rc = DevAlloc(s, &s->kv_pool, s->page_elems * (size_t)s->kv_pages)) != SHAHD_OK) return fail(rc);
+  if ((rc = DevAlloc(s, &s->d_block_table, (size_t)R * s->max_blocks)) != SHAHD_OK) return fail(rc);
+  if ((rc = DevAlloc(s, &s->d_seq_len, (size_t)R)) != SHAHD_OK) return fail(rc);
+  if (cudaMallocHost(&s->h_block_table, sizeof(int) * (size_t)R * s->max_blocks) != cudaSuccess ||
+      cudaMallocHost(&s->h_pinned_rows, sizeof(int) * (size_t)R * 8) != cudaSuccess) {
+    SetError("cudaMallocHost failed");
+    return fail(SHAHD_ENOMEM);
+  }
+  std::fill(s->h_block_table, s->h_block_table + (size_t)R * s->max_blocks, -1);
+  s->free_pages.resize(s->kv_pages);
+  for (int i = 0; i < s->kv_pages; i++) s->free_pages[i] = s->kv_pages - 1 - i;
+  s->h_len.assign(R, 0);
+  cudaMemset(s->d_seq_len, 0, sizeof(int) * R);
+
+  // ---- per-row scratch ----
+  s->am_stride = std::max(CeilDiv(s->V, kSimtCols), UmmaGridN(s->V));
+  const size_t hd = (size_t)s->H * d;
+  if ((rc = DevAlloc(s, &s->x, (size_t)R * s->E)) != SHAHD_OK ||
+      (rc = DevAlloc(s, &s->q, (size_t)R * hd)) != SHAHD_OK ||
+      (rc = DevAlloc(s, &s->ctx, (size_t)R * hd)) != SHAHD_OK ||
+      (rc = DevAlloc(s, &s->act, (size_t)R * s->F)) != SHAHD_OK ||
+      (rc = DevAlloc(s, &s->logits, (size_t)R * s->V)) != SHAHD_OK ||
+      (rc = DevAlloc(s, &s->am_val, (size_t)R * s->am_stride)) != SHAHD_OK ||
+      (rc = DevAlloc(s, &s->am_idx, (size_t)R * s->am_stride)) != SHAHD_OK ||
+      (rc = DevAlloc(s, &s->part_o, (size_t)R * s->H * s->max_blocks * d)) != SHAHD_OK ||
+      (rc = DevAlloc(s, &s->part_m, (size_t)R * s->H * s->max_blocks)) != SHAHD_OK ||
+      (rc = DevAlloc(s, &s->part_l, (size_t)R * s->H * s->max_blocks)) != SHAHD_OK ||
+      (rc = DevAlloc(s, &s->attn_counter, (size_t)R * s->Hk)) != SHAHD_OK ||
+      (rc = DevAlloc(s, &s->d_slot, (size_t)R)) != SHAHD_OK || (rc = DevAlloc(s, &s->d_tok, (size_t)R)) != SHAHD_OK ||
+      (rc = DevAlloc(s, &s->d_pos, (size_t)R)) != SHAHD_OK || (rc = DevAlloc(s, &s->d_next, (size_t)R)) != SHAHD_OK ||
+      (rc = DevAlloc(s, &s->d_gen_count, (size_t)R)) != SHAHD_OK ||
+      (rc = DevAlloc(s, &s->d_poff, (size_t)R)) != SHAHD_OK ||
+      (rc = DevAlloc(s, &s->d_pf_slot, (size_t)R)) != SHAHD_OK ||
+      (rc = DevAlloc(s, &s->d_pf_poff, (size_t)R)) != SHAHD_OK ||
+      (rc = DevAlloc(s, &s->d_window, (size_t)R * s->C)) != SHAHD_OK)
+    return fail(rc);
+  cudaMemset(s->attn_counter, 0, sizeof(int) * (size_t)R * s->Hk);
+  s->d_prompt = nullptr;
+  s->prompt_cap = 0;
+  s->d_out = nullptr;
+  s->out_cap = 0;
+  if (cudaDeviceSynchronize() != cudaSuccess) {
+    SetError("shahd_session_create: device error during setup");
+    return fail(SHAHD_ECUDA);
+  }
+  *out = s;
+  return SHAHD_OK;
+}
+
+extern "C" int shahd_session_destroy(ShahdSession* s) {
+  if (!s) return SHAHD_OK;
+  cudaSetDevice(s->device);
+  if (s->stream) cudaStreamSynchronize(s->stream);
+  for (auto& kv : s->graphs) cudaGraphExecDestroy(kv.second);
+  for (cudaEvent_t e : s->ev_pool) cudaEventDestroy(e);
+  for (void* p : s->allocs) cudaFree(p);
+  if (s->h_block_table) cudaFreeHost(s->h_block_table);
+  if (s->h_pinned_rows) cudaFreeHost(s->h_pinned_rows);
+  if (s->stream) cudaStreamDestroy(s->stream);
+  delete s;
+  return SHAHD_OK;
+}
+
+extern "C" int shahd_reset(ShahdSession* s, const int32_t* slots, int32_t n) {
+  ClearError();
+  if (!s || (n > 0 && !slots) || n < 0) {
+    SetError("shahd_reset: bad arguments");
+    return SHAHD_EINVAL;
+  }
+  std::lock_guard<std::mutex> g(s->mu);
+  cudaSetDevice(s->device);
+  SHAHD_TRY(ValidateSlots(s, slots, n, "shahd_reset"));
+  SHAHD_CUDA_TRY(cudaStreamSynchronize(s->stream));
+  for (int i = 0; i < n; i++) ResetSlot(s, slots[i]);
+  SHAHD_TRY(UploadTables(s));
+  return UploadLengths(s);
+}
+
+extern "C" int32_t shahd_seq_length(ShahdSession* s, int32_t slot) {
+  ClearError();
+  if (!s || slot < 0 || slot >= s->max_seqs) {
+    SetError("shahd_seq_length: bad slot");
+    return SHAHD_EINVAL;
+  }
+  std::lock_guard<std::mutex> g(s->mu);
+  return s->h_len[slot];
+}
+
+extern "C" int shahd_prefill(ShahdSession* s, const int32_t* slots, const int32_t* ids, const int32_t* offsets, int32_t n) {
+  ClearError();
+  if (!s || n < 0 || (n > 0 && (!slots || !offsets))) {
+    SetError("shahd_prefill: bad arguments");
+    return SHAHD_EINVAL;
+  }
+  std::lock_guard<std::mutex> g(s->mu);
+  cudaSetDevice(s->device);
+  SHAHD_TRY(ValidateSlots(s, slots, n, "shahd_prefill"));
+  if (n > s->max_seqs) {
+    SetError("shahd_prefill: %d slots exceed max_seqs %d", n, s->max_seqs);
+    return SHAHD_EINVAL;
+  }
+  size_t total = 0;
+  for (int i = 0; i < n; i++) {
+    int len = offsets[i + 1] - offsets[i];
+    if (offsets[i] < 0 || len < 0) {
+      SetError("shahd_prefill: offsets must be non-decreasing from 0");
+      return SHAHD_EINVAL;
+    }
+    if (len > s->C) {
+      SetError("PrefillCache: %d tokens exceed the cache capacity %d", len, s->C);
+      return SHAHD_EINVAL;
+    }
+    total = offsets[i + 1];
+  }
+  if (total > 0 && !ids) {
+    SetError("shahd_prefill: ids is null");
+    return SHAHD_EINVAL;
+  }
+  SHAHD_TRY(ValidateIds(s, ids, total, "PrefillCache"));
+  SHAHD_CUDA_TRY(cudaStreamSynchronize(s->stream));
+  for (int i = 0; i < n; i++) ResetSlot(s, slots[i]);
+  SHAHD_TRY(UploadLengths(s));
+  if (total == 0) return UploadTables(s);
+  SHAHD_TRY(GrowPrompt(s, total));
+  SHAHD_CUDA_TRY(cudaMemcpy(s->d_prompt, ids, sizeof(int) * total, cudaMemcpyHostToDevice));
+  std::vector<int> order(n);
+  std::iota(order.begin(), order.end(), 0);
+  std::stable_sort(order.begin(), order.end(),
+                   [&](int a, int b) { return offsets[a + 1] - offsets[a] > offsets[b + 1] - offsets[b]; });
+  std::vector<int> lens(n), sl(n), po(n);
+  for (int i = 0; i < n; i++) {
+    lens[i] = offsets[order[i] + 1] - offsets[order[i]];
+    sl[i] = slots[order[i]];
+    po[i] = offsets[order[i]];
+  }
+  SHAHD_CUDA_TRY(cudaMemcpy(s->d_pf_slot, sl.data(), sizeof(int) * n, cudaMemcpyHostToDevice));
+  SHAHD_CUDA_TRY(cudaMemcpy(s->d_pf_poff, po.data(), sizeof(int) * n, cudaMemcpyHostToDevice));
+  SHAHD_TRY(PrefillBySteps(s, s->d_pf_slot, s->d_pf_poff, s->d_prompt, lens, sl));
+  SHAHD_CUDA_TRY(cudaStreamSynchronize(s->stream));
+  return SHAHD_OK;
+}
+
+extern "C" int shahd_step(ShahdSession* s, const int32_t* slots, const int32_t* tokens, int32_t n, float* logits,
+                          int32_t* next_ids) {
+  ClearError();
+  if (!s || n < 1 || !slots || !tokens) {
+    SetError("shahd_step: bad arguments");
+    return SHAHD_EINVAL;
+  }
+  std::lock_guard<std::mutex> g(s->mu);
+  cudaSetDevice(s->device);
+  if (n > s->max_seqs) {
+    SetError("shahd_step: %d rows exceed max_seqs %d", n, s->max_seqs);
+    return SHAHD_EINVAL;
+  }
+  SHAHD_TRY(ValidateSlots(s, slots, n, "shahd_step"));
+  SHAHD_TRY(ValidateIds(s, tokens, n, "CachedForwardStep"));
+  for (int i = 0; i < n; i++)
+    if (s->h_len[slots[i]] >= s->C) {
+      SetError("CachedForwardStep: position %d is outside the %d-token window — rebuild the cache", s->h_len[slots[i]],
+               s->C);
+      return SHAHD_EINVAL;
+    }
+  SHAHD_CUDA_TRY(cudaStreamSynchronize(s->stream));
+  for (int i = 0; i < n; i++) SHAHD_TRY(EnsurePages(s, slots[i], s->h_len[slots[i]] + 1));
+  SHAHD_TRY(UploadTables(s));
+  SHAHD_CUDA_TRY(cudaMemcpy(s->d_slot, slots, sizeof(int) * n, cudaMemcpyHostToDevice));
+  SHAHD_CUDA_TRY(cudaMemcpy(s->d_tok, tokens, sizeof(int) * n, cudaMemcpyHostToDevice));
+  StepPlan p{n, s->d_slot, s->d_tok, nullptr, nullptr, true, logits ? s->logits : nullptr, s->d_next, nullptr, nullptr, 0, 0};
+  for (int i = 0; i < n; i++) p.attended += s->h_len[slots[i]] + 1;
+  EnqueueStep(s, p, s->stream);
+  SHAHD_TRY(CheckLaunch("shahd_step"));
+  for (int i = 0; i < n; i++) s->h_len[slots[i]] += 1;
+  if (logits) SHAHD_CUDA_TRY(cudaMemcpyAsync(logits, s->logits, sizeof(float) * (size_t)n * s->V, cudaMemcpyDeviceToHost, s->stream));
+  if (next_ids) SHAHD_CUDA_TRY(cudaMemcpyAsync(next_ids, s->d_next, sizeof(int) * n, cudaMemcpyDeviceToHost, s->stream));
+  SHAHD_CUDA_TRY(cudaStreamSynchronize(s->stream));
+  return SHAHD_OK;
+}
+
+static int ValidateGenerate(ShahdSession* s, const int32_t* offsets, int32_t n, int32_t max_new) {
+  if (n < 1 || n > s->max_seqs) {
+    SetError("shahd_generate: %d sequences, session holds %d", n, s->max_seqs);
+    return SHAHD_EINVAL;
+  }
+  if (max_new < 0) {
+    SetError("shahd_generate: max_new must be >= 0");
+    return SHAHD_EINVAL;
+  }
+  if (offsets[0] != 0) {
+    SetError("shahd_generate: offsets[0] must be 0");
+    return SHAHD_EINVAL;
+  }
+  for (int i = 0; i < n; i++)
+    if (offsets[i + 1] - offsets[i] < 1) {
+      SetError("CachedGenerate: empty prompt — nothing to condition on (sequence %d)", i);
+      return SHAHD_EINVAL;
+    }
+  return SHAHD_OK;
+}
+
+extern "C" int shahd_generate(ShahdSession* s, const int32_t* prompts, const int32_t* offsets, int32_t n, int32_t max_new,
+                              const ShahdSampling* opts, uint32_t* rng_states, int32_t* out_ids) {
+  ClearError();
+  if (!s || !prompts || !offsets || (max_new > 0 && !out_ids)) {
+    SetError("shahd_generate: null argument");
+    return SHAHD_EINVAL;
+  }
+  std::lock_guard<std::mutex> g(s->mu);
+  cudaSetDevice(s->device);
+  SHAHD_TRY(ValidateGenerate(s, offsets, n, max_new));
+  const size_t total = offsets[n];
+  SHAHD_TRY(ValidateIds(s, prompts, total, "CachedGenerate"));
+  if (max_new == 0) return SHAHD_OK;  // CachedGenerate returns the prompt untouched, no prefill
+  std::vector<int> offs(offsets, offsets + n + 1);
+  SHAHD_TRY(GrowPrompt(s, total));
+  SHAHD_TRY(GrowOut(s, (size_t)n * max_new));
+  SHAHD_CUDA_TRY(cudaMemcpy(s->d_prompt, prompts, sizeof(int) * total, cudaMemcpyHostToDevice));
+  int rc = GenerateCore(s, s->d_prompt, offs, n, max_new, opts, s->d_out, s->stream);
+  if (rc != SHAHD_OK) return rc;
+  SHAHD_CUDA_TRY(cudaMemcpyAsync(out_ids, s->d_out, sizeof(int) * (size_t)n * max_new, cudaMemcpyDeviceToHost, s->stream));
+  SHAHD_CUDA_TRY(cudaStreamSynchronize(s->stream));
+  (void)rng_states;
+  return SHAHD_OK;
+}
+
+extern "C" int shahd_generate_device(ShahdSession* s, const int32_t* d_prompts, const int32_t* host_offsets, int32_t n,
+                                     int32_t max_new, const ShahdSampling* opts, uint32_t* d_rng_states, int32_t* d_out_ids,
+                                     void* stream) {
+  ClearError();
+  if (!s || !d_prompts || !host_offsets || (max_new > 0 && !d_out_ids)) {
+    SetError("shahd_generate_device: null argument");
+    return SHAHD_EINVAL;
+  }
+  std::lock_guard<std::mutex> g(s->mu);
+  cudaSetDevice(s->device);
+  SHAHD_TRY(ValidateGenerate(s, host_offsets, n, max_new));
+  if (max_new == 0) return SHAHD_OK;
+  std::vector<int> offs(host_offsets, host_offsets + n + 1);
+  cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : s->stream;
+  (void)d_rng_states;
+  return GenerateCore(s, d_prompts, offs, n, max_new, opts, d_out_ids, st);
+}
+
+extern "C" int shahd_sync(ShahdSession* s) {
+  ClearError();
+  if (!s) return SHAHD_EINVAL;
+  cudaSetDevice(s->device);
+  SHAHD_CUDA_TRY(cudaStreamSynchronize(s->stream));
+  SHAHD_CUDA_TRY(cudaDeviceSynchronize());
+  return SHAHD_OK;
+}
+
+extern "C" int32_t shahd_step_launches(ShahdSession* s, int32_t n) {
+  if (!s) return -1;
+  // embed + per layer (QKV, attention, O, up, down) + head + finish
+  (void)n;
+  return 1 + 5 * s->L + 2;
+}
+
+extern "C" int shahd_profile(ShahdSession* s, int32_t enable) {
+  ClearError();
+  if (!s) return SHAHD_EINVAL;
+  std::lock_guard<std::mutex> g(s->mu);
+  cudaSetDevice(s->device);
+  SHAHD_CUDA_TRY(cudaDeviceSynchronize());
+  s->prof = enable != 0;
+  s->prof_recs.clear();
+  s->ev_used = 0;
+  return SHAHD_OK;
+}
+
+extern "C" int shahd_profile_read(ShahdSession* s, int32_t kind, double* total_ms, int64_t* launches, double* bytes) {
+  ClearError();
+  if (!s || kind < 0 || kind >= kProfKinds || !total_ms || !launches || !bytes) {
+    SetError("shahd_profile_read: bad arguments");
+    return SHAHD_EINVAL;
+  }
+  std::lock_guard<std::mutex> g(s->mu);
+  cudaSetDevice(s->device);
+  SHAHD_CUDA_TRY(cudaDeviceSynchronize());
+  double ms = 0, b = 0;
+  int64_t n = 0;
+  for (const auto& r : s->prof_recs) {
+    if (r.kind != kind) continue;
+    float t = 0;
+    SHAHD_CUDA_TRY(cudaEventElapsedTime(&t, s->ev_pool[r.ev0], s->ev_pool[r.ev1]));
+    ms += t;
+    b += r.bytes;
+    n++;
+  }
+  *total_ms = ms;
+  *launches = n;
+  *bytes = b;
+  return SHAHD_OK;
+}
+
+extern "C" int64_t shahd_kernel_launches(ShahdSession* s) { return s ? (int64_t)s->launches : -1; }
+
+extern "C" const char* shahd_last_error(void) { return GetError(); }
