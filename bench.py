@@ -132,7 +132,7 @@ def run_reference(args, rank: int, world: int) -> None:
     w = pkg.configs.WORKLOADS[args.workload]
     params = pkg.init_params(w.model, w.weight_seed)
     threads = os.cpu_count() or 1
-    seqs, new = threads, 32
+    seqs, new = min(threads, w.seqs), w.new_tokens
     for _ in range(args.warmup):
         cpu_baseline(w, params, threads, seqs, new)
     vals = [cpu_baseline(w, params, threads, seqs, new) for _ in range(args.steps)]
@@ -171,7 +171,8 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
     offs = np.arange(0, (w.seqs + 1) * w.prompt_len, w.prompt_len, dtype=np.int32)
     d_prompts = torch.from_numpy(prompts.reshape(-1).copy()).to(dev)
     d_out = torch.empty(w.seqs * w.new_tokens, dtype=torch.int32, device=dev)
-    stream = torch.cuda.current_stream(dev)
+    stream = torch.cuda.Stream(device=dev)  # a real stream handle: the library joins it with events
+    torch.cuda.set_stream(stream)
     flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=dev)
 
     def step():
@@ -214,6 +215,13 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
     ms_per_step = max_ms / args.steps
     tokens_per_step_all = world * w.seqs * w.new_tokens
     value = tokens_per_step_all / (ms_per_step / 1000.0)
+
+    if args.no_extras:
+        if dist is not None:
+            dist.destroy_process_group()
+        if rank == 0:
+            print(json.dumps({"ms_per_step": ms_per_step, "value": value, "gpu_launches": int(launches)}), flush=True)
+        return
 
     # gather per-rank output checksums (the only collective, outside the timed region)
     chk = torch.tensor([int(d_out.sum().item())], dtype=torch.int64, device=dev)
@@ -273,7 +281,7 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
     cpu = None
     if world == 1:
         threads = os.cpu_count() or 1
-        cpu = cpu_baseline(w, params, threads, min(threads, w.seqs), 24)
+        cpu = cpu_baseline(w, params, threads, min(threads, w.seqs), w.new_tokens)
     line = {
         "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
@@ -301,6 +309,8 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", default="microchat", choices=sorted(pkg.configs.WORKLOADS))
+    ap.add_argument("--no-extras", action="store_true",
+                    help="time the steps only (no e2e, profile or CPU legs): the profiling command line")
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))

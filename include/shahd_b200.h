@@ -61,7 +61,7 @@ void SetScalarKernels(int force);
 int ShahdGpuAvailable(void);
 /* Thread-local message of the last failure on this thread ("" when none). */
 const char* ShahdLastError(void);
-/* Row count from which decode projections use tcgen05 tiles instead of the SIMT kernel (default 32;
+/* Row count from which decode projections use tcgen05 tiles instead of the SIMT kernel (default 17;
  * 1 forces tensor cores everywhere). Process-wide tuning/test hook; no counterpart in the reference. */
 void ShahdSetTensorCoreMinRows(int rows);
 /* First error code a kernel recorded for a bounded device-side wait that gave up (0 = none). */

@@ -3,6 +3,12 @@
 // CachedRowMath.ts:14-137) as: embed -> per layer [norm+QKV+RoPE+KV append] -> [attention over the
 // paged cache] -> [O projection + residual] -> [norm + gate/up + SwiGLU/GeGLU | fc + ReLU] ->
 // [down projection + residual] -> [final norm + LM head + argmax partials] -> finish.
+//
+// Norms are folded into the projection that consumes them: the weights carry gamma (W' = W·diag(gamma),
+// repacked once), and the kernel applies the row statistics: RMSNorm out = is·(x·W'), LayerNorm
+// out = is·(x·W' - mu·c1) + c2 with c1 = sum_k W', c2 = beta·W (NormRow, CachedRowMath.ts:25-56).
+// Activations keep an fp32 master copy (read by the CUDA-core kernels) and a bf16 copy (the tensor-core
+// operand, loaded by TMA).
 #pragma once
 
 #include "common.cuh"
@@ -13,6 +19,9 @@ __device__ int g_shahd_device_error;  // 0 = ok; otherwise the first kDevErr* co
 constexpr int kDevErrUmmaTimeout = 1;
 constexpr int kDevErrGemmTimeout = 2;
 constexpr int kDevErrNoPage = 3;
+constexpr int kDevErrAttnTimeout = 4;
+
+constexpr uint32_t kWaitLimit = 1u << 22;  // mbarrier probes before a wait gives up
 
 constexpr int kPageTokens = 64;  // positions per KV page (and per attention chunk)
 
@@ -47,9 +56,13 @@ struct KvView {
   }
 };
 
-// ---- epilogues: apply(m, n, v0, v1) gets the fp32 dot products of output columns n and n+1 (n even)
-// of row m. Pairs keep RoPE's interleaved (2i, 2i+1) rotation (RotaryEmbedding.ts:42-60) and the
-// gate/up columns of the interleaved W1|W3 layout in one thread.
+__device__ __forceinline__ void StoreBf16x2(bf16* p, float a, float b) {
+  *reinterpret_cast<__nv_bfloat162*>(p) = __floats2bfloat162_rn(a, b);
+}
+
+// ---- epilogues: apply(m, n, v0, v1) gets the final values of output columns n and n+1 (n even) of row
+// m (norm already applied). Pairs keep RoPE's interleaved (2i, 2i+1) rotation (RotaryEmbedding.ts:42-60)
+// and the gate/up columns of the interleaved W1|W3 layout in one thread.
 
 // Q/K/V projection: RoPE on q and k at the row's position, q to fp32 scratch, k/v appended to the cache.
 struct EpiQKV {
@@ -79,15 +92,16 @@ struct EpiQKV {
     const int g = (n - hd - kvsel * Hk * d) / d;
     const long long off = kv.Offset(slot[m], p, layer, g, kvsel);
     if (off < 0) return;
-    *reinterpret_cast<__nv_bfloat162*>(kv.pool + off + j) = __floats2bfloat162_rn(v0, v1);
+    StoreBf16x2(kv.pool + off + j, v0, v1);
   }
 };
 
-// Residual update x += v (+ bias): the attention output projection (summed per-head Wo,
-// CachedForward.ts:75-84) and the MLP down projection (CachedForward.ts:86-87).
+// Residual update x += v (+ bias), bf16 copy refreshed: the attention output projection (summed
+// per-head Wo, CachedForward.ts:75-84) and the MLP down projection (CachedForward.ts:86-87).
 struct EpiResid {
   float* x;  // [M, ldx]
-  int ldx;
+  bf16* xb;  // [M, ldxb]
+  int ldx, ldxb;
   const float* bias;  // nullable
   __device__ __forceinline__ void apply(int m, int n, float v0, float v1, int N) const {
     float* p = x + (size_t)m * ldx + n;
@@ -95,8 +109,14 @@ struct EpiResid {
       v0 += bias[n];
       if (n + 1 < N) v1 += bias[n + 1];
     }
-    p[0] += v0;
-    if (n + 1 < N) p[1] += v1;
+    const float a = p[0] + v0;
+    p[0] = a;
+    float b = 0.f;
+    if (n + 1 < N) {
+      b = p[1] + v1;
+      p[1] = b;
+    }
+    StoreBf16x2(xb + (size_t)m * ldxb + n, a, b);
   }
 };
 
@@ -104,7 +124,8 @@ struct EpiResid {
 // (MlpRow, CachedRowMath.ts:107-112; SiluValue Silu.ts:8-10; GeluValue Gelu.ts:7-14).
 struct EpiGated {
   float* act;  // [M, F]
-  int F;
+  bf16* actb;  // [M, ldb]
+  int F, ldb;
   int gelu;
   __device__ __forceinline__ void apply(int m, int n, float g, float u, int N) const {
     float a;
@@ -114,23 +135,31 @@ struct EpiGated {
     } else {
       a = g * (1.0f / (1.0f + __expf(-g)));
     }
-    act[(size_t)m * F + (n >> 1)] = a * u;
+    const float h = a * u;
+    act[(size_t)m * F + (n >> 1)] = h;
+    actb[(size_t)m * ldb + (n >> 1)] = __float2bfloat16_rn(h);
   }
 };
 
 // Relu MLP hidden: relu(x·Wfc + bfc) (MlpRow, CachedRowMath.ts:95-101).
 struct EpiReluFc {
   float* act;  // [M, F]
-  int F;
+  bf16* actb;
+  int F, ldb;
   const float* bias;
   __device__ __forceinline__ void apply(int m, int n, float v0, float v1, int N) const {
     float* p = act + (size_t)m * F + n;
     v0 += bias[n];
-    p[0] = v0 > 0.f ? v0 : 0.f;
+    v0 = v0 > 0.f ? v0 : 0.f;
+    p[0] = v0;
     if (n + 1 < N) {
       v1 += bias[n + 1];
-      p[1] = v1 > 0.f ? v1 : 0.f;
+      v1 = v1 > 0.f ? v1 : 0.f;
+      p[1] = v1;
+    } else {
+      v1 = 0.f;
     }
+    StoreBf16x2(actb + (size_t)m * ldb + n, v0, v1);
   }
 };
 
@@ -158,24 +187,28 @@ struct IsLogits<EpiLogits> {
   static constexpr bool value = true;
 };
 
-// ---- SIMT linear (GEMV regime, few rows): out[m, n] = sum_k T(a[m, k]) * W[n, k] --------------------
-// T is the row norm of the layer (NormRow, CachedRowMath.ts:25-56) or identity. W is bf16 [N, Kp]
-// (K padded to a multiple of 8 with zeros). 4 warps x 2 columns per CTA; rows in tiles of MT.
+// ---- projection arguments ------------------------------------------------------------------------
 
 struct LinearArgs {
-  const float* a;
+  const float* a;   // fp32 rows [M, lda]  (CUDA-core path)
   int lda;
+  const bf16* ab;   // bf16 rows [a_rows, ldab] (tensor-core path, TMA)
+  int ldab;
+  int a_rows;
   int M;
-  int K;   // logical reduction length
-  int Kp;  // padded row length of W (multiple of 8)
-  const bf16* w;
+  int K;            // logical reduction length
+  int Kp;           // padded row length of W and ab (multiple of 8)
+  const bf16* w;    // [N, Kp], gamma folded in for norm-consuming projections
   int N;
-  const float* gamma;
-  const float* beta;
   float eps;
-  float* am_val;  // argmax partials [M, gridDim.x] (logits only)
+  const float* c1;  // LayerNorm: sum_k W'[n,k]
+  const float* c2;  // LayerNorm: sum_k beta[k] W[n,k]
+  float* am_val;    // argmax partials [M, gridDim.x] (logits only)
   int* am_idx;
 };
+
+// ---- SIMT linear (GEMV regime, few rows): out[m, n] = sum_k xhat[m, k] * W'[n, k] -------------------
+// xhat = x·is (RMS) or (x - mu)·is (LayerNorm, + c2 in the epilogue) or x. 4 warps x 2 columns per CTA.
 
 constexpr int kSimtWarps = 4;
 constexpr int kSimtCols = kSimtWarps * 2;
@@ -186,37 +219,46 @@ __device__ __forceinline__ void StageRowsNormalized(const LinearArgs& la, float*
   for (int r = warp; r < MT; r += kSimtWarps) {
     float* dst = sA + (size_t)r * la.Kp;
     if (m0 + r >= la.M) {
-      for (int k = lane; k < la.Kp; k += 32) dst[k] = 0.f;
+      for (int k = lane * 4; k < la.Kp; k += 128) *reinterpret_cast<float4*>(dst + k) = make_float4(0.f, 0.f, 0.f, 0.f);
       continue;
     }
     const float* src = la.a + (size_t)(m0 + r) * la.lda;
-    float mu = 0.f, is = 1.f;
+    // copy (zero-padded) into shared memory first; the statistics are then taken from there
+    const bool vec = (la.lda & 3) == 0 && (la.K & 3) == 0;
+#pragma unroll 4
+    for (int k = lane * 4; k < la.Kp; k += 128) {
+      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (vec && k < la.K) {
+        v = *reinterpret_cast<const float4*>(src + k);
+      } else if (!vec) {
+        if (k < la.K) v.x = src[k];
+        if (k + 1 < la.K) v.y = src[k + 1];
+        if (k + 2 < la.K) v.z = src[k + 2];
+        if (k + 3 < la.K) v.w = src[k + 3];
+      }
+      *reinterpret_cast<float4*>(dst + k) = v;
+    }
+    if (NORM == kNormNone) continue;
+    __syncwarp();
+    float mu = 0.f, is;
     if (NORM == kNormRms) {
       float ss = 0.f;
-      for (int k = lane; k < la.K; k += 32) ss += src[k] * src[k];
+      for (int k = lane; k < la.K; k += 32) ss += dst[k] * dst[k];
       ss = WarpSum(ss);
       is = 1.0f / sqrtf(ss / la.K + la.eps);
-    } else if (NORM == kNormLayer) {
+    } else {
       float s = 0.f;
-      for (int k = lane; k < la.K; k += 32) s += src[k];
+      for (int k = lane; k < la.K; k += 32) s += dst[k];
       mu = WarpSum(s) / la.K;
       float v = 0.f;
       for (int k = lane; k < la.K; k += 32) {
-        float t = src[k] - mu;
+        const float t = dst[k] - mu;
         v += t * t;
       }
       v = WarpSum(v) / la.K;
       is = 1.0f / sqrtf(v + la.eps);
     }
-    for (int k = lane; k < la.Kp; k += 32) {
-      float v = 0.f;
-      if (k < la.K) {
-        v = src[k];
-        if (NORM == kNormRms) v = la.gamma[k] * v * is;
-        else if (NORM == kNormLayer) v = la.gamma[k] * ((v - mu) * is) + la.beta[k];
-      }
-      dst[k] = v;
-    }
+    for (int k = lane; k < la.K; k += 32) dst[k] = (dst[k] - mu) * is;
   }
 }
 
@@ -236,11 +278,11 @@ __global__ void __launch_bounds__(kSimtWarps * 32) LinearSimtKernel(LinearArgs l
   for (int m = 0; m < MT; m++) acc[m][0] = acc[m][1] = 0.f;
   if (col < la.N) {
     const bf16* w0 = la.w + (size_t)col * la.Kp;
-    const bool has1 = col + 1 < la.N;
-    const bf16* w1 = has1 ? w0 + la.Kp : w0;
+    const bf16* w1 = col + 1 < la.N ? w0 + la.Kp : w0;
+#pragma unroll 4
     for (int k = lane * 8; k < la.Kp; k += 256) {
-      uint4 u0 = LoadNc16(w0 + k);
-      uint4 u1 = LoadNc16(w1 + k);
+      const uint4 u0 = LoadNc16(w0 + k);
+      const uint4 u1 = LoadNc16(w1 + k);
       float f0[8], f1[8];
       Bf16x8ToFloat(u0, f0);
       Bf16x8ToFloat(u1, f1);
@@ -268,6 +310,10 @@ __global__ void __launch_bounds__(kSimtWarps * 32) LinearSimtKernel(LinearArgs l
   for (int m = 0; m < MT; m++) {
     if (lane == m && m0 + m < la.M && col < la.N) {
       float v0 = acc[m][0], v1 = acc[m][1];
+      if (NORM == kNormLayer) {
+        v0 += la.c2[col];
+        if (col + 1 < la.N) v1 += la.c2[col + 1];
+      }
       epi.apply(m0 + m, col, v0, v1, la.N);
       if constexpr (IsLogits<Epi>::value) {
         ArgmaxMerge(bv, bi, v0, col);
@@ -303,7 +349,8 @@ struct EmbedArgs {
   const float* wte;     // [V, E]
   const float* wpe;     // [C, E] or nullptr
   float* x;             // [M, E]
-  int E;
+  bf16* xb;             // [M, ldxb]
+  int E, ldxb;
 };
 
 __global__ void EmbedKernel(EmbedArgs e) {
@@ -314,18 +361,26 @@ __global__ void EmbedKernel(EmbedArgs e) {
   const float* src = e.wte + (size_t)tok * e.E;
   const float* pe = e.wpe ? e.wpe + (size_t)p * e.E : nullptr;
   float* dst = e.x + (size_t)r * e.E;
-  for (int j = threadIdx.x; j < e.E; j += blockDim.x) dst[j] = pe ? src[j] + pe[j] : src[j];
+  bf16* db = e.xb + (size_t)r * e.ldxb;
+  for (int j = threadIdx.x; j < e.E; j += blockDim.x) {
+    const float v = pe ? src[j] + pe[j] : src[j];
+    dst[j] = v;
+    db[j] = __float2bfloat16_rn(v);
+  }
 }
 
 // ---- decode attention over the paged cache (AttendRow, CachedRowMath.ts:60-86) ---------------------
-// Grid (chunk, kv head, row). Each CTA takes one 64-position page of one KV head for one row, scores it
-// against the head's whole query group (GQA: heads g*G .. g*G+G-1 share the page), and writes a
-// partial (o, max, sum). The last CTA of a (row, kv head) to finish — counted with an atomic — merges
-// the partials in chunk order; with a single chunk the CTA writes the context directly.
+// Grid (chunk, kv head, row). Each CTA takes one 64-position page of one KV head for one row: one thread
+// copies the page's K and V blocks into shared memory with two bulk async copies, the CTA scores them
+// against the head's whole query group (GQA: heads g*G .. g*G+G-1 share the page) and writes a partial
+// (o, max, sum). The last CTA of a (row, kv head) to finish — counted with an atomic — merges the partials
+// in chunk order; with a single chunk the CTA writes the context directly.
 
 struct AttnArgs {
   const float* q;   // [M, H*d] post-RoPE
   float* ctx;       // [M, H*d]
+  bf16* ctxb;       // [M, ldcb]
+  int ldcb;
   KvView kv;
   int layer;
   const int* pos;
@@ -340,10 +395,15 @@ struct AttnArgs {
 };
 
 constexpr int kAttnThreads = 128;
+constexpr int kAttnWarps = kAttnThreads / 32;
 constexpr int kMaxGroup = 8;
 
+__device__ __forceinline__ void StoreCtx(const AttnArgs& aa, int m, int col, float v) {
+  aa.ctx[(size_t)m * aa.H * aa.d + col] = v;
+  aa.ctxb[(size_t)m * aa.ldcb + col] = __float2bfloat16_rn(v);
+}
+
 __device__ __forceinline__ void AttnMerge(const AttnArgs& aa, int m, int g, int nch) {
-  const int hd = aa.H * aa.d;
   for (int e = threadIdx.x; e < aa.G * aa.d; e += blockDim.x) {
     const int i = e / aa.d, j = e % aa.d;
     const int h = g * aa.G + i;
@@ -356,18 +416,17 @@ __device__ __forceinline__ void AttnMerge(const AttnArgs& aa, int m, int g, int 
       num += w * __ldcg(aa.part_o + (base + c) * aa.d + j);
       den += w * __ldcg(aa.part_l + base + c);
     }
-    aa.ctx[(size_t)m * hd + h * aa.d + j] = num / den;
+    StoreCtx(aa, m, h * aa.d + j, num / den);
   }
 }
 
 // Writes this CTA's per-head results; merges when it is the last chunk of its (row, kv head).
 __device__ __forceinline__ void AttnFinishChunk(const AttnArgs& aa, int m, int g, int c, int nch, const float* so,
                                                 const float* sm, const float* sl) {
-  const int hd = aa.H * aa.d;
   if (nch == 1) {
     for (int e = threadIdx.x; e < aa.G * aa.d; e += blockDim.x) {
       const int i = e / aa.d, j = e % aa.d;
-      aa.ctx[(size_t)m * hd + (g * aa.G + i) * aa.d + j] = so[e] / sl[i];
+      StoreCtx(aa, m, (g * aa.G + i) * aa.d + j, so[e] / sl[i]);
     }
     return;
   }
@@ -395,17 +454,28 @@ __device__ __forceinline__ void AttnFinishChunk(const AttnArgs& aa, int m, int g
   }
 }
 
+// One-dimensional bulk async copy global -> shared (16-byte aligned, size a multiple of 16), counted on bar.
+__device__ __forceinline__ void BulkCopyG2S(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   SmemAddr(dst)),
+               "l"(src), "r"(bytes), "r"(SmemAddr(bar))
+               : "memory");
+}
+
 // Fast path: head_dim D (multiple of 8, 32..128) known at compile time.
 template <int D>
 __global__ void __launch_bounds__(kAttnThreads) AttnDecodeKernel(AttnArgs aa) {
-  constexpr int LPP = D / 8;           // lanes per position (16 B of K each)
-  constexpr int PPW = 32 / LPP;        // positions per warp pass
-  constexpr int JPL = D / 32;          // output dims per lane
+  constexpr int LPP = D / 8;    // lanes per position (16 B of K each)
+  constexpr int PPW = 32 / LPP; // positions per warp pass
+  constexpr int JPL = D / 32;   // output dims per lane
+  __shared__ __align__(128) bf16 sk[kPageTokens * D];  // reused for the per-warp partial outputs
+  __shared__ __align__(128) bf16 sv[kPageTokens * D];
+  __shared__ __align__(8) uint64_t bar;
   __shared__ float sq[kMaxGroup][D];
   __shared__ float ss[kMaxGroup][kPageTokens];
-  __shared__ float so_part[kAttnThreads / 32][kMaxGroup * D];
   __shared__ float so[kMaxGroup * D];
   __shared__ float sm[kMaxGroup], sl[kMaxGroup];
+  static_assert(kAttnWarps * kMaxGroup * D * 4 <= kPageTokens * D * 2, "partials must fit in the K buffer");
   const int c = blockIdx.x, g = blockIdx.y, m = blockIdx.z;
   const int p = aa.pos[m];
   const int nch = (p + kPageTokens) / kPageTokens;  // positions 0..p
@@ -418,18 +488,34 @@ __global__ void __launch_bounds__(kAttnThreads) AttnDecodeKernel(AttnArgs aa) {
   const int slot = aa.slot[m];
   const bf16* kb = aa.kv.Block(slot, c, aa.layer, g, 0);
   const bf16* vb = aa.kv.Block(slot, c, aa.layer, g, 1);
-  const int tv = kb ? tn : 0;  // a missing page (recorded as an error) contributes no positions
+  int tv = kb ? tn : 0;  // a missing page (recorded as an error) contributes no positions
 
+  if (threadIdx.x == 0) {
+    MbarInit(&bar, 1);
+    FenceMbarInit();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0 && tv > 0) {
+    const uint32_t bytes = (uint32_t)tv * D * 2;
+    MbarArriveExpectTx(&bar, 2 * bytes);
+    BulkCopyG2S(sk, kb, bytes, &bar);
+    BulkCopyG2S(sv, vb, bytes, &bar);
+  }
   for (int e = threadIdx.x; e < G * D; e += blockDim.x) sq[e / D][e % D] = aa.q[(size_t)m * hd + g * G * D + e];
+  if (tv > 0 && !MbarWaitBounded(&bar, 0, kWaitLimit)) {
+    atomicCAS(&g_shahd_device_error, 0, kDevErrAttnTimeout);
+    tv = 0;
+  }
   __syncthreads();
 
   // scores s[i][t] = (q_i · k_t) * scale
   const int seg = lane % LPP;
-  for (int tb = warp * PPW; tb < kPageTokens; tb += (kAttnThreads / 32) * PPW) {
+#pragma unroll
+  for (int tb = warp * PPW; tb < kPageTokens; tb += kAttnWarps * PPW) {
     const int t = tb + lane / LPP;
     float kf[8];
     if (t < tv) {
-      uint4 u = LoadNc16(kb + (size_t)t * D + seg * 8);
+      const uint4 u = *reinterpret_cast<const uint4*>(sk + t * D + seg * 8);
       Bf16x8ToFloat(u, kf);
     } else {
 #pragma unroll
@@ -447,7 +533,7 @@ __global__ void __launch_bounds__(kAttnThreads) AttnDecodeKernel(AttnArgs aa) {
   __syncthreads();
 
   // per-head max and exp-sum over this chunk
-  for (int i = warp; i < G; i += kAttnThreads / 32) {
+  for (int i = warp; i < G; i += kAttnWarps) {
     float mx = -INFINITY;
     for (int t = lane; t < tv; t += 32) mx = fmaxf(mx, ss[i][t]);
     mx = WarpMax(mx);
@@ -471,15 +557,16 @@ __global__ void __launch_bounds__(kAttnThreads) AttnDecodeKernel(AttnArgs aa) {
   for (int i = 0; i < kMaxGroup; i++)
 #pragma unroll
     for (int jj = 0; jj < JPL; jj++) o[i][jj] = 0.f;
-  for (int t = warp; t < tv; t += kAttnThreads / 32) {
+#pragma unroll 4
+  for (int t = warp; t < tv; t += kAttnWarps) {
     float vf[JPL];
     if constexpr (JPL == 2) {
-      const float2 v2 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(vb + (size_t)t * D + lane * 2));
+      const float2 v2 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(sv + t * D + lane * 2));
       vf[0] = v2.x;
       vf[1] = v2.y;
     } else {
 #pragma unroll
-      for (int jj = 0; jj < JPL; jj++) vf[jj] = __bfloat162float(vb[(size_t)t * D + lane * JPL + jj]);
+      for (int jj = 0; jj < JPL; jj++) vf[jj] = __bfloat162float(sv[t * D + lane * JPL + jj]);
     }
 #pragma unroll
     for (int i = 0; i < kMaxGroup; i++) {
@@ -490,16 +577,17 @@ __global__ void __launch_bounds__(kAttnThreads) AttnDecodeKernel(AttnArgs aa) {
       }
     }
   }
+  float* so_part = reinterpret_cast<float*>(sk);  // K is no longer read: [warps][G*D]
 #pragma unroll
   for (int i = 0; i < kMaxGroup; i++)
     if (i < G)
 #pragma unroll
-      for (int jj = 0; jj < JPL; jj++) so_part[warp][i * D + lane * JPL + jj] = o[i][jj];
+      for (int jj = 0; jj < JPL; jj++) so_part[(warp * kMaxGroup + i) * D + lane * JPL + jj] = o[i][jj];
   __syncthreads();
   for (int e = threadIdx.x; e < G * D; e += blockDim.x) {
     float s = 0.f;
 #pragma unroll
-    for (int w = 0; w < kAttnThreads / 32; w++) s += so_part[w][e];
+    for (int w = 0; w < kAttnWarps; w++) s += so_part[w * kMaxGroup * D + e];
     so[e] = s;
   }
   __syncthreads();

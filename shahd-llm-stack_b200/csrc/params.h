@@ -7,8 +7,10 @@
 //         [F, Ep]  relu       row f = Wfc[:, f]
 //   w_down [E, Fp]            row e = W2[:, e] (or Wproj)
 //   w_head [V, Ep]            tied: Wte rows; untied: LmHead columns
-// All bf16, reduction dims zero-padded to multiples of 8 (16-byte rows for TMA); norms, biases,
-// embedding tables and the RoPE cos/sin table stay fp32.
+// All bf16, reduction dims zero-padded to multiples of 8 (16-byte rows for TMA); biases, embedding
+// tables and the RoPE cos/sin table stay fp32. The norm in front of w_qkv / w_up / w_head is folded in:
+// those weights carry gamma (W'[n,k] = W[n,k]·gamma[k]); for LayerNorm the per-column constants
+// c1[n] = sum_k W'[n,k] and c2[n] = sum_k beta[k]·W[n,k] let the kernels apply the mean and beta.
 #pragma once
 
 #include <cuda_bf16.h>
@@ -90,14 +92,39 @@ inline int BuildParamLayout(const ShahdModelCfg& c, ParamLayout* lay) {
 
 struct HostLayer {
   std::vector<bf16> w_qkv, w_o, w_up, w_down;
-  std::vector<float> ln1_g, ln1_b, ln2_g, ln2_b, b_fc, b_proj;
+  std::vector<float> qkv_c1, qkv_c2, up_c1, up_c2, b_fc, b_proj;
 };
 
 struct HostWeights {
   std::vector<HostLayer> layers;
   std::vector<bf16> w_head;
-  std::vector<float> head_bias, lnf_g, lnf_b, wte, wpe, rope_cos, rope_sin;
+  std::vector<float> head_bias, head_c1, head_c2, wte, wpe, rope_cos, rope_sin;
 };
+
+// Folds the norm (gamma, beta) in front of a projection stored as w [N, Kp] (rows already = columns of
+// the reference [K, N] matrix, in fp32 in `wf`): w = bf16(wf * gamma); LayerNorm constants c1/c2.
+inline void FoldNorm(const std::vector<float>& wf, int N, int K, int Kp, const float* gamma, const float* beta,
+                     bool layer_norm, std::vector<bf16>* w, std::vector<float>* c1, std::vector<float>* c2) {
+  w->assign((size_t)N * Kp, __float2bfloat16_rn(0.f));
+  if (layer_norm) {
+    c1->assign(N, 0.f);
+    c2->assign(N, 0.f);
+  }
+  for (int n = 0; n < N; n++) {
+    double s1 = 0, s2 = 0;
+    for (int k = 0; k < K; k++) {
+      const float orig = wf[(size_t)n * K + k];
+      const bf16 b = __float2bfloat16_rn(orig * gamma[k]);
+      (*w)[(size_t)n * Kp + k] = b;
+      s1 += (double)__bfloat162float(b);
+      if (beta) s2 += (double)beta[k] * orig;
+    }
+    if (layer_norm) {
+      (*c1)[n] = (float)s1;
+      (*c2)[n] = (float)s2;
+    }
+  }
+}
 
 template <typename T>
 inline int RepackTyped(const ShahdModelCfg& c, const ParamLayout& lay, const T* p, HostWeights* hw) {
@@ -120,58 +147,62 @@ inline int RepackTyped(const ShahdModelCfg& c, const ParamLayout& lay, const T* 
     const LayerParamOff& L = lay.layers[l];
     HostLayer& h = hw->layers[l];
     const int nqkv = (H + 2 * Hk) * d;
-    h.w_qkv.assign((size_t)nqkv * Ep, bf(0));
+    const bool lnorm = c.norm_kind == 0;
+    std::vector<float> g1 = vec(L.ln1_g, E), b1 = lnorm ? vec(L.ln1_b, E) : std::vector<float>();
+    std::vector<float> g2 = vec(L.ln2_g, E), b2 = lnorm ? vec(L.ln2_b, E) : std::vector<float>();
+    std::vector<float> wf((size_t)nqkv * E);
     for (int hh = 0; hh < H; hh++)
       for (int e = 0; e < E; e++)
-        for (int j = 0; j < d; j++)
-          h.w_qkv[(size_t)(hh * d + j) * Ep + e] = bf(p[L.wq + (int64_t)hh * E * d + (int64_t)e * d + j]);
+        for (int j = 0; j < d; j++) wf[(size_t)(hh * d + j) * E + e] = (float)p[L.wq + (int64_t)hh * E * d + (int64_t)e * d + j];
     for (int g = 0; g < Hk; g++)
       for (int e = 0; e < E; e++)
         for (int j = 0; j < d; j++) {
-          h.w_qkv[(size_t)(H * d + g * d + j) * Ep + e] = bf(p[L.wk + (int64_t)g * E * d + (int64_t)e * d + j]);
-          h.w_qkv[(size_t)((H + Hk) * d + g * d + j) * Ep + e] = bf(p[L.wv + (int64_t)g * E * d + (int64_t)e * d + j]);
+          wf[(size_t)(H * d + g * d + j) * E + e] = (float)p[L.wk + (int64_t)g * E * d + (int64_t)e * d + j];
+          wf[(size_t)((H + Hk) * d + g * d + j) * E + e] = (float)p[L.wv + (int64_t)g * E * d + (int64_t)e * d + j];
         }
+    FoldNorm(wf, nqkv, E, Ep, g1.data(), lnorm ? b1.data() : nullptr, lnorm, &h.w_qkv, &h.qkv_c1, &h.qkv_c2);
     h.w_o.assign((size_t)E * HDp, bf(0));
     for (int hh = 0; hh < H; hh++)
       for (int j = 0; j < d; j++)
         for (int e = 0; e < E; e++)
           h.w_o[(size_t)e * HDp + hh * d + j] = bf(p[L.wo + (int64_t)hh * d * E + (int64_t)j * E + e]);
-    h.ln1_g = vec(L.ln1_g, E);
-    if (L.ln1_b >= 0) h.ln1_b = vec(L.ln1_b, E);
-    h.ln2_g = vec(L.ln2_g, E);
-    if (L.ln2_b >= 0) h.ln2_b = vec(L.ln2_b, E);
     if (c.mlp_kind == 0) {
-      h.w_up.assign((size_t)F * Ep, bf(0));
+      std::vector<float> uf((size_t)F * E);
       for (int e = 0; e < E; e++)
-        for (int f = 0; f < F; f++) h.w_up[(size_t)f * Ep + e] = bf(p[L.wfc + (int64_t)e * F + f]);
+        for (int f = 0; f < F; f++) uf[(size_t)f * E + e] = (float)p[L.wfc + (int64_t)e * F + f];
+      FoldNorm(uf, F, E, Ep, g2.data(), lnorm ? b2.data() : nullptr, lnorm, &h.w_up, &h.up_c1, &h.up_c2);
       h.b_fc = vec(L.bfc, F);
       h.w_down.assign((size_t)E * Fp, bf(0));
       for (int f = 0; f < F; f++)
         for (int e = 0; e < E; e++) h.w_down[(size_t)e * Fp + f] = bf(p[L.wproj + (int64_t)f * E + e]);
       h.b_proj = vec(L.bproj, E);
     } else {
-      h.w_up.assign((size_t)2 * F * Ep, bf(0));
+      std::vector<float> uf((size_t)2 * F * E);
       for (int e = 0; e < E; e++)
         for (int f = 0; f < F; f++) {
-          h.w_up[(size_t)(2 * f) * Ep + e] = bf(p[L.w1 + (int64_t)e * F + f]);
-          h.w_up[(size_t)(2 * f + 1) * Ep + e] = bf(p[L.w3 + (int64_t)e * F + f]);
+          uf[(size_t)(2 * f) * E + e] = (float)p[L.w1 + (int64_t)e * F + f];
+          uf[(size_t)(2 * f + 1) * E + e] = (float)p[L.w3 + (int64_t)e * F + f];
         }
+      FoldNorm(uf, 2 * F, E, Ep, g2.data(), lnorm ? b2.data() : nullptr, lnorm, &h.w_up, &h.up_c1, &h.up_c2);
       h.w_down.assign((size_t)E * Fp, bf(0));
       for (int f = 0; f < F; f++)
         for (int e = 0; e < E; e++) h.w_down[(size_t)e * Fp + f] = bf(p[L.w2 + (int64_t)f * E + e]);
     }
   }
-  hw->w_head.assign((size_t)V * Ep, bf(0));
-  if (c.weight_tying) {
-    for (int v = 0; v < V; v++)
-      for (int e = 0; e < E; e++) hw->w_head[(size_t)v * Ep + e] = bf(p[lay.wte + (int64_t)v * E + e]);
-  } else {
-    for (int e = 0; e < E; e++)
-      for (int v = 0; v < V; v++) hw->w_head[(size_t)v * Ep + e] = bf(p[lay.lm_head + (int64_t)e * V + v]);
+  {
+    const bool lnorm = c.norm_kind == 0;
+    std::vector<float> gf = vec(lay.lnf_g, E), bfv = lnorm ? vec(lay.lnf_b, E) : std::vector<float>();
+    std::vector<float> hf((size_t)V * E);
+    if (c.weight_tying) {
+      for (int v = 0; v < V; v++)
+        for (int e = 0; e < E; e++) hf[(size_t)v * E + e] = (float)p[lay.wte + (int64_t)v * E + e];
+    } else {
+      for (int e = 0; e < E; e++)
+        for (int v = 0; v < V; v++) hf[(size_t)v * E + e] = (float)p[lay.lm_head + (int64_t)e * V + v];
+    }
+    FoldNorm(hf, V, E, Ep, gf.data(), lnorm ? bfv.data() : nullptr, lnorm, &hw->w_head, &hw->head_c1, &hw->head_c2);
   }
   hw->head_bias = vec(lay.lm_bias, V);
-  hw->lnf_g = vec(lay.lnf_g, E);
-  if (lay.lnf_b >= 0) hw->lnf_b = vec(lay.lnf_b, E);
   hw->wte = vec(lay.wte, (int64_t)V * E);
   if (lay.wpe >= 0) hw->wpe = vec(lay.wpe, (int64_t)C * E);
   if (c.position_scheme == 1) {

@@ -11,7 +11,7 @@
 
 namespace shahd {
 
-int g_umma_min_rows = 32;
+int g_umma_min_rows = 17;
 
 // ---- thread-local last error --------------------------------------------------------------------
 static thread_local std::string t_error;
@@ -382,7 +382,7 @@ void SetKernelThreads(int n) { (void)n; }
 
 int ShahdCpuSupportsAvx2Fma(void) { return DeviceOk(); }
 
-void SetScalarKernels(int force) { g_umma_min_rows = force ? 0x7fffffff : 32; }
+void SetScalarKernels(int force) { g_umma_min_rows = force ? 0x7fffffff : 17; }
 
 int ShahdGpuAvailable(void) { return DeviceOk(); }
 

@@ -1,6 +1,11 @@
 // Decode-level session: device-resident weights, paged KV pool, batched cached steps and the
 // on-device CachedGenerate loop (Brain/Sampling/CachedForward.ts:94-199) behind the C ABI of
 // include/shahd_b200.h.
+//
+// All device work of a session runs on the session's own stream; a caller stream passed to
+// shahd_generate_device is joined with events at entry and exit. Prefill and decode steps are captured
+// once per shape into CUDA graphs and replayed; positions, tokens and outputs live in device buffers, so
+// a replay needs no host update.
 #include <algorithm>
 #include <cmath>
 #include <cstdarg>
@@ -8,6 +13,7 @@
 #include <map>
 #include <mutex>
 #include <numeric>
+#include <tuple>
 #include <vector>
 
 #include "../../include/shahd_b200.h"
@@ -19,13 +25,25 @@ namespace shahd {
 
 struct Layer {
   bf16 *w_qkv, *w_o, *w_up, *w_down;
-  float *ln1_g, *ln1_b, *ln2_g, *ln2_b, *b_fc, *b_proj;
+  float *qkv_c1, *qkv_c2, *up_c1, *up_c2, *b_fc, *b_proj;
 };
 
+// Everything a captured step bakes in.
 struct GraphKey {
-  int n;
-  int mode;
-  bool operator<(const GraphKey& o) const { return n != o.n ? n < o.n : mode < o.mode; }
+  int kind;  // 0 = prefill step, 1 = decode step
+  int M;
+  const void *slot, *tok, *poff, *prompt, *out;
+  int out_ld;
+  int min_rows;
+  bool operator<(const GraphKey& o) const {
+    return std::tie(kind, M, slot, tok, poff, prompt, out, out_ld, min_rows) <
+           std::tie(o.kind, o.M, o.slot, o.tok, o.poff, o.prompt, o.out, o.out_ld, o.min_rows);
+  }
+};
+
+struct StepGraph {
+  cudaGraphExec_t exec;
+  int launches;
 };
 
 }  // namespace shahd
@@ -37,40 +55,42 @@ struct ShahdSession {
   int Nqkv, Nup;
   int device;
   int max_seqs;
-  cudaStream_t stream;
+  cudaStream_t stream = nullptr;
+  cudaEvent_t join_in = nullptr, join_out = nullptr;
   std::mutex mu;
   std::vector<void*> allocs;
 
   std::vector<shahd::Layer> layers;
   shahd::bf16* w_head;
-  float *head_bias, *lnf_g, *lnf_b, *wte, *wpe, *rope_cos, *rope_sin;
+  float *head_bias, *head_c1, *head_c2, *wte, *wpe, *rope_cos, *rope_sin;
 
   // paged KV pool
   shahd::bf16* kv_pool;
   size_t page_elems;
   int kv_pages, max_blocks;
   int* d_block_table;
-  int* h_block_table;  // pinned mirror
+  int* h_block_table = nullptr;  // pinned mirror
   std::vector<int> free_pages;
   std::vector<int> h_len;
   int* d_seq_len;
 
-  // per-row scratch (capacity max_seqs rows)
+  // per-row scratch (capacity max_seqs rows): fp32 masters and bf16 tensor-core operands
   float *x, *q, *ctx, *act, *logits, *am_val;
+  shahd::bf16 *xb, *ctxb, *actb;
   int* am_idx;
   int am_stride;
   float *part_o, *part_m, *part_l;
   int* attn_counter;
-  int *d_slot, *d_tok, *d_pos, *d_next, *d_gen_count, *d_poff, *d_pf_slot, *d_pf_poff;
-  int* d_prompt;
-  size_t prompt_cap;
+  int *d_slot, *d_tok, *d_pos, *d_next, *d_gen_count, *d_ends, *d_pf_slot, *d_pf_poff, *d_starts, *d_full_len,
+      *d_rows;
+  int* d_prompt = nullptr;
+  size_t prompt_cap = 0;
   int* d_window;
-  int* d_out;
-  size_t out_cap;
-  int* h_pinned_rows;  // pinned staging for per-call row arrays
-  float* d_logits_full;
+  int* d_out = nullptr;
+  size_t out_cap = 0;
+  int* h_pinned_rows = nullptr;  // pinned staging for per-call row arrays [kStagingRows][max_seqs]
 
-  std::map<shahd::GraphKey, cudaGraphExec_t> graphs;
+  std::map<shahd::GraphKey, shahd::StepGraph> graphs;
 
   // measurement: kernel launch count, and optional CUDA-event timing per kernel class
   long long launches = 0;
@@ -89,6 +109,8 @@ namespace shahd {
 
 namespace {
 
+constexpr int kStagingRows = 8;
+
 template <class T>
 int DevAlloc(ShahdSession* s, T** p, size_t count) {
   void* v = nullptr;
@@ -103,9 +125,9 @@ int DevAlloc(ShahdSession* s, T** p, size_t count) {
   return SHAHD_OK;
 }
 
-#define SHAHD_TRY(expr)        \
-  do {                         \
-    int rc_ = (expr);          \
+#define SHAHD_TRY(expr)              \
+  do {                               \
+    int rc_ = (expr);                \
     if (rc_ != SHAHD_OK) return rc_; \
   } while (0)
 
@@ -150,6 +172,7 @@ int HeadBlocks(const ShahdSession* s, int M) {
   la.K = s->E;
   la.Kp = s->Ep;
   la.N = s->V;
+  la.ab = s->xb;
   if (M >= kUmmaMinRows && UmmaLinearSupported(la)) return CeilDiv(la.N, UmmaBN(M, la.N));
   return CeilDiv(s->V, kSimtCols);
 }
@@ -195,31 +218,41 @@ void Timed(ShahdSession* s, cudaStream_t st, int kind, double bytes, F&& launch)
   s->prof_recs.push_back({kind, e0, e1, bytes});
 }
 
-// Algorithmic bytes of one projection: bf16 weights once, fp32 activations in, fp32 results out.
-double LinearBytes(int M, int K, int Kp, int N) { return 2.0 * N * Kp + 4.0 * M * K + 4.0 * M * N; }
+// Algorithmic bytes of one projection: bf16 weights once, bf16 activations in, fp32 results out.
+double LinearBytes(int M, int K, int Kp, int N) { return 2.0 * N * Kp + 2.0 * M * K + 4.0 * M * N; }
 
-// Enqueue one batched cached step (AdvanceOneToken + HeadLogitsRow for M rows) on `st`.
-void EnqueueStep(ShahdSession* s, const StepPlan& p, cudaStream_t st) {
-  const int M = p.M;
+LinearArgs Lin(const float* a, int lda, const bf16* ab, int ldab, int rows_cap, int M, int K, int Kp, const bf16* w,
+               int N, float eps, const float* c1, const float* c2, float* amv = nullptr, int* ami = nullptr) {
+  LinearArgs la;
+  la.a = a; la.lda = lda; la.ab = ab; la.ldab = ldab; la.a_rows = rows_cap; la.M = M; la.K = K; la.Kp = Kp;
+  la.w = w; la.N = N; la.eps = eps; la.c1 = c1; la.c2 = c2; la.am_val = amv; la.am_idx = ami;
+  return la;
+}
+
+// Enqueue one batched cached step (AdvanceOneToken + HeadLogitsRow for M rows) on `st`; returns the
+// number of kernels it launched.
+int EnqueueStep(ShahdSession* s, const StepPlan& p, cudaStream_t st) {
+  const long long before = s->launches;
+  const int M = p.M, R = s->max_seqs;
   const int norm = s->cfg.norm_kind == 1 ? kNormRms : kNormLayer;
+  const float eps = (float)s->cfg.layer_norm_eps;
   Timed(s, st, kProfOther, 8.0 * M * s->E, [&] {
-    EmbedArgs e{p.slot, p.tok, p.prompt, p.poff, s->d_seq_len, s->d_pos, s->wte, s->wpe, s->x, s->E};
+    EmbedArgs e{p.slot, p.tok, p.prompt, p.poff, s->d_seq_len, s->d_pos, s->wte, s->wpe, s->x, s->xb, s->E, s->Ep};
     EmbedKernel<<<M, 128, 0, st>>>(e);
   });
   KvView kv{s->kv_pool, s->d_block_table, s->max_blocks, s->Hk, s->d, s->page_elems};
   const int hd = s->H * s->d;
-  // K and V rows read (bf16) + q read and ctx written (fp32)
-  const double attn_bytes = 4.0 * s->Hk * s->d * (double)p.attended + 8.0 * M * hd;
+  // K and V rows read (bf16) + q read and ctx written (fp32 + bf16)
+  const double attn_bytes = 4.0 * s->Hk * s->d * (double)p.attended + 10.0 * M * hd;
   for (int l = 0; l < s->L; l++) {
     const Layer& Ly = s->layers[l];
     // norm1 + QKV + RoPE + KV append (CachedForward.ts:66-73, :78-79)
-    LinearArgs la{s->x, s->E, M, s->E, s->Ep, Ly.w_qkv, s->Nqkv, Ly.ln1_g, Ly.ln1_b, (float)s->cfg.layer_norm_eps,
-                  nullptr, nullptr};
-    EpiQKV eq{s->q, kv, l, s->d_pos, p.slot, s->rope_cos, s->rope_sin, s->H, s->Hk, s->d};
+    const LinearArgs la = Lin(s->x, s->E, s->xb, s->Ep, R, M, s->E, s->Ep, Ly.w_qkv, s->Nqkv, eps, Ly.qkv_c1, Ly.qkv_c2);
+    const EpiQKV eq{s->q, kv, l, s->d_pos, p.slot, s->rope_cos, s->rope_sin, s->H, s->Hk, s->d};
     Timed(s, st, kProfLinear, LinearBytes(M, s->E, s->Ep, s->Nqkv), [&] { LaunchLinear(norm, la, eq, st); });
     // attention over the cache (CachedForward.ts:76-80)
-    AttnArgs aa{s->q, s->ctx, kv, l, s->d_pos, p.slot, s->H, s->Hk, s->G, s->d, (float)(1.0 / std::sqrt((double)s->d)),
-                s->max_blocks, s->part_o, s->part_m, s->part_l, s->attn_counter};
+    AttnArgs aa{s->q, s->ctx, s->ctxb, s->HDp, kv, l, s->d_pos, p.slot, s->H, s->Hk, s->G, s->d,
+                (float)(1.0 / std::sqrt((double)s->d)), s->max_blocks, s->part_o, s->part_m, s->part_l, s->attn_counter};
     dim3 ag(s->max_blocks, s->Hk, M);
     Timed(s, st, kProfAttention, attn_bytes, [&] {
       if (s->d == 64) AttnDecodeKernel<64><<<ag, kAttnThreads, 0, st>>>(aa);
@@ -228,32 +261,32 @@ void EnqueueStep(ShahdSession* s, const StepPlan& p, cudaStream_t st) {
       else AttnDecodeGenericKernel<<<ag, kAttnThreads, 0, st>>>(aa);
     });
     // summed per-head Wo + residual (CachedForward.ts:81-84)
-    LinearArgs lo{s->ctx, hd, M, hd, s->HDp, Ly.w_o, s->E, nullptr, nullptr, 0.f, nullptr, nullptr};
+    const LinearArgs lo = Lin(s->ctx, hd, s->ctxb, s->HDp, R, M, hd, s->HDp, Ly.w_o, s->E, eps, nullptr, nullptr);
     Timed(s, st, kProfLinear, LinearBytes(M, hd, s->HDp, s->E),
-          [&] { LaunchLinear(kNormNone, lo, EpiResid{s->x, s->E, nullptr}, st); });
+          [&] { LaunchLinear(kNormNone, lo, EpiResid{s->x, s->xb, s->E, s->Ep, nullptr}, st); });
     // norm2 + MLP + residual (CachedForward.ts:86-87)
-    LinearArgs lu{s->x, s->E, M, s->E, s->Ep, Ly.w_up, s->Nup, Ly.ln2_g, Ly.ln2_b, (float)s->cfg.layer_norm_eps,
-                  nullptr, nullptr};
+    const LinearArgs lu = Lin(s->x, s->E, s->xb, s->Ep, R, M, s->E, s->Ep, Ly.w_up, s->Nup, eps, Ly.up_c1, Ly.up_c2);
     Timed(s, st, kProfLinear, LinearBytes(M, s->E, s->Ep, s->Nup), [&] {
-      if (s->cfg.mlp_kind == 0) LaunchLinear(norm, lu, EpiReluFc{s->act, s->F, Ly.b_fc}, st);
-      else LaunchLinear(norm, lu, EpiGated{s->act, s->F, s->cfg.mlp_kind == 2}, st);
+      if (s->cfg.mlp_kind == 0) LaunchLinear(norm, lu, EpiReluFc{s->act, s->actb, s->F, s->Fp, Ly.b_fc}, st);
+      else LaunchLinear(norm, lu, EpiGated{s->act, s->actb, s->F, s->Fp, s->cfg.mlp_kind == 2}, st);
     });
-    LinearArgs ld{s->act, s->F, M, s->F, s->Fp, Ly.w_down, s->E, nullptr, nullptr, 0.f, nullptr, nullptr};
+    const LinearArgs ld = Lin(s->act, s->F, s->actb, s->Fp, R, M, s->F, s->Fp, Ly.w_down, s->E, eps, nullptr, nullptr);
     Timed(s, st, kProfLinear, LinearBytes(M, s->F, s->Fp, s->E),
-          [&] { LaunchLinear(kNormNone, ld, EpiResid{s->x, s->E, Ly.b_proj}, st); });
+          [&] { LaunchLinear(kNormNone, ld, EpiResid{s->x, s->xb, s->E, s->Ep, Ly.b_proj}, st); });
   }
   int nblk = 0;
   if (p.head) {
     // final norm + LM head + argmax partials (HeadLogitsRow, CachedRowMath.ts:117-137)
     nblk = HeadBlocks(s, M);
-    LinearArgs lh{s->x, s->E, M, s->E, s->Ep, s->w_head, s->V, s->lnf_g, s->lnf_b, (float)s->cfg.layer_norm_eps,
-                  s->am_val, s->am_idx};
+    const LinearArgs lh = Lin(s->x, s->E, s->xb, s->Ep, R, M, s->E, s->Ep, s->w_head, s->V, eps, s->head_c1, s->head_c2,
+                              s->am_val, s->am_idx);
     Timed(s, st, kProfLinear, LinearBytes(M, s->E, s->Ep, s->V),
           [&] { LaunchLinear(norm, lh, EpiLogits{p.logits, s->head_bias}, st); });
   }
   FinishArgs f{M, p.slot, s->d_pos, s->d_seq_len, p.head ? s->am_val : nullptr, s->am_idx, nblk, p.next_ids,
                p.cur_tok, p.out_ids, p.out_ld, s->d_gen_count, nullptr};
   Timed(s, st, kProfOther, 16.0 * M, [&] { FinishKernel<<<CeilDiv(M, 128), 128, 0, st>>>(f); });
+  return (int)(s->launches - before);
 }
 
 int CheckLaunch(const char* what) {
@@ -262,6 +295,47 @@ int CheckLaunch(const char* what) {
     SetError("%s: kernel launch failed: %s", what, cudaGetErrorString(e));
     return SHAHD_ECUDA;
   }
+  return SHAHD_OK;
+}
+
+// Run a step through a cached CUDA graph. The first use of a shape runs eagerly (lazy host-side setup
+// such as kernel attributes and TMA descriptors stays out of capture), the second captures it, every
+// later one replays it. Profiling runs eagerly so each kernel can be bracketed with events.
+int RunStep(ShahdSession* s, const StepPlan& p, int kind) {
+  if (s->prof) {
+    EnqueueStep(s, p, s->stream);
+    return CheckLaunch("step");
+  }
+  GraphKey key{kind, p.M, p.slot, p.tok, p.poff, p.prompt, p.out_ids, p.out_ld, g_umma_min_rows};
+  auto it = s->graphs.find(key);
+  if (it == s->graphs.end()) {
+    EnqueueStep(s, p, s->stream);
+    SHAHD_TRY(CheckLaunch("step"));
+    s->graphs.emplace(key, StepGraph{nullptr, 0});
+    return SHAHD_OK;
+  }
+  if (it->second.exec == nullptr) {
+    cudaGraph_t g = nullptr;
+    SHAHD_CUDA_TRY(cudaStreamBeginCapture(s->stream, cudaStreamCaptureModeThreadLocal));
+    const long long saved = s->launches;
+    const int n = EnqueueStep(s, p, s->stream);
+    s->launches = saved;
+    cudaError_t e = cudaStreamEndCapture(s->stream, &g);
+    if (e != cudaSuccess) {
+      SetError("step capture failed: %s", cudaGetErrorString(e));
+      return SHAHD_ECUDA;
+    }
+    e = cudaGraphInstantiate(&it->second.exec, g, 0);
+    cudaGraphDestroy(g);
+    if (e != cudaSuccess) {
+      it->second.exec = nullptr;
+      SetError("step graph instantiate failed: %s", cudaGetErrorString(e));
+      return SHAHD_ECUDA;
+    }
+    it->second.launches = n;
+  }
+  SHAHD_CUDA_TRY(cudaGraphLaunch(it->second.exec, s->stream));
+  s->launches += it->second.launches;
   return SHAHD_OK;
 }
 
@@ -296,17 +370,20 @@ int EnsurePages(ShahdSession* s, int slot, int upto) {
   return SHAHD_OK;
 }
 
+// Block table and lengths to the device. The pinned mirror is only modified while the session stream is
+// idle, so the asynchronous copy reads the values of this call.
 int UploadTables(ShahdSession* s) {
   SHAHD_CUDA_TRY(cudaMemcpyAsync(s->d_block_table, s->h_block_table, sizeof(int) * (size_t)s->max_seqs * s->max_blocks,
                                  cudaMemcpyHostToDevice, s->stream));
-  // Synchronous on purpose: the pinned mirror may change right after this call returns.
-  SHAHD_CUDA_TRY(cudaStreamSynchronize(s->stream));
   return SHAHD_OK;
 }
 
+int* Staging(ShahdSession* s, int row) { return s->h_pinned_rows + (size_t)row * s->max_seqs; }
+
 int UploadLengths(ShahdSession* s) {
-  std::vector<int> tmp(s->h_len);
-  SHAHD_CUDA_TRY(cudaMemcpy(s->d_seq_len, tmp.data(), sizeof(int) * tmp.size(), cudaMemcpyHostToDevice));
+  int* h = Staging(s, kStagingRows - 1);
+  std::copy(s->h_len.begin(), s->h_len.end(), h);
+  SHAHD_CUDA_TRY(cudaMemcpyAsync(s->d_seq_len, h, sizeof(int) * s->max_seqs, cudaMemcpyHostToDevice, s->stream));
   return SHAHD_OK;
 }
 
@@ -315,7 +392,7 @@ __global__ void GatherLastTokens(const int* prompt, const int* ends, int n, int*
   if (r < n) cur[r] = prompt[ends[r] - 1];
 }
 
-// Window rebuild input: the last (C-1) tokens of prompt_r ++ out_r[0..gen) (CachedForward.ts:133-141).
+// Window rebuild input: the last `keep` ids of prompt_r ++ out_r[0..gen) (CachedForward.ts:133-141).
 __global__ void GatherWindow(const int* prompt, const int* pstart, const int* plen, const int* out, int out_ld,
                              const int* rows, int nrows, int gen, int keep, int* window) {
   int i = blockIdx.x;
@@ -334,18 +411,16 @@ __global__ void SetLengths(int* seq_len, const int* slots, int n, int value) {
   if (i < n) seq_len[slots[i]] = value;
 }
 
-// Prefill rows (already reset, lengths 0) by cached steps over their contexts: row i of the plan takes
-// ids[poff_i + t] at step t while t < len_i. Rows must be ordered by descending length.
+// Prefill rows (already reset, lengths 0, pages assigned) by cached steps over their contexts: row i of
+// the plan takes ids[poff_i + t] at step t while t < len_i. Rows are ordered by descending length.
 int PrefillBySteps(ShahdSession* s, const int* d_slots, const int* d_poff, const int* d_prompt,
                    const std::vector<int>& lens_desc, const std::vector<int>& slots_desc) {
   if (lens_desc.empty() || lens_desc[0] == 0) return SHAHD_OK;
-  for (size_t i = 0; i < slots_desc.size(); i++) SHAHD_TRY(EnsurePages(s, slots_desc[i], lens_desc[i]));
-  SHAHD_TRY(UploadTables(s));
   for (int t = 0; t < lens_desc[0]; t++) {
     int M = 0;
     while (M < (int)lens_desc.size() && lens_desc[M] > t) M++;
     StepPlan p{M, d_slots, nullptr, d_poff, d_prompt, false, nullptr, nullptr, nullptr, nullptr, 0, (long long)M * (t + 1)};
-    EnqueueStep(s, p, s->stream);
+    SHAHD_TRY(RunStep(s, p, 0));
   }
   for (size_t i = 0; i < slots_desc.size(); i++) s->h_len[slots_desc[i]] = lens_desc[i];
   return CheckLaunch("prefill");
@@ -396,10 +471,10 @@ int GrowOut(ShahdSession* s, size_t count) {
   return SHAHD_OK;
 }
 
-// Core of shahd_generate / shahd_generate_device. d_prompt_packed holds the packed prompts on the
-// device; offs their host offsets. Output ids land in d_out [n, max_new].
+// Core of shahd_generate / shahd_generate_device on the session stream. d_prompt_packed holds the packed
+// prompts on the device; offs their host offsets. Output ids land in d_out [n, max_new].
 int GenerateCore(ShahdSession* s, const int* d_prompt_packed, const std::vector<int>& offs, int n, int max_new,
-                 const ShahdSampling* o, int* d_out, cudaStream_t st) {
+                 const ShahdSampling* o, int* d_out) {
   if (o && o->temperature > 0) {
     SetError("shahd_generate: stochastic sampling (temperature > 0) is not supported by this build");
     return SHAHD_EINVAL;
@@ -409,91 +484,90 @@ int GenerateCore(ShahdSession* s, const int* d_prompt_packed, const std::vector<
   std::vector<int> plen(n), pstart(n), full_len(n);
   for (int i = 0; i < n; i++) {
     full_len[i] = offs[i + 1] - offs[i];
-    int ctx = std::min(full_len[i], C);
+    const int ctx = std::min(full_len[i], C);
     pstart[i] = offs[i + 1] - ctx;
     plen[i] = ctx - 1;
   }
-  SHAHD_CUDA_TRY(cudaStreamSynchronize(s->stream));
+  SHAHD_CUDA_TRY(cudaStreamSynchronize(s->stream));  // pinned staging and tables are rewritten below
   for (int i = 0; i < n; i++) ResetSlot(s, i);
   // Pages for the whole run up front: positions reach min(plen + max_new, C).
   for (int i = 0; i < n; i++) SHAHD_TRY(EnsurePages(s, i, std::min(plen[i] + max_new, C)));
   SHAHD_TRY(UploadTables(s));
   SHAHD_TRY(UploadLengths(s));
 
-  // prefill-by-steps in descending-length order
   std::vector<int> order(n);
   std::iota(order.begin(), order.end(), 0);
   std::stable_sort(order.begin(), order.end(), [&](int a, int b) { return plen[a] > plen[b]; });
-  int* h = s->h_pinned_rows;
   std::vector<int> lens_desc(n), slots_desc(n);
+  int *h_pf_slot = Staging(s, 0), *h_pf_poff = Staging(s, 1), *h_slot = Staging(s, 2), *h_ends = Staging(s, 3),
+      *h_starts = Staging(s, 4), *h_full = Staging(s, 5);
   for (int i = 0; i < n; i++) {
-    h[i] = order[i];                 // slot
-    h[s->max_seqs + i] = pstart[order[i]];  // gather offset
+    h_pf_slot[i] = order[i];
+    h_pf_poff[i] = pstart[order[i]];
     lens_desc[i] = plen[order[i]];
     slots_desc[i] = order[i];
+    h_slot[i] = i;
+    h_ends[i] = offs[i + 1];
+    h_starts[i] = offs[i];
+    h_full[i] = full_len[i];
   }
-  SHAHD_CUDA_TRY(cudaMemcpyAsync(s->d_pf_slot, h, sizeof(int) * n, cudaMemcpyHostToDevice, st));
-  SHAHD_CUDA_TRY(cudaMemcpyAsync(s->d_pf_poff, h + s->max_seqs, sizeof(int) * n, cudaMemcpyHostToDevice, st));
-  // decode-order rows: slot r = row r
-  for (int i = 0; i < n; i++) {
-    h[2 * s->max_seqs + i] = i;
-    h[3 * s->max_seqs + i] = offs[i + 1];
-    h[4 * s->max_seqs + i] = offs[i];
-    h[5 * s->max_seqs + i] = full_len[i];
-  }
-  SHAHD_CUDA_TRY(cudaMemcpyAsync(s->d_slot, h + 2 * s->max_seqs, sizeof(int) * n, cudaMemcpyHostToDevice, st));
-  SHAHD_CUDA_TRY(cudaMemcpyAsync(s->d_poff, h + 3 * s->max_seqs, sizeof(int) * n, cudaMemcpyHostToDevice, st));
-  SHAHD_CUDA_TRY(cudaMemsetAsync(s->d_gen_count, 0, sizeof(int) * n, st));
-  SHAHD_CUDA_TRY(cudaStreamSynchronize(st));  // pinned staging reused below
-  if (st != s->stream) {
-    // all work of this call is ordered on the caller's stream
-  }
-  cudaStream_t saved = s->stream;
-  s->stream = st;
-  int rc = PrefillBySteps(s, s->d_pf_slot, s->d_pf_poff, d_prompt_packed, lens_desc, slots_desc);
-  if (rc == SHAHD_OK) {
-    GatherLastTokens<<<CeilDiv(n, 128), 128, 0, st>>>(d_prompt_packed, s->d_poff, n, s->d_tok);
-    s->launches++;
-    // the decode loop: step k consumes the last context id (k = 0) or the id sampled at k-1
-    StepPlan p{n, s->d_slot, s->d_tok, nullptr, nullptr, true, nullptr, nullptr, s->d_tok, d_out, max_new, 0};
-    for (int k = 0; k < max_new && rc == SHAHD_OK; k++) {
-      // rows whose window is full rebuild it from their last C-1 ids first (CachedForward.ts:135-141)
-      std::vector<int> slide;
-      for (int i = 0; i < n; i++)
-        if (s->h_len[i] >= C) slide.push_back(i);
-      if (!slide.empty()) {
-        const int keep = C - 1;
-        const int ns = (int)slide.size();
-        for (int i = 0; i < ns; i++) h[6 * s->max_seqs + i] = slide[i];
-        int* d_rows = s->d_next;  // scratch [ns]
-        cudaMemcpyAsync(d_rows, h + 6 * s->max_seqs, sizeof(int) * ns, cudaMemcpyHostToDevice, st);
-        cudaMemcpyAsync(s->d_pf_slot, h + 5 * s->max_seqs, sizeof(int) * n, cudaMemcpyHostToDevice, st);  // full lengths
-        // GatherWindow needs per-row prompt start/length and the output so far: rows are slots here
-        cudaMemcpyAsync(s->d_pf_poff, h + 4 * s->max_seqs, sizeof(int) * n, cudaMemcpyHostToDevice, st);  // prompt starts
-        GatherWindow<<<ns, 128, 0, st>>>(d_prompt_packed, s->d_pf_poff, s->d_pf_slot, d_out, max_new, d_rows, ns, k - 1,
-                                         keep, s->d_window);
-        SetLengths<<<CeilDiv(ns, 128), 128, 0, st>>>(s->d_seq_len, d_rows, ns, 0);
-        s->launches += 2;
-        for (int i = 0; i < ns; i++) {
-          h[7 * s->max_seqs + i] = i * keep;  // gather offsets into the window buffer
-          s->h_len[slide[i]] = 0;
-        }
-        cudaMemcpyAsync(s->d_pf_poff, h + 7 * s->max_seqs, sizeof(int) * ns, cudaMemcpyHostToDevice, st);
-        cudaMemcpyAsync(s->d_pf_slot, h + 6 * s->max_seqs, sizeof(int) * ns, cudaMemcpyHostToDevice, st);
-        std::vector<int> lens(ns, keep);
-        rc = PrefillBySteps(s, s->d_pf_slot, s->d_pf_poff, s->d_window, lens, slide);
-        cudaStreamSynchronize(st);  // pinned staging reused next step
-        if (rc != SHAHD_OK) break;
+  SHAHD_CUDA_TRY(cudaMemcpyAsync(s->d_pf_slot, h_pf_slot, sizeof(int) * n, cudaMemcpyHostToDevice, s->stream));
+  SHAHD_CUDA_TRY(cudaMemcpyAsync(s->d_pf_poff, h_pf_poff, sizeof(int) * n, cudaMemcpyHostToDevice, s->stream));
+  SHAHD_CUDA_TRY(cudaMemcpyAsync(s->d_slot, h_slot, sizeof(int) * n, cudaMemcpyHostToDevice, s->stream));
+  SHAHD_CUDA_TRY(cudaMemcpyAsync(s->d_ends, h_ends, sizeof(int) * n, cudaMemcpyHostToDevice, s->stream));
+  SHAHD_CUDA_TRY(cudaMemcpyAsync(s->d_starts, h_starts, sizeof(int) * n, cudaMemcpyHostToDevice, s->stream));
+  SHAHD_CUDA_TRY(cudaMemcpyAsync(s->d_full_len, h_full, sizeof(int) * n, cudaMemcpyHostToDevice, s->stream));
+  SHAHD_CUDA_TRY(cudaMemsetAsync(s->d_gen_count, 0, sizeof(int) * n, s->stream));
+
+  SHAHD_TRY(PrefillBySteps(s, s->d_pf_slot, s->d_pf_poff, d_prompt_packed, lens_desc, slots_desc));
+  GatherLastTokens<<<CeilDiv(n, 128), 128, 0, s->stream>>>(d_prompt_packed, s->d_ends, n, s->d_tok);
+  s->launches++;
+  // the decode loop: step k consumes the last context id (k = 0) or the id sampled at k-1
+  StepPlan p{n, s->d_slot, s->d_tok, nullptr, nullptr, true, nullptr, nullptr, s->d_tok, d_out, max_new, 0};
+  for (int k = 0; k < max_new; k++) {
+    // rows whose window is full rebuild it from their last C-1 ids first (CachedForward.ts:135-141)
+    std::vector<int> slide;
+    for (int i = 0; i < n; i++)
+      if (s->h_len[i] >= C) slide.push_back(i);
+    if (!slide.empty()) {
+      const int keep = C - 1;
+      const int ns = (int)slide.size();
+      SHAHD_CUDA_TRY(cudaStreamSynchronize(s->stream));  // staging rows 0, 1 and 6 are rewritten
+      int *h_rows = Staging(s, 6), *h_woff = Staging(s, 1);
+      for (int i = 0; i < ns; i++) {
+        h_rows[i] = slide[i];
+        h_woff[i] = i * keep;  // gather offsets into the window buffer
+        s->h_len[slide[i]] = 0;
       }
-      p.attended = 0;
-      for (int i = 0; i < n; i++) p.attended += s->h_len[i] + 1;
-      EnqueueStep(s, p, st);
-      for (int i = 0; i < n; i++) s->h_len[i] += 1;
-      rc = CheckLaunch("generate step");
+      SHAHD_CUDA_TRY(cudaMemcpyAsync(s->d_rows, h_rows, sizeof(int) * ns, cudaMemcpyHostToDevice, s->stream));
+      GatherWindow<<<ns, 128, 0, s->stream>>>(d_prompt_packed, s->d_starts, s->d_full_len, d_out, max_new, s->d_rows,
+                                              ns, k - 1, keep, s->d_window);
+      SetLengths<<<CeilDiv(ns, 128), 128, 0, s->stream>>>(s->d_seq_len, s->d_rows, ns, 0);
+      s->launches += 2;
+      SHAHD_CUDA_TRY(cudaMemcpyAsync(s->d_pf_poff, h_woff, sizeof(int) * ns, cudaMemcpyHostToDevice, s->stream));
+      SHAHD_CUDA_TRY(cudaMemcpyAsync(s->d_pf_slot, h_rows, sizeof(int) * ns, cudaMemcpyHostToDevice, s->stream));
+      std::vector<int> lens(ns, keep);
+      SHAHD_TRY(PrefillBySteps(s, s->d_pf_slot, s->d_pf_poff, s->d_window, lens, slide));
     }
+    p.attended = 0;
+    for (int i = 0; i < n; i++) p.attended += s->h_len[i] + 1;
+    SHAHD_TRY(RunStep(s, p, 1));
+    for (int i = 0; i < n; i++) s->h_len[i] += 1;
   }
-  s->stream = saved;
-  return rc;
+  return CheckLaunch("generate");
+}
+
+// Join a caller stream: our stream waits for work already queued on `caller`, and at exit the caller
+// waits for ours.
+void JoinIn(ShahdSession* s, cudaStream_t caller) {
+  if (caller == s->stream) return;
+  cudaEventRecord(s->join_in, caller);
+  cudaStreamWaitEvent(s->stream, s->join_in, 0);
+}
+void JoinOut(ShahdSession* s, cudaStream_t caller) {
+  if (caller == s->stream) return;
+  cudaEventRecord(s->join_out, s->stream);
+  cudaStreamWaitEvent(caller, s->join_out, 0);
 }
 
 }  // namespace
@@ -540,6 +614,10 @@ extern "C" int shahd_session_create(const ShahdModelCfg* cfg, const void* params
     SetError("shahd_session_create: query group %d exceeds %d", cfg->num_heads / cfg->kv_heads, kMaxGroup);
     return SHAHD_EINVAL;
   }
+  if ((size_t)16 * RoundUp(std::max(cfg->embed_dim, cfg->mlp_hidden), 8) * 4 > 224 * 1024) {
+    SetError("shahd_session_create: EmbedDim/MlpHidden above 3584 are not supported by the row kernels");
+    return SHAHD_EINVAL;
+  }
   int ndev = 0;
   if (cudaGetDeviceCount(&ndev) != cudaSuccess || opts->device < 0 || opts->device >= ndev) {
     SetError("shahd_session_create: CUDA device %d not available", opts->device);
@@ -569,10 +647,11 @@ extern "C" int shahd_session_create(const ShahdModelCfg* cfg, const void* params
     shahd_session_destroy(s);
     return rc;
   };
-  if (cudaStreamCreateWithFlags(&s->stream, cudaStreamNonBlocking) != cudaSuccess) {
-    SetError("cudaStreamCreate failed");
-    delete s;
-    return SHAHD_ECUDA;
+  if (cudaStreamCreateWithFlags(&s->stream, cudaStreamNonBlocking) != cudaSuccess ||
+      cudaEventCreateWithFlags(&s->join_in, cudaEventDisableTiming) != cudaSuccess ||
+      cudaEventCreateWithFlags(&s->join_out, cudaEventDisableTiming) != cudaSuccess) {
+    SetError("cudaStreamCreate/cudaEventCreate failed");
+    return fail(SHAHD_ECUDA);
   }
 
   // ---- weights: repack on the host, one copy each ----
@@ -601,17 +680,17 @@ extern "C" int shahd_session_create(const ShahdModelCfg* cfg, const void* params
     if (rc == SHAHD_OK) rc = up_bf(hl.w_o, &Ly.w_o);
     if (rc == SHAHD_OK) rc = up_bf(hl.w_up, &Ly.w_up);
     if (rc == SHAHD_OK) rc = up_bf(hl.w_down, &Ly.w_down);
-    if (rc == SHAHD_OK) rc = up_f(hl.ln1_g, &Ly.ln1_g);
-    if (rc == SHAHD_OK) rc = up_f(hl.ln1_b, &Ly.ln1_b);
-    if (rc == SHAHD_OK) rc = up_f(hl.ln2_g, &Ly.ln2_g);
-    if (rc == SHAHD_OK) rc = up_f(hl.ln2_b, &Ly.ln2_b);
+    if (rc == SHAHD_OK) rc = up_f(hl.qkv_c1, &Ly.qkv_c1);
+    if (rc == SHAHD_OK) rc = up_f(hl.qkv_c2, &Ly.qkv_c2);
+    if (rc == SHAHD_OK) rc = up_f(hl.up_c1, &Ly.up_c1);
+    if (rc == SHAHD_OK) rc = up_f(hl.up_c2, &Ly.up_c2);
     if (rc == SHAHD_OK) rc = up_f(hl.b_fc, &Ly.b_fc);
     if (rc == SHAHD_OK) rc = up_f(hl.b_proj, &Ly.b_proj);
   }
   if (rc == SHAHD_OK) rc = up_bf(hw.w_head, &s->w_head);
   if (rc == SHAHD_OK) rc = up_f(hw.head_bias, &s->head_bias);
-  if (rc == SHAHD_OK) rc = up_f(hw.lnf_g, &s->lnf_g);
-  if (rc == SHAHD_OK) rc = up_f(hw.lnf_b, &s->lnf_b);
+  if (rc == SHAHD_OK) rc = up_f(hw.head_c1, &s->head_c1);
+  if (rc == SHAHD_OK) rc = up_f(hw.head_c2, &s->head_c2);
   if (rc == SHAHD_OK) rc = up_f(hw.wte, &s->wte);
   if (rc == SHAHD_OK) rc = up_f(hw.wpe, &s->wpe);
   if (rc == SHAHD_OK) rc = up_f(hw.rope_cos, &s->rope_cos);
@@ -624,7 +703,7 @@ extern "C" int shahd_session_create(const ShahdModelCfg* cfg, const void* params
   if ((rc = DevAlloc(s, &s->d_block_table, (size_t)R * s->max_blocks)) != SHAHD_OK) return fail(rc);
   if ((rc = DevAlloc(s, &s->d_seq_len, (size_t)R)) != SHAHD_OK) return fail(rc);
   if (cudaMallocHost(&s->h_block_table, sizeof(int) * (size_t)R * s->max_blocks) != cudaSuccess ||
-      cudaMallocHost(&s->h_pinned_rows, sizeof(int) * (size_t)R * 8) != cudaSuccess) {
+      cudaMallocHost(&s->h_pinned_rows, sizeof(int) * (size_t)R * kStagingRows) != cudaSuccess) {
     SetError("cudaMallocHost failed");
     return fail(SHAHD_ENOMEM);
   }
@@ -632,15 +711,17 @@ extern "C" int shahd_session_create(const ShahdModelCfg* cfg, const void* params
   s->free_pages.resize(s->kv_pages);
   for (int i = 0; i < s->kv_pages; i++) s->free_pages[i] = s->kv_pages - 1 - i;
   s->h_len.assign(R, 0);
-  cudaMemset(s->d_seq_len, 0, sizeof(int) * R);
 
   // ---- per-row scratch ----
   s->am_stride = std::max(CeilDiv(s->V, kSimtCols), UmmaGridN(s->V));
   const size_t hd = (size_t)s->H * d;
   if ((rc = DevAlloc(s, &s->x, (size_t)R * s->E)) != SHAHD_OK ||
+      (rc = DevAlloc(s, &s->xb, (size_t)R * s->Ep)) != SHAHD_OK ||
       (rc = DevAlloc(s, &s->q, (size_t)R * hd)) != SHAHD_OK ||
       (rc = DevAlloc(s, &s->ctx, (size_t)R * hd)) != SHAHD_OK ||
+      (rc = DevAlloc(s, &s->ctxb, (size_t)R * s->HDp)) != SHAHD_OK ||
       (rc = DevAlloc(s, &s->act, (size_t)R * s->F)) != SHAHD_OK ||
+      (rc = DevAlloc(s, &s->actb, (size_t)R * s->Fp)) != SHAHD_OK ||
       (rc = DevAlloc(s, &s->logits, (size_t)R * s->V)) != SHAHD_OK ||
       (rc = DevAlloc(s, &s->am_val, (size_t)R * s->am_stride)) != SHAHD_OK ||
       (rc = DevAlloc(s, &s->am_idx, (size_t)R * s->am_stride)) != SHAHD_OK ||
@@ -651,16 +732,20 @@ extern "C" int shahd_session_create(const ShahdModelCfg* cfg, const void* params
       (rc = DevAlloc(s, &s->d_slot, (size_t)R)) != SHAHD_OK || (rc = DevAlloc(s, &s->d_tok, (size_t)R)) != SHAHD_OK ||
       (rc = DevAlloc(s, &s->d_pos, (size_t)R)) != SHAHD_OK || (rc = DevAlloc(s, &s->d_next, (size_t)R)) != SHAHD_OK ||
       (rc = DevAlloc(s, &s->d_gen_count, (size_t)R)) != SHAHD_OK ||
-      (rc = DevAlloc(s, &s->d_poff, (size_t)R)) != SHAHD_OK ||
+      (rc = DevAlloc(s, &s->d_ends, (size_t)R)) != SHAHD_OK ||
+      (rc = DevAlloc(s, &s->d_starts, (size_t)R)) != SHAHD_OK ||
+      (rc = DevAlloc(s, &s->d_full_len, (size_t)R)) != SHAHD_OK ||
+      (rc = DevAlloc(s, &s->d_rows, (size_t)R)) != SHAHD_OK ||
       (rc = DevAlloc(s, &s->d_pf_slot, (size_t)R)) != SHAHD_OK ||
       (rc = DevAlloc(s, &s->d_pf_poff, (size_t)R)) != SHAHD_OK ||
       (rc = DevAlloc(s, &s->d_window, (size_t)R * s->C)) != SHAHD_OK)
     return fail(rc);
+  // bf16 operand rows are read over their padded width: padding columns must stay zero
+  cudaMemset(s->xb, 0, sizeof(bf16) * (size_t)R * s->Ep);
+  cudaMemset(s->ctxb, 0, sizeof(bf16) * (size_t)R * s->HDp);
+  cudaMemset(s->actb, 0, sizeof(bf16) * (size_t)R * s->Fp);
   cudaMemset(s->attn_counter, 0, sizeof(int) * (size_t)R * s->Hk);
-  s->d_prompt = nullptr;
-  s->prompt_cap = 0;
-  s->d_out = nullptr;
-  s->out_cap = 0;
+  cudaMemset(s->d_seq_len, 0, sizeof(int) * R);
   if (cudaDeviceSynchronize() != cudaSuccess) {
     SetError("shahd_session_create: device error during setup");
     return fail(SHAHD_ECUDA);
@@ -673,11 +758,14 @@ extern "C" int shahd_session_destroy(ShahdSession* s) {
   if (!s) return SHAHD_OK;
   cudaSetDevice(s->device);
   if (s->stream) cudaStreamSynchronize(s->stream);
-  for (auto& kv : s->graphs) cudaGraphExecDestroy(kv.second);
+  for (auto& kv : s->graphs)
+    if (kv.second.exec) cudaGraphExecDestroy(kv.second.exec);
   for (cudaEvent_t e : s->ev_pool) cudaEventDestroy(e);
   for (void* p : s->allocs) cudaFree(p);
   if (s->h_block_table) cudaFreeHost(s->h_block_table);
   if (s->h_pinned_rows) cudaFreeHost(s->h_pinned_rows);
+  if (s->join_in) cudaEventDestroy(s->join_in);
+  if (s->join_out) cudaEventDestroy(s->join_out);
   if (s->stream) cudaStreamDestroy(s->stream);
   delete s;
   return SHAHD_OK;
@@ -695,7 +783,9 @@ extern "C" int shahd_reset(ShahdSession* s, const int32_t* slots, int32_t n) {
   SHAHD_CUDA_TRY(cudaStreamSynchronize(s->stream));
   for (int i = 0; i < n; i++) ResetSlot(s, slots[i]);
   SHAHD_TRY(UploadTables(s));
-  return UploadLengths(s);
+  SHAHD_TRY(UploadLengths(s));
+  SHAHD_CUDA_TRY(cudaStreamSynchronize(s->stream));
+  return SHAHD_OK;
 }
 
 extern "C" int32_t shahd_seq_length(ShahdSession* s, int32_t slot) {
@@ -717,13 +807,9 @@ extern "C" int shahd_prefill(ShahdSession* s, const int32_t* slots, const int32_
   std::lock_guard<std::mutex> g(s->mu);
   cudaSetDevice(s->device);
   SHAHD_TRY(ValidateSlots(s, slots, n, "shahd_prefill"));
-  if (n > s->max_seqs) {
-    SetError("shahd_prefill: %d slots exceed max_seqs %d", n, s->max_seqs);
-    return SHAHD_EINVAL;
-  }
   size_t total = 0;
   for (int i = 0; i < n; i++) {
-    int len = offsets[i + 1] - offsets[i];
+    const int len = offsets[i + 1] - offsets[i];
     if (offsets[i] < 0 || len < 0) {
       SetError("shahd_prefill: offsets must be non-decreasing from 0");
       return SHAHD_EINVAL;
@@ -741,23 +827,28 @@ extern "C" int shahd_prefill(ShahdSession* s, const int32_t* slots, const int32_
   SHAHD_TRY(ValidateIds(s, ids, total, "PrefillCache"));
   SHAHD_CUDA_TRY(cudaStreamSynchronize(s->stream));
   for (int i = 0; i < n; i++) ResetSlot(s, slots[i]);
-  SHAHD_TRY(UploadLengths(s));
-  if (total == 0) return UploadTables(s);
-  SHAHD_TRY(GrowPrompt(s, total));
-  SHAHD_CUDA_TRY(cudaMemcpy(s->d_prompt, ids, sizeof(int) * total, cudaMemcpyHostToDevice));
   std::vector<int> order(n);
   std::iota(order.begin(), order.end(), 0);
   std::stable_sort(order.begin(), order.end(),
                    [&](int a, int b) { return offsets[a + 1] - offsets[a] > offsets[b + 1] - offsets[b]; });
-  std::vector<int> lens(n), sl(n), po(n);
+  std::vector<int> lens(n), sl(n);
+  int *h_sl = Staging(s, 0), *h_po = Staging(s, 1);
   for (int i = 0; i < n; i++) {
     lens[i] = offsets[order[i] + 1] - offsets[order[i]];
     sl[i] = slots[order[i]];
-    po[i] = offsets[order[i]];
+    h_sl[i] = sl[i];
+    h_po[i] = offsets[order[i]];
+    SHAHD_TRY(EnsurePages(s, sl[i], lens[i]));
   }
-  SHAHD_CUDA_TRY(cudaMemcpy(s->d_pf_slot, sl.data(), sizeof(int) * n, cudaMemcpyHostToDevice));
-  SHAHD_CUDA_TRY(cudaMemcpy(s->d_pf_poff, po.data(), sizeof(int) * n, cudaMemcpyHostToDevice));
-  SHAHD_TRY(PrefillBySteps(s, s->d_pf_slot, s->d_pf_poff, s->d_prompt, lens, sl));
+  SHAHD_TRY(UploadTables(s));
+  SHAHD_TRY(UploadLengths(s));
+  if (total > 0) {
+    SHAHD_TRY(GrowPrompt(s, total));
+    SHAHD_CUDA_TRY(cudaMemcpyAsync(s->d_prompt, ids, sizeof(int) * total, cudaMemcpyHostToDevice, s->stream));
+    SHAHD_CUDA_TRY(cudaMemcpyAsync(s->d_pf_slot, h_sl, sizeof(int) * n, cudaMemcpyHostToDevice, s->stream));
+    SHAHD_CUDA_TRY(cudaMemcpyAsync(s->d_pf_poff, h_po, sizeof(int) * n, cudaMemcpyHostToDevice, s->stream));
+    SHAHD_TRY(PrefillBySteps(s, s->d_pf_slot, s->d_pf_poff, s->d_prompt, lens, sl));
+  }
   SHAHD_CUDA_TRY(cudaStreamSynchronize(s->stream));
   return SHAHD_OK;
 }
@@ -786,14 +877,18 @@ extern "C" int shahd_step(ShahdSession* s, const int32_t* slots, const int32_t* 
   SHAHD_CUDA_TRY(cudaStreamSynchronize(s->stream));
   for (int i = 0; i < n; i++) SHAHD_TRY(EnsurePages(s, slots[i], s->h_len[slots[i]] + 1));
   SHAHD_TRY(UploadTables(s));
-  SHAHD_CUDA_TRY(cudaMemcpy(s->d_slot, slots, sizeof(int) * n, cudaMemcpyHostToDevice));
-  SHAHD_CUDA_TRY(cudaMemcpy(s->d_tok, tokens, sizeof(int) * n, cudaMemcpyHostToDevice));
+  int *h_sl = Staging(s, 0), *h_tk = Staging(s, 1);
+  std::copy(slots, slots + n, h_sl);
+  std::copy(tokens, tokens + n, h_tk);
+  SHAHD_CUDA_TRY(cudaMemcpyAsync(s->d_slot, h_sl, sizeof(int) * n, cudaMemcpyHostToDevice, s->stream));
+  SHAHD_CUDA_TRY(cudaMemcpyAsync(s->d_tok, h_tk, sizeof(int) * n, cudaMemcpyHostToDevice, s->stream));
   StepPlan p{n, s->d_slot, s->d_tok, nullptr, nullptr, true, logits ? s->logits : nullptr, s->d_next, nullptr, nullptr, 0, 0};
   for (int i = 0; i < n; i++) p.attended += s->h_len[slots[i]] + 1;
   EnqueueStep(s, p, s->stream);
   SHAHD_TRY(CheckLaunch("shahd_step"));
   for (int i = 0; i < n; i++) s->h_len[slots[i]] += 1;
-  if (logits) SHAHD_CUDA_TRY(cudaMemcpyAsync(logits, s->logits, sizeof(float) * (size_t)n * s->V, cudaMemcpyDeviceToHost, s->stream));
+  if (logits)
+    SHAHD_CUDA_TRY(cudaMemcpyAsync(logits, s->logits, sizeof(float) * (size_t)n * s->V, cudaMemcpyDeviceToHost, s->stream));
   if (next_ids) SHAHD_CUDA_TRY(cudaMemcpyAsync(next_ids, s->d_next, sizeof(int) * n, cudaMemcpyDeviceToHost, s->stream));
   SHAHD_CUDA_TRY(cudaStreamSynchronize(s->stream));
   return SHAHD_OK;
@@ -834,11 +929,11 @@ extern "C" int shahd_generate(ShahdSession* s, const int32_t* prompts, const int
   SHAHD_TRY(ValidateIds(s, prompts, total, "CachedGenerate"));
   if (max_new == 0) return SHAHD_OK;  // CachedGenerate returns the prompt untouched, no prefill
   std::vector<int> offs(offsets, offsets + n + 1);
+  SHAHD_CUDA_TRY(cudaStreamSynchronize(s->stream));
   SHAHD_TRY(GrowPrompt(s, total));
   SHAHD_TRY(GrowOut(s, (size_t)n * max_new));
-  SHAHD_CUDA_TRY(cudaMemcpy(s->d_prompt, prompts, sizeof(int) * total, cudaMemcpyHostToDevice));
-  int rc = GenerateCore(s, s->d_prompt, offs, n, max_new, opts, s->d_out, s->stream);
-  if (rc != SHAHD_OK) return rc;
+  SHAHD_CUDA_TRY(cudaMemcpyAsync(s->d_prompt, prompts, sizeof(int) * total, cudaMemcpyHostToDevice, s->stream));
+  SHAHD_TRY(GenerateCore(s, s->d_prompt, offs, n, max_new, opts, s->d_out));
   SHAHD_CUDA_TRY(cudaMemcpyAsync(out_ids, s->d_out, sizeof(int) * (size_t)n * max_new, cudaMemcpyDeviceToHost, s->stream));
   SHAHD_CUDA_TRY(cudaStreamSynchronize(s->stream));
   (void)rng_states;
@@ -858,9 +953,12 @@ extern "C" int shahd_generate_device(ShahdSession* s, const int32_t* d_prompts, 
   SHAHD_TRY(ValidateGenerate(s, host_offsets, n, max_new));
   if (max_new == 0) return SHAHD_OK;
   std::vector<int> offs(host_offsets, host_offsets + n + 1);
-  cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : s->stream;
+  cudaStream_t caller = stream ? static_cast<cudaStream_t>(stream) : s->stream;
   (void)d_rng_states;
-  return GenerateCore(s, d_prompts, offs, n, max_new, opts, d_out_ids, st);
+  JoinIn(s, caller);
+  const int rc = GenerateCore(s, d_prompts, offs, n, max_new, opts, d_out_ids);
+  JoinOut(s, caller);
+  return rc;
 }
 
 extern "C" int shahd_sync(ShahdSession* s) {
@@ -874,9 +972,8 @@ extern "C" int shahd_sync(ShahdSession* s) {
 
 extern "C" int32_t shahd_step_launches(ShahdSession* s, int32_t n) {
   if (!s) return -1;
-  // embed + per layer (QKV, attention, O, up, down) + head + finish
   (void)n;
-  return 1 + 5 * s->L + 2;
+  return 1 + 5 * s->L + 2;  // embed + per layer (QKV, attention, O, up, down) + head + finish
 }
 
 extern "C" int shahd_profile(ShahdSession* s, int32_t enable) {

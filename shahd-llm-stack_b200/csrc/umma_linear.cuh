@@ -23,8 +23,6 @@
 
 namespace shahd {
 
-constexpr uint32_t kWaitLimit = 1u << 22;
-
 constexpr int kUmmaBM = 128;
 constexpr int kUmmaBK = 64;
 constexpr int kUmmaStages = 4;
@@ -41,14 +39,14 @@ __host__ inline int UmmaBN(int M, int N) {
 }
 __host__ inline int UmmaGridN(int N) { return CeilDiv(N, 32); }  // upper bound of N tiles (BN >= 32)
 
-inline bool UmmaLinearSupported(const LinearArgs& la) { return la.Kp % 8 == 0 && la.N >= 1; }
+inline bool UmmaLinearSupported(const LinearArgs& la) { return la.Kp % 8 == 0 && la.N >= 1 && la.ab != nullptr; }
 
 template <int BN>
 struct UmmaSmem {
   static constexpr int kA = kUmmaBM * kUmmaBK * 2;  // 16 KB
   static constexpr int kB = BN * kUmmaBK * 2;
   static constexpr int kStage = kA + kB;
-  static constexpr int kBytes = kUmmaStages * kStage + 1024 /*align*/ + 256 /*barriers*/ + 2 * kUmmaBM * 4;
+  static constexpr int kBytes = kUmmaStages * kStage + 1024 /*align*/ + 256 /*barriers*/;
 };
 
 // ---- host: TMA descriptor for a bf16 row-major [rows, cols] matrix, box [box_rows, 64] ------------
@@ -118,31 +116,32 @@ inline void ForgetTmaRange(const void* lo, const void* hi) { (void)lo; (void)hi;
 
 template <int NORM, class Epi, int BN>
 __global__ void __launch_bounds__(kUmmaThreads, 1)
-    LinearUmmaKernel(LinearArgs la, Epi epi, const __grid_constant__ CUtensorMap tmap_w) {
+    LinearUmmaKernel(LinearArgs la, Epi epi, const __grid_constant__ CUtensorMap tmap_a,
+                     const __grid_constant__ CUtensorMap tmap_w) {
   using L = UmmaSmem<BN>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* full_b = reinterpret_cast<uint64_t*>(smem + kUmmaStages * L::kStage);
-  uint64_t* mma_done = full_b + kUmmaStages;
-  uint64_t* final_bar = mma_done + kUmmaStages;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kUmmaStages * L::kStage);
+  uint64_t* empty = full + kUmmaStages;
+  uint64_t* final_bar = empty + kUmmaStages;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(final_bar + 1);
-  int* s_abort = reinterpret_cast<int*>(tmem_slot + 1);
-  float* s_mu = reinterpret_cast<float*>(smem + kUmmaStages * L::kStage + 256);
-  float* s_is = s_mu + kUmmaBM;
+  volatile int* s_abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n0 = blockIdx.x * BN;
   const int m0 = blockIdx.y * kUmmaBM;
   const int rows = min(kUmmaBM, la.M - m0);
+  const int nk = CeilDiv(la.Kp, kUmmaBK);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kUmmaStages; s++) {
-      MbarInit(&full_b[s], 1);
-      MbarInit(&mma_done[s], 1);
+      MbarInit(&full[s], 1);
+      MbarInit(&empty[s], 1);
     }
     MbarInit(final_bar, 1);
     *s_abort = 0;
     FenceMbarInit();
+    PrefetchTmaDesc(&tmap_a);
     PrefetchTmaDesc(&tmap_w);
   }
   __syncwarp();
@@ -150,124 +149,89 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
     TmemAlloc(tmem_slot, BN);
     TmemRelinquish();
   }
-  // Row statistics of the norm (one warp per 32 rows).
-  if (NORM != kNormNone) {
-    for (int r = warp * 32; r < warp * 32 + 32; r++) {
-      if (r >= rows) break;
-      const float* src = la.a + (size_t)(m0 + r) * la.lda;
-      float mu = 0.f, is;
-      if (NORM == kNormRms) {
-        float ss = 0.f;
-        for (int k = lane; k < la.K; k += 32) ss += src[k] * src[k];
-        ss = WarpSum(ss);
-        is = 1.0f / sqrtf(ss / la.K + la.eps);
-      } else {
-        float s = 0.f;
-        for (int k = lane; k < la.K; k += 32) s += src[k];
-        mu = WarpSum(s) / la.K;
-        float v = 0.f;
-        for (int k = lane; k < la.K; k += 32) {
-          float t = src[k] - mu;
-          v += t * t;
-        }
-        v = WarpSum(v) / la.K;
-        is = 1.0f / sqrtf(v + la.eps);
-      }
-      if (lane == 0) {
-        s_mu[r] = mu;
-        s_is[r] = is;
-      }
-    }
-  }
   TcgenFenceBefore();
   __syncthreads();
   TcgenFenceAfter();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t idesc = UmmaIdescBf16(kUmmaBM, BN);
-  const int nk = CeilDiv(la.Kp, kUmmaBK);
 
-  for (int kb = 0; kb < nk; kb++) {
-    const int st = kb % kUmmaStages;
-    uint8_t* sa = smem + st * L::kStage;
-    uint8_t* sb = sa + L::kA;
-    if (kb >= kUmmaStages) {
-      // the MMAs that read this stage kUmmaStages iterations ago must be done before it is refilled
-      if (!MbarWaitBounded(&mma_done[st], ((kb / kUmmaStages) - 1) & 1, kWaitLimit)) {
-        if (lane == 0) atomicCAS(&g_shahd_device_error, 0, kDevErrUmmaTimeout);
-        *s_abort = 1;
-      }
-    }
-    __syncthreads();
-    if (*s_abort) break;
-    if (threadIdx.x == 0) {
-      MbarArriveExpectTx(&full_b[st], L::kB);
-      TmaLoad2D(sb, &tmap_w, &full_b[st], kb * kUmmaBK, n0);
-    }
-    // A tile: 128 rows x 64 k, fp32 -> (norm) -> bf16, two rows per warp instruction (16 lanes x 4 k).
-    const int k0 = kb * kUmmaBK;
-    const int half = lane >> 4, kl = (lane & 15) * 4;
-    for (int rr = warp * 32; rr < warp * 32 + 32; rr += 2) {
-      const int r = rr + half;
-      const int k = k0 + kl;
-      float v[4] = {0.f, 0.f, 0.f, 0.f};
-      if (r < rows) {
-        const float* src = la.a + (size_t)(m0 + r) * la.lda;
-        if (k + 3 < la.K && (la.lda & 3) == 0) {
-          const float4 t = *reinterpret_cast<const float4*>(src + k);
-          v[0] = t.x; v[1] = t.y; v[2] = t.z; v[3] = t.w;
-        } else {
-#pragma unroll
-          for (int j = 0; j < 4; j++)
-            if (k + j < la.K) v[j] = src[k + j];
-        }
-        if (NORM != kNormNone) {
-          const float mu = s_mu[r], is = s_is[r];
-#pragma unroll
-          for (int j = 0; j < 4; j++) {
-            if (k + j < la.K) {
-              if (NORM == kNormRms) v[j] = la.gamma[k + j] * v[j] * is;
-              else v[j] = la.gamma[k + j] * ((v[j] - mu) * is) + la.beta[k + j];
-            }
-          }
-        }
-      }
-      __nv_bfloat162 p0 = __floats2bfloat162_rn(v[0], v[1]);
-      __nv_bfloat162 p1 = __floats2bfloat162_rn(v[2], v[3]);
-      uint2 pk;
-      pk.x = *reinterpret_cast<uint32_t*>(&p0);
-      pk.y = *reinterpret_cast<uint32_t*>(&p1);
-      const int chunk = kl >> 3, sub = (kl & 7) * 2;  // 16-byte chunk and byte offset inside it
-      *reinterpret_cast<uint2*>(sa + Sw128Offset(r, chunk) + sub) = pk;
-    }
-    FenceProxyAsyncShared();
-    __syncthreads();
-    if (threadIdx.x == 0) {
-      if (!MbarWaitBounded(&full_b[st], (kb / kUmmaStages) & 1, kWaitLimit)) {
-        atomicCAS(&g_shahd_device_error, 0, kDevErrUmmaTimeout);
-        *s_abort = 1;
-      } else {
-        TcgenFenceAfter();
-        const uint64_t ad = SmemDescSw128(SmemAddr(sa));
-        const uint64_t bd = SmemDescSw128(SmemAddr(sb));
-#pragma unroll
-        for (int kk = 0; kk < kUmmaBK / 16; kk++)
-          UmmaBf16(tmem, ad + (uint64_t)(kk * 2), bd + (uint64_t)(kk * 2), idesc, (kb > 0 || kk > 0) ? 1u : 0u);
-        UmmaCommit(&mma_done[st]);
-      }
+  // producer prologue: fill the pipeline
+  if (threadIdx.x == 0) {
+    for (int kb = 0; kb < nk && kb < kUmmaStages; kb++) {
+      uint8_t* sa = smem + kb * L::kStage;
+      MbarArriveExpectTx(&full[kb], L::kStage);
+      TmaLoad2D(sa, &tmap_a, &full[kb], kb * kUmmaBK, m0);
+      TmaLoad2D(sa + L::kA, &tmap_w, &full[kb], kb * kUmmaBK, n0);
     }
   }
+
+  // row statistics of the norm from the bf16 rows the MMA consumes (thread = row), overlapping the loads
+  const int r = warp * 32 + lane;
+  float mu = 0.f, is = 1.f;
+  if (NORM != kNormNone && r < rows) {
+    const bf16* src = la.ab + (size_t)(m0 + r) * la.ldab;
+    float s1 = 0.f, s2 = 0.f;
+#pragma unroll 8
+    for (int k = 0; k < la.K; k += 8) {
+      float f[8];
+      Bf16x8ToFloat(LoadNc16(src + k), f);
+#pragma unroll
+      for (int j = 0; j < 8; j++) {
+        const float v = (k + j < la.K) ? f[j] : 0.f;
+        s1 += v;
+        s2 += v * v;
+      }
+    }
+    if (NORM == kNormRms) {
+      is = 1.0f / sqrtf(s2 / la.K + la.eps);
+    } else {
+      mu = s1 / la.K;
+      const float var = fmaxf(s2 / la.K - mu * mu, 0.f);
+      is = 1.0f / sqrtf(var + la.eps);
+    }
+  }
+
+  // MMA issue (one thread): consume stage kb, then refill it with kb + kUmmaStages
+  if (threadIdx.x == 0) {
+    const uint32_t idesc = UmmaIdescBf16(kUmmaBM, BN);
+    for (int kb = 0; kb < nk; kb++) {
+      const int st = kb % kUmmaStages;
+      const uint32_t ph = (kb / kUmmaStages) & 1;
+      if (!MbarWaitBounded(&full[st], ph, kWaitLimit)) {
+        atomicCAS(&g_shahd_device_error, 0, kDevErrUmmaTimeout);
+        *s_abort = 1;
+        break;
+      }
+      TcgenFenceAfter();
+      uint8_t* sa = smem + st * L::kStage;
+      const uint64_t ad = SmemDescSw128(SmemAddr(sa));
+      const uint64_t bd = SmemDescSw128(SmemAddr(sa + L::kA));
+#pragma unroll
+      for (int kk = 0; kk < kUmmaBK / 16; kk++)
+        UmmaBf16(tmem, ad + (uint64_t)(kk * 2), bd + (uint64_t)(kk * 2), idesc, (kb > 0 || kk > 0) ? 1u : 0u);
+      UmmaCommit(&empty[st]);
+      if (kb + kUmmaStages < nk) {
+        if (!MbarWaitBounded(&empty[st], ph, kWaitLimit)) {
+          atomicCAS(&g_shahd_device_error, 0, kDevErrUmmaTimeout);
+          *s_abort = 1;
+          break;
+        }
+        const int kn = kb + kUmmaStages;
+        MbarArriveExpectTx(&full[st], L::kStage);
+        TmaLoad2D(sa, &tmap_a, &full[st], kn * kUmmaBK, m0);
+        TmaLoad2D(sa + L::kA, &tmap_w, &full[st], kn * kUmmaBK, n0);
+      }
+    }
+    if (!*s_abort) UmmaCommit(final_bar);
+  }
   __syncthreads();
-  const bool ok = *s_abort == 0;
-  if (ok && threadIdx.x == 0) UmmaCommit(final_bar);
-  if (ok && !MbarWaitBounded(final_bar, 0, kWaitLimit)) {
+  if (!*s_abort && !MbarWaitBounded(final_bar, 0, kWaitLimit)) {
     if (lane == 0) atomicCAS(&g_shahd_device_error, 0, kDevErrUmmaTimeout);
     *s_abort = 1;
   }
   __syncthreads();
   TcgenFenceAfter();
-  if (*s_abort == 0) {
+  if (!*s_abort) {
     // Epilogue: thread = row (m0 + 32*warp + lane), 16 consecutive accumulator columns per TMEM load.
-    const int r = warp * 32 + lane;
     const bool row_ok = r < rows;
     float bv = -INFINITY;
     int bi = 0x7fffffff;
@@ -282,6 +246,13 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
           const int n = n0 + c + j;
           if (n < la.N) {
             float v0 = __uint_as_float(u[j]), v1 = __uint_as_float(u[j + 1]);
+            if (NORM == kNormRms) {
+              v0 *= is;
+              v1 *= is;
+            } else if (NORM == kNormLayer) {
+              v0 = is * (v0 - mu * la.c1[n]) + la.c2[n];
+              if (n + 1 < la.N) v1 = is * (v1 - mu * la.c1[n + 1]) + la.c2[n + 1];
+            }
             epi.apply(m0 + r, n, v0, v1, la.N);
             if constexpr (IsLogits<Epi>::value) {
               ArgmaxMerge(bv, bi, v0, n);
@@ -306,8 +277,9 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
 
 template <int NORM, class Epi, int BN>
 void LaunchUmmaLinearBN(const LinearArgs& la, const Epi& epi, cudaStream_t st) {
-  CUtensorMap tm;
-  if (!MakeTmaBf16(la.w, la.N, la.Kp, la.Kp, BN, &tm)) return;  // launch error surfaces via CheckLaunch
+  CUtensorMap tw, ta;
+  if (!MakeTmaBf16(la.w, la.N, la.Kp, la.Kp, BN, &tw) || !MakeTmaBf16(la.ab, la.a_rows, la.Kp, la.ldab, kUmmaBM, &ta))
+    return;  // the missing launch surfaces through the caller's result checks
   static bool configured = false;
   if (!configured) {
     cudaFuncSetAttribute(LinearUmmaKernel<NORM, Epi, BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -315,7 +287,7 @@ void LaunchUmmaLinearBN(const LinearArgs& la, const Epi& epi, cudaStream_t st) {
     configured = true;
   }
   dim3 grid(CeilDiv(la.N, BN), CeilDiv(la.M, kUmmaBM));
-  LinearUmmaKernel<NORM, Epi, BN><<<grid, kUmmaThreads, UmmaSmem<BN>::kBytes, st>>>(la, epi, tm);
+  LinearUmmaKernel<NORM, Epi, BN><<<grid, kUmmaThreads, UmmaSmem<BN>::kBytes, st>>>(la, epi, ta, tw);
 }
 
 template <int NORM, class Epi>
