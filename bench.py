@@ -311,12 +311,18 @@ def main() -> None:
     ap.add_argument("--workload", default="microchat", choices=sorted(pkg.configs.WORKLOADS))
     ap.add_argument("--no-extras", action="store_true",
                     help="time the steps only (no e2e, profile or CPU legs): the profiling command line")
+    ap.add_argument("--new-tokens", type=int, default=None,
+                    help="override the workload's new tokens per sequence (small ncu captures only)")
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     if args.warmup < 3:
         args.warmup = 3
+    if args.new_tokens is not None:
+        import dataclasses
+        w = pkg.configs.WORKLOADS[args.workload]
+        pkg.configs.WORKLOADS[args.workload] = dataclasses.replace(w, new_tokens=args.new_tokens)
     if args.impl == "reference":
         run_reference(args, rank, world)
     else:

@@ -28,6 +28,26 @@ void ClearError();
 
 using bf16 = __nv_bfloat16;
 
+// Kernel launches of a decode step use programmatic dependent launch: the next kernel is scheduled while
+// its predecessor drains and runs its independent prologue (barrier init, TMEM allocation, weight loads)
+// before GridDepWait(). Process-wide switch, on by default.
+extern bool g_use_pdl;
+
+template <typename... KArgs, typename... Args>
+inline void LaunchPdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = g_use_pdl ? 1 : 0;
+  cudaLaunchKernelEx(&cfg, kern, args...);
+}
+
 __host__ __device__ inline int CeilDiv(int a, int b) { return (a + b - 1) / b; }
 __host__ __device__ inline int RoundUp(int a, int b) { return CeilDiv(a, b) * b; }
 
@@ -70,6 +90,13 @@ __device__ __forceinline__ void ArgmaxMerge(float& bv, int& bi, float v, int i) 
     bi = i;
   }
 }
+
+// ---- programmatic dependent launch ---------------------------------------------------------------
+// Wait until every prerequisite grid has completed and its memory is visible (a no-op when the kernel
+// was launched without the programmatic-serialization attribute).
+__device__ __forceinline__ void GridDepWait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+// Allow the dependent grid to be scheduled; it still waits for this grid's completion in GridDepWait.
+__device__ __forceinline__ void GridDepLaunch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
 // ---- shared-memory address, mbarrier, TMA, tcgen05 (inline PTX, sm_100a) -------------------------
 

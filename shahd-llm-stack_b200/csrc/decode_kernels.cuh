@@ -269,6 +269,8 @@ __global__ void __launch_bounds__(kSimtWarps * 32) LinearSimtKernel(LinearArgs l
   __shared__ int s_am_i[kSimtWarps][MT];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int m0 = blockIdx.y * MT;
+  GridDepWait();
+  GridDepLaunch();
   StageRowsNormalized<MT, NORM>(la, sA, m0);
   __syncthreads();
 
@@ -340,6 +342,7 @@ __global__ void __launch_bounds__(kSimtWarps * 32) LinearSimtKernel(LinearArgs l
 // ---- embedding: x = Wte[token] (+ Wpe[pos]) (AdvanceOneToken, CachedForward.ts:48-53) ---------------
 
 struct EmbedArgs {
+  const int* pos_in;    // [M] explicit positions (batched prefill rows), or nullptr: the slot's length
   const int* slot;      // [M]
   const int* tok;       // direct tokens [M] (when poff == nullptr)
   const int* prompt;    // packed prompt ids (prefill gather)
@@ -354,8 +357,10 @@ struct EmbedArgs {
 };
 
 __global__ void EmbedKernel(EmbedArgs e) {
+  GridDepWait();
+  GridDepLaunch();
   const int r = blockIdx.x;
-  const int p = e.seq_len[e.slot[r]];
+  const int p = e.pos_in ? e.pos_in[r] : e.seq_len[e.slot[r]];
   const int tok = e.poff ? e.prompt[e.poff[r] + p] : e.tok[r];
   if (threadIdx.x == 0) e.pos[r] = p;
   const float* src = e.wte + (size_t)tok * e.E;
@@ -370,11 +375,13 @@ __global__ void EmbedKernel(EmbedArgs e) {
 }
 
 // ---- decode attention over the paged cache (AttendRow, CachedRowMath.ts:60-86) ---------------------
-// Grid (chunk, kv head, row). Each CTA takes one 64-position page of one KV head for one row: one thread
-// copies the page's K and V blocks into shared memory with two bulk async copies, the CTA scores them
-// against the head's whole query group (GQA: heads g*G .. g*G+G-1 share the page) and writes a partial
-// (o, max, sum). The last CTA of a (row, kv head) to finish — counted with an atomic — merges the partials
-// in chunk order; with a single chunk the CTA writes the context directly.
+// Grid (split, kv head, row). Row m attends over positions 0..pos[m] of its slot. Each CTA streams the
+// pages of its split [c * pages / nsplit, (c + 1) * pages / nsplit) through a ring of shared-memory
+// buffers filled by bulk async copies (one thread issues the K and V block copies of a page), scores each
+// page against the head's whole query group (GQA: heads g*G .. g*G+G-1 share it) and keeps an online
+// softmax (running max and sum, rescaled output). One split writes the context directly; with several
+// splits each writes a partial (o, max, sum) and the last split of a (row, kv head) to finish — counted
+// with an atomic — merges them in split order.
 
 struct AttnArgs {
   const float* q;   // [M, H*d] post-RoPE
@@ -387,7 +394,7 @@ struct AttnArgs {
   const int* slot;
   int H, Hk, G, d;
   float scale;
-  int max_chunks;
+  int max_chunks;   // partial stride (>= gridDim.x)
   float* part_o;    // [M, H, max_chunks, d]
   float* part_m;    // [M, H, max_chunks]
   float* part_l;
@@ -397,22 +404,24 @@ struct AttnArgs {
 constexpr int kAttnThreads = 128;
 constexpr int kAttnWarps = kAttnThreads / 32;
 constexpr int kMaxGroup = 8;
+constexpr int kAttnRing = 3;  // page buffers in flight per CTA
 
 __device__ __forceinline__ void StoreCtx(const AttnArgs& aa, int m, int col, float v) {
   aa.ctx[(size_t)m * aa.H * aa.d + col] = v;
   aa.ctxb[(size_t)m * aa.ldcb + col] = __float2bfloat16_rn(v);
 }
 
-__device__ __forceinline__ void AttnMerge(const AttnArgs& aa, int m, int g, int nch) {
+__device__ __forceinline__ void AttnMerge(const AttnArgs& aa, int m, int g, int nsplit) {
   for (int e = threadIdx.x; e < aa.G * aa.d; e += blockDim.x) {
     const int i = e / aa.d, j = e % aa.d;
     const int h = g * aa.G + i;
     const size_t base = ((size_t)m * aa.H + h) * aa.max_chunks;
     float mx = -INFINITY;
-    for (int c = 0; c < nch; c++) mx = fmaxf(mx, __ldcg(aa.part_m + base + c));
+    for (int c = 0; c < nsplit; c++) mx = fmaxf(mx, __ldcg(aa.part_m + base + c));
     float num = 0.f, den = 0.f;
-    for (int c = 0; c < nch; c++) {
-      const float w = __expf(__ldcg(aa.part_m + base + c) - mx);
+    for (int c = 0; c < nsplit; c++) {
+      const float pm = __ldcg(aa.part_m + base + c);
+      const float w = pm == -INFINITY ? 0.f : __expf(pm - mx);
       num += w * __ldcg(aa.part_o + (base + c) * aa.d + j);
       den += w * __ldcg(aa.part_l + base + c);
     }
@@ -420,10 +429,12 @@ __device__ __forceinline__ void AttnMerge(const AttnArgs& aa, int m, int g, int 
   }
 }
 
-// Writes this CTA's per-head results; merges when it is the last chunk of its (row, kv head).
-__device__ __forceinline__ void AttnFinishChunk(const AttnArgs& aa, int m, int g, int c, int nch, const float* so,
-                                                const float* sm, const float* sl) {
-  if (nch == 1) {
+// Writes this CTA's per-head results (so = unnormalized output [G*d], sm/sl = running max/sum); merges
+// when it is the last split of its (row, kv head).
+__device__ __forceinline__ void AttnFinishSplit(const AttnArgs& aa, int m, int g, const float* so, const float* sm,
+                                                const float* sl) {
+  const int c = blockIdx.x, nsplit = gridDim.x;
+  if (nsplit == 1) {
     for (int e = threadIdx.x; e < aa.G * aa.d; e += blockDim.x) {
       const int i = e / aa.d, j = e % aa.d;
       StoreCtx(aa, m, (g * aa.G + i) * aa.d + j, so[e] / sl[i]);
@@ -444,12 +455,12 @@ __device__ __forceinline__ void AttnFinishChunk(const AttnArgs& aa, int m, int g
   __shared__ int s_last;
   if (threadIdx.x == 0) {
     const int prev = atomicAdd(aa.counter + m * aa.Hk + g, 1);
-    s_last = (prev == nch - 1);
+    s_last = (prev == nsplit - 1);
   }
   __syncthreads();
   if (s_last) {
     __threadfence();
-    AttnMerge(aa, m, g, nch);
+    AttnMerge(aa, m, g, nsplit);
     if (threadIdx.x == 0) aa.counter[m * aa.Hk + g] = 0;
   }
 }
@@ -462,122 +473,159 @@ __device__ __forceinline__ void BulkCopyG2S(void* dst, const void* src, uint32_t
                : "memory");
 }
 
-// Fast path: head_dim D (multiple of 8, 32..128) known at compile time.
+__host__ __device__ constexpr int AttnSmemBytes(int D) { return kAttnRing * 2 * kPageTokens * D * 2; }
+
+// Fast path: head_dim D (multiple of 8, 32..128) known at compile time. Dynamic shared memory holds the
+// ring of K|V page buffers.
 template <int D>
 __global__ void __launch_bounds__(kAttnThreads) AttnDecodeKernel(AttnArgs aa) {
   constexpr int LPP = D / 8;    // lanes per position (16 B of K each)
   constexpr int PPW = 32 / LPP; // positions per warp pass
   constexpr int JPL = D / 32;   // output dims per lane
-  __shared__ __align__(128) bf16 sk[kPageTokens * D];  // reused for the per-warp partial outputs
-  __shared__ __align__(128) bf16 sv[kPageTokens * D];
-  __shared__ __align__(8) uint64_t bar;
+  constexpr int PAGE = kPageTokens * D;  // elements of one K (or V) page
+  extern __shared__ __align__(128) uint8_t attn_smem[];
+  bf16* ring = reinterpret_cast<bf16*>(attn_smem);  // [kAttnRing][K page | V page]
+  __shared__ __align__(8) uint64_t bar[kAttnRing];
   __shared__ float sq[kMaxGroup][D];
   __shared__ float ss[kMaxGroup][kPageTokens];
   __shared__ float so[kMaxGroup * D];
-  __shared__ float sm[kMaxGroup], sl[kMaxGroup];
-  static_assert(kAttnWarps * kMaxGroup * D * 4 <= kPageTokens * D * 2, "partials must fit in the K buffer");
-  const int c = blockIdx.x, g = blockIdx.y, m = blockIdx.z;
+  __shared__ float s_m[kMaxGroup], s_l[kMaxGroup], s_scale[kMaxGroup];
+  __shared__ int s_fail;
+  static_assert(kAttnWarps * kMaxGroup * D * 4 <= kAttnRing * 2 * PAGE * 2, "partials must fit in the ring");
+  GridDepWait();
+  GridDepLaunch();
+  const int g = blockIdx.y, m = blockIdx.z;
   const int p = aa.pos[m];
-  const int nch = (p + kPageTokens) / kPageTokens;  // positions 0..p
-  if (c >= nch) return;
-  const int t0 = c * kPageTokens;
-  const int tn = min(kPageTokens, p + 1 - t0);
+  const int pages = (p + kPageTokens) / kPageTokens;  // positions 0..p
+  const int pb = (int)((long long)blockIdx.x * pages / gridDim.x);
+  const int pe = (int)((long long)(blockIdx.x + 1) * pages / gridDim.x);
   const int G = aa.G;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int hd = aa.H * D;
   const int slot = aa.slot[m];
-  const bf16* kb = aa.kv.Block(slot, c, aa.layer, g, 0);
-  const bf16* vb = aa.kv.Block(slot, c, aa.layer, g, 1);
-  int tv = kb ? tn : 0;  // a missing page (recorded as an error) contributes no positions
 
   if (threadIdx.x == 0) {
-    MbarInit(&bar, 1);
+    for (int b = 0; b < kAttnRing; b++) MbarInit(&bar[b], 1);
     FenceMbarInit();
-  }
-  __syncthreads();
-  if (threadIdx.x == 0 && tv > 0) {
-    const uint32_t bytes = (uint32_t)tv * D * 2;
-    MbarArriveExpectTx(&bar, 2 * bytes);
-    BulkCopyG2S(sk, kb, bytes, &bar);
-    BulkCopyG2S(sv, vb, bytes, &bar);
+    s_fail = 0;
   }
   for (int e = threadIdx.x; e < G * D; e += blockDim.x) sq[e / D][e % D] = aa.q[(size_t)m * hd + g * G * D + e];
-  if (tv > 0 && !MbarWaitBounded(&bar, 0, kWaitLimit)) {
-    atomicCAS(&g_shahd_device_error, 0, kDevErrAttnTimeout);
-    tv = 0;
+  if (threadIdx.x < kMaxGroup) {
+    s_m[threadIdx.x] = -INFINITY;
+    s_l[threadIdx.x] = 0.f;
   }
   __syncthreads();
+  // Positions held by page `pg` (0 when its block is missing: the miss is recorded as an error).
+  auto page_len = [&](int pg) { return min(kPageTokens, p + 1 - pg * kPageTokens); };
+  auto issue = [&](int pg, int b) {
+    const bf16* kb = aa.kv.Block(slot, pg, aa.layer, g, 0);
+    const bf16* vb = aa.kv.Block(slot, pg, aa.layer, g, 1);
+    if (kb == nullptr) {
+      MbarArrive(&bar[b]);  // complete the phase with no data
+      return;
+    }
+    const uint32_t bytes = (uint32_t)page_len(pg) * D * 2;
+    MbarArriveExpectTx(&bar[b], 2 * bytes);
+    BulkCopyG2S(ring + (size_t)b * 2 * PAGE, kb, bytes, &bar[b]);
+    BulkCopyG2S(ring + (size_t)b * 2 * PAGE + PAGE, vb, bytes, &bar[b]);
+  };
+  if (threadIdx.x == 0)
+    for (int pg = pb; pg < pe && pg < pb + kAttnRing; pg++) issue(pg, (pg - pb) % kAttnRing);
 
-  // scores s[i][t] = (q_i · k_t) * scale
-  const int seg = lane % LPP;
-#pragma unroll
-  for (int tb = warp * PPW; tb < kPageTokens; tb += kAttnWarps * PPW) {
-    const int t = tb + lane / LPP;
-    float kf[8];
-    if (t < tv) {
-      const uint4 u = *reinterpret_cast<const uint4*>(sk + t * D + seg * 8);
-      Bf16x8ToFloat(u, kf);
-    } else {
-#pragma unroll
-      for (int j = 0; j < 8; j++) kf[j] = 0.f;
-    }
-    for (int i = 0; i < G; i++) {
-      float part = 0.f;
-#pragma unroll
-      for (int j = 0; j < 8; j++) part = fmaf(kf[j], sq[i][seg * 8 + j], part);
-#pragma unroll
-      for (int o = LPP / 2; o > 0; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
-      if (seg == 0 && t < tv) ss[i][t] = part * aa.scale;
-    }
-  }
-  __syncthreads();
-
-  // per-head max and exp-sum over this chunk
-  for (int i = warp; i < G; i += kAttnWarps) {
-    float mx = -INFINITY;
-    for (int t = lane; t < tv; t += 32) mx = fmaxf(mx, ss[i][t]);
-    mx = WarpMax(mx);
-    float sum = 0.f;
-    for (int t = lane; t < tv; t += 32) {
-      const float e = __expf(ss[i][t] - mx);
-      ss[i][t] = e;
-      sum += e;
-    }
-    sum = WarpSum(sum);
-    if (lane == 0) {
-      sm[i] = mx;
-      sl[i] = sum;
-    }
-  }
-  __syncthreads();
-
-  // o[i][j] = sum_t e[i][t] * v_t[j]; warps split t, lanes split j
   float o[kMaxGroup][JPL];
 #pragma unroll
   for (int i = 0; i < kMaxGroup; i++)
 #pragma unroll
     for (int jj = 0; jj < JPL; jj++) o[i][jj] = 0.f;
-#pragma unroll 4
-  for (int t = warp; t < tv; t += kAttnWarps) {
-    float vf[JPL];
-    if constexpr (JPL == 2) {
-      const float2 v2 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(sv + t * D + lane * 2));
-      vf[0] = v2.x;
-      vf[1] = v2.y;
-    } else {
-#pragma unroll
-      for (int jj = 0; jj < JPL; jj++) vf[jj] = __bfloat162float(sv[t * D + lane * JPL + jj]);
+  const int seg = lane % LPP;
+  for (int pg = pb; pg < pe; pg++) {
+    const int it = pg - pb, b = it % kAttnRing;
+    const bool present = aa.kv.block_table[slot * aa.kv.max_blocks + pg] >= 0;
+    if (!MbarWaitBounded(&bar[b], (it / kAttnRing) & 1, kWaitLimit)) {
+      atomicCAS(&g_shahd_device_error, 0, kDevErrAttnTimeout);
+      s_fail = 1;
     }
+    __syncthreads();
+    if (s_fail) break;  // uniform: read after the barrier
+    const int tv = present ? page_len(pg) : 0;
+    const bf16* sk = ring + (size_t)b * 2 * PAGE;
+    const bf16* sv = sk + PAGE;
+    // scores s[i][t] = (q_i · k_t) * scale
 #pragma unroll
-    for (int i = 0; i < kMaxGroup; i++) {
-      if (i < G) {
-        const float e = ss[i][t];
+    for (int tb = warp * PPW; tb < kPageTokens; tb += kAttnWarps * PPW) {
+      const int t = tb + lane / LPP;
+      float kf[8];
+      if (t < tv) {
+        Bf16x8ToFloat(*reinterpret_cast<const uint4*>(sk + t * D + seg * 8), kf);
+      } else {
 #pragma unroll
-        for (int jj = 0; jj < JPL; jj++) o[i][jj] = fmaf(e, vf[jj], o[i][jj]);
+        for (int j = 0; j < 8; j++) kf[j] = 0.f;
+      }
+      for (int i = 0; i < G; i++) {
+        float part = 0.f;
+#pragma unroll
+        for (int j = 0; j < 8; j++) part = fmaf(kf[j], sq[i][seg * 8 + j], part);
+#pragma unroll
+        for (int off = LPP / 2; off > 0; off >>= 1) part += __shfl_xor_sync(0xffffffffu, part, off);
+        if (seg == 0 && t < tv) ss[i][t] = part * aa.scale;
       }
     }
+    __syncthreads();
+    // online softmax update per head
+    for (int i = warp; i < G; i += kAttnWarps) {
+      float pm = -INFINITY;
+      for (int t = lane; t < tv; t += 32) pm = fmaxf(pm, ss[i][t]);
+      pm = WarpMax(pm);
+      const float old = s_m[i];
+      const float nm = fmaxf(old, pm);
+      float sum = 0.f;
+      for (int t = lane; t < tv; t += 32) {
+        const float e = __expf(ss[i][t] - nm);
+        ss[i][t] = e;
+        sum += e;
+      }
+      sum = WarpSum(sum);
+      if (lane == 0) {
+        const float sc = old == -INFINITY ? 0.f : __expf(old - nm);
+        s_scale[i] = sc;
+        s_l[i] = s_l[i] * sc + sum;
+        s_m[i] = nm;
+      }
+    }
+    __syncthreads();
+    // o = o * scale + sum_t e[i][t] * v_t; warps split t, lanes split j
+#pragma unroll
+    for (int i = 0; i < kMaxGroup; i++)
+      if (i < G) {
+        const float sc = s_scale[i];
+#pragma unroll
+        for (int jj = 0; jj < JPL; jj++) o[i][jj] *= sc;
+      }
+#pragma unroll 4
+    for (int t = warp; t < tv; t += kAttnWarps) {
+      float vf[JPL];
+      if constexpr (JPL == 2) {
+        const float2 v2 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(sv + t * D + lane * 2));
+        vf[0] = v2.x;
+        vf[1] = v2.y;
+      } else {
+#pragma unroll
+        for (int jj = 0; jj < JPL; jj++) vf[jj] = __bfloat162float(sv[t * D + lane * JPL + jj]);
+      }
+#pragma unroll
+      for (int i = 0; i < kMaxGroup; i++) {
+        if (i < G) {
+          const float e = ss[i][t];
+#pragma unroll
+          for (int jj = 0; jj < JPL; jj++) o[i][jj] = fmaf(e, vf[jj], o[i][jj]);
+        }
+      }
+    }
+    __syncthreads();  // buffer b and ss are free again
+    if (threadIdx.x == 0 && pg + kAttnRing < pe) issue(pg + kAttnRing, b);
   }
-  float* so_part = reinterpret_cast<float*>(sk);  // K is no longer read: [warps][G*D]
+  // combine the warps' partial outputs (the ring is free now)
+  float* so_part = reinterpret_cast<float*>(ring);  // [warps][kMaxGroup * D]
 #pragma unroll
   for (int i = 0; i < kMaxGroup; i++)
     if (i < G)
@@ -585,67 +633,81 @@ __global__ void __launch_bounds__(kAttnThreads) AttnDecodeKernel(AttnArgs aa) {
       for (int jj = 0; jj < JPL; jj++) so_part[(warp * kMaxGroup + i) * D + lane * JPL + jj] = o[i][jj];
   __syncthreads();
   for (int e = threadIdx.x; e < G * D; e += blockDim.x) {
-    float s = 0.f;
+    float acc = 0.f;
 #pragma unroll
-    for (int w = 0; w < kAttnWarps; w++) s += so_part[w * kMaxGroup * D + e];
-    so[e] = s;
+    for (int w = 0; w < kAttnWarps; w++) acc += so_part[w * kMaxGroup * D + e];
+    so[e] = acc;
   }
   __syncthreads();
-  AttnFinishChunk(aa, m, g, c, nch, so, sm, sl);
+  AttnFinishSplit(aa, m, g, so, s_m, s_l);
 }
 
-// Any even head_dim up to 128 (the reference's small test shapes use d = 4, 8, 16): scalar loops.
+// Any even head_dim up to 128 (the reference's small test shapes use d = 4, 8, 16): scalar loops over
+// global memory, one split per (row, kv head), online softmax over the pages.
 constexpr int kMaxHeadDimGeneric = 128;
 __global__ void __launch_bounds__(kAttnThreads) AttnDecodeGenericKernel(AttnArgs aa) {
   __shared__ float sq[kMaxGroup * kMaxHeadDimGeneric];
   __shared__ float ss[kMaxGroup][kPageTokens];
   __shared__ float so[kMaxGroup * kMaxHeadDimGeneric];
-  __shared__ float sm[kMaxGroup], sl[kMaxGroup];
-  const int c = blockIdx.x, g = blockIdx.y, m = blockIdx.z;
+  __shared__ float s_m[kMaxGroup], s_l[kMaxGroup], s_scale[kMaxGroup];
+  GridDepWait();
+  GridDepLaunch();
+  const int g = blockIdx.y, m = blockIdx.z;
   const int p = aa.pos[m];
-  const int nch = (p + kPageTokens) / kPageTokens;
-  if (c >= nch) return;
-  const int t0 = c * kPageTokens;
-  const int tn = min(kPageTokens, p + 1 - t0);
+  const int pages = (p + kPageTokens) / kPageTokens;
+  const int pb = (int)((long long)blockIdx.x * pages / gridDim.x);
+  const int pe = (int)((long long)(blockIdx.x + 1) * pages / gridDim.x);
   const int G = aa.G, D = aa.d;
   const int hd = aa.H * D;
   const int slot = aa.slot[m];
-  const bf16* kb = aa.kv.Block(slot, c, aa.layer, g, 0);
-  const bf16* vb = aa.kv.Block(slot, c, aa.layer, g, 1);
-  const int tv = kb ? tn : 0;
-  for (int e = threadIdx.x; e < G * D; e += blockDim.x) sq[e] = aa.q[(size_t)m * hd + g * G * D + e];
-  __syncthreads();
-  for (int e = threadIdx.x; e < G * kPageTokens; e += blockDim.x) {
-    const int i = e / kPageTokens, t = e % kPageTokens;
-    if (t < tv) {
-      float dot = 0.f;
-      for (int j = 0; j < D; j++) dot = fmaf(sq[i * D + j], __bfloat162float(kb[(size_t)t * D + j]), dot);
-      ss[i][t] = dot * aa.scale;
-    }
-  }
-  __syncthreads();
-  if (threadIdx.x < G) {
-    const int i = threadIdx.x;
-    float mx = -INFINITY;
-    for (int t = 0; t < tv; t++) mx = fmaxf(mx, ss[i][t]);
-    float sum = 0.f;
-    for (int t = 0; t < tv; t++) {
-      const float e = __expf(ss[i][t] - mx);
-      ss[i][t] = e;
-      sum += e;
-    }
-    sm[i] = mx;
-    sl[i] = sum;
-  }
-  __syncthreads();
   for (int e = threadIdx.x; e < G * D; e += blockDim.x) {
-    const int i = e / D, j = e % D;
-    float acc = 0.f;
-    for (int t = 0; t < tv; t++) acc = fmaf(ss[i][t], __bfloat162float(vb[(size_t)t * D + j]), acc);
-    so[e] = acc;
+    sq[e] = aa.q[(size_t)m * hd + g * G * D + e];
+    so[e] = 0.f;
+  }
+  if (threadIdx.x < kMaxGroup) {
+    s_m[threadIdx.x] = -INFINITY;
+    s_l[threadIdx.x] = 0.f;
   }
   __syncthreads();
-  AttnFinishChunk(aa, m, g, c, nch, so, sm, sl);
+  for (int pg = pb; pg < pe; pg++) {
+    const bf16* kb = aa.kv.Block(slot, pg, aa.layer, g, 0);
+    const bf16* vb = aa.kv.Block(slot, pg, aa.layer, g, 1);
+    const int tv = kb ? min(kPageTokens, p + 1 - pg * kPageTokens) : 0;
+    for (int e = threadIdx.x; e < G * kPageTokens; e += blockDim.x) {
+      const int i = e / kPageTokens, t = e % kPageTokens;
+      if (t < tv) {
+        float dot = 0.f;
+        for (int j = 0; j < D; j++) dot = fmaf(sq[i * D + j], __bfloat162float(kb[(size_t)t * D + j]), dot);
+        ss[i][t] = dot * aa.scale;
+      }
+    }
+    __syncthreads();
+    if (threadIdx.x < G) {
+      const int i = threadIdx.x;
+      float pm = -INFINITY;
+      for (int t = 0; t < tv; t++) pm = fmaxf(pm, ss[i][t]);
+      const float old = s_m[i], nm = fmaxf(old, pm);
+      float sum = 0.f;
+      for (int t = 0; t < tv; t++) {
+        const float e = __expf(ss[i][t] - nm);
+        ss[i][t] = e;
+        sum += e;
+      }
+      const float sc = old == -INFINITY ? 0.f : __expf(old - nm);
+      s_scale[i] = sc;
+      s_l[i] = s_l[i] * sc + sum;
+      s_m[i] = nm;
+    }
+    __syncthreads();
+    for (int e = threadIdx.x; e < G * D; e += blockDim.x) {
+      const int i = e / D, j = e % D;
+      float acc = so[e] * s_scale[i];
+      for (int t = 0; t < tv; t++) acc = fmaf(ss[i][t], __bfloat162float(vb[(size_t)t * D + j]), acc);
+      so[e] = acc;
+    }
+    __syncthreads();
+  }
+  AttnFinishSplit(aa, m, g, so, s_m, s_l);
 }
 
 // ---- finish: positions advance; greedy argmax over the head's per-CTA partials -------------------------
@@ -667,9 +729,12 @@ struct FinishArgs {
 };
 
 __global__ void FinishKernel(FinishArgs f) {
-  const int r = blockIdx.x * blockDim.x + threadIdx.x;
+  GridDepWait();
+  GridDepLaunch();
+  const int r = blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
   if (r >= f.M) return;
-  f.seq_len[f.slot[r]] = f.pos[r] + 1;
+  if (lane == 0) f.seq_len[f.slot[r]] = f.pos[r] + 1;
   if (f.am_val == nullptr && f.sampled == nullptr) return;
   int id;
   if (f.sampled) {
@@ -677,9 +742,16 @@ __global__ void FinishKernel(FinishArgs f) {
   } else {
     float bv = -INFINITY;
     int bi = 0x7fffffff;
-    for (int b = 0; b < f.nblk; b++) ArgmaxMerge(bv, bi, f.am_val[(size_t)r * f.nblk + b], f.am_idx[(size_t)r * f.nblk + b]);
+    for (int b = lane; b < f.nblk; b += 32) ArgmaxMerge(bv, bi, f.am_val[(size_t)r * f.nblk + b], f.am_idx[(size_t)r * f.nblk + b]);
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, bv, off);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, off);
+      ArgmaxMerge(bv, bi, ov, oi);
+    }
     id = bi == 0x7fffffff ? 0 : bi;
   }
+  if (lane != 0) return;
   if (f.next_ids) f.next_ids[r] = id;
   if (f.cur_tok) f.cur_tok[r] = id;
   if (f.out_ids) {

@@ -12,6 +12,7 @@
 namespace shahd {
 
 int g_umma_min_rows = 17;
+bool g_use_pdl = true;
 
 // ---- thread-local last error --------------------------------------------------------------------
 static thread_local std::string t_error;
@@ -389,6 +390,8 @@ int ShahdGpuAvailable(void) { return DeviceOk(); }
 const char* ShahdLastError(void) { return GetError(); }
 
 void ShahdSetTensorCoreMinRows(int rows) { g_umma_min_rows = rows < 1 ? 1 : rows; }
+
+void ShahdSetProgrammaticLaunch(int enable) { g_use_pdl = enable != 0; }
 
 int ShahdDeviceErrorFlag(void) {
   int v = 0;

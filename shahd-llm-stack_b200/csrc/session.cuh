@@ -55,6 +55,8 @@ struct ShahdSession {
   int Nqkv, Nup;
   int device;
   int max_seqs;
+  int rows_cap;  // rows of the activation buffers: max(max_seqs, prefill chunk)
+  int num_sms;
   cudaStream_t stream = nullptr;
   cudaEvent_t join_in = nullptr, join_out = nullptr;
   std::mutex mu;
@@ -81,8 +83,9 @@ struct ShahdSession {
   int am_stride;
   float *part_o, *part_m, *part_l;
   int* attn_counter;
-  int *d_slot, *d_tok, *d_pos, *d_next, *d_gen_count, *d_ends, *d_pf_slot, *d_pf_poff, *d_starts, *d_full_len,
-      *d_rows;
+  int *d_slot, *d_tok, *d_pos, *d_next, *d_gen_count, *d_ends, *d_starts, *d_full_len, *d_rows;
+  int *d_seq_plan;                              // [4][max_seqs]: prefill slot, context start, length, row offset
+  int *d_row_slot, *d_row_pos, *d_row_poff;     // [rows_cap] expanded prefill rows
   int* d_prompt = nullptr;
   size_t prompt_cap = 0;
   int* d_window;
@@ -109,7 +112,11 @@ namespace shahd {
 
 namespace {
 
-constexpr int kStagingRows = 8;
+// Pinned staging rows (each max_seqs ints). A row is rewritten only after the stream has drained the
+// copies that read it: 0-1 per-call slots/tokens, 2-5 generate plan, 6 window-rebuild rows,
+// 7 lengths, 8-11 the prefill plan.
+constexpr int kStagingRows = 12;
+constexpr int kPrefillRows = 8192;  // rows of one batched prefill chunk (whole sequences per chunk)
 
 template <class T>
 int DevAlloc(ShahdSession* s, T** p, size_t count) {
@@ -142,7 +149,7 @@ void LaunchSimt(const LinearArgs& la, const Epi& epi, cudaStream_t st) {
     configured = true;
   }
   dim3 grid(CeilDiv(la.N, kSimtCols), CeilDiv(la.M, MT));
-  LinearSimtKernel<MT, NORM, Epi><<<grid, kSimtWarps * 32, smem, st>>>(la, epi);
+  LaunchPdl(LinearSimtKernel<MT, NORM, Epi>, grid, dim3(kSimtWarps * 32), smem, st, la, epi);
 }
 
 template <int NORM, class Epi>
@@ -179,6 +186,8 @@ int HeadBlocks(const ShahdSession* s, int M) {
 
 struct StepPlan {
   int M;
+  const int* pos_in; // device [M] explicit positions (batched prefill rows) or nullptr: the slots' lengths
+  bool finish;       // run the finish kernel (lengths advance, greedy id); off for batched prefill
   const int* slot;   // device [M]
   const int* tok;    // device [M] (direct tokens) or nullptr
   const int* poff;   // device [M] prompt gather offsets, or nullptr
@@ -233,12 +242,12 @@ LinearArgs Lin(const float* a, int lda, const bf16* ab, int ldab, int rows_cap, 
 // number of kernels it launched.
 int EnqueueStep(ShahdSession* s, const StepPlan& p, cudaStream_t st) {
   const long long before = s->launches;
-  const int M = p.M, R = s->max_seqs;
+  const int M = p.M, R = s->rows_cap;
   const int norm = s->cfg.norm_kind == 1 ? kNormRms : kNormLayer;
   const float eps = (float)s->cfg.layer_norm_eps;
   Timed(s, st, kProfOther, 8.0 * M * s->E, [&] {
-    EmbedArgs e{p.slot, p.tok, p.prompt, p.poff, s->d_seq_len, s->d_pos, s->wte, s->wpe, s->x, s->xb, s->E, s->Ep};
-    EmbedKernel<<<M, 128, 0, st>>>(e);
+    EmbedArgs e{p.pos_in, p.slot, p.tok, p.prompt, p.poff, s->d_seq_len, s->d_pos, s->wte, s->wpe, s->x, s->xb, s->E, s->Ep};
+    LaunchPdl(EmbedKernel, dim3(M), dim3(128), 0, st, e);
   });
   KvView kv{s->kv_pool, s->d_block_table, s->max_blocks, s->Hk, s->d, s->page_elems};
   const int hd = s->H * s->d;
@@ -253,12 +262,15 @@ int EnqueueStep(ShahdSession* s, const StepPlan& p, cudaStream_t st) {
     // attention over the cache (CachedForward.ts:76-80)
     AttnArgs aa{s->q, s->ctx, s->ctxb, s->HDp, kv, l, s->d_pos, p.slot, s->H, s->Hk, s->G, s->d,
                 (float)(1.0 / std::sqrt((double)s->d)), s->max_blocks, s->part_o, s->part_m, s->part_l, s->attn_counter};
-    dim3 ag(s->max_blocks, s->Hk, M);
+    // splits per (row, kv head): enough CTAs to fill the GPU; one split (no partials) beyond max_seqs rows
+    int nsplit = 1;
+    if (M <= s->max_seqs) nsplit = std::max(1, std::min(s->max_blocks, CeilDiv(3 * s->num_sms, M * s->Hk)));
+    dim3 ag(nsplit, s->Hk, M);
     Timed(s, st, kProfAttention, attn_bytes, [&] {
-      if (s->d == 64) AttnDecodeKernel<64><<<ag, kAttnThreads, 0, st>>>(aa);
-      else if (s->d == 32) AttnDecodeKernel<32><<<ag, kAttnThreads, 0, st>>>(aa);
-      else if (s->d == 128) AttnDecodeKernel<128><<<ag, kAttnThreads, 0, st>>>(aa);
-      else AttnDecodeGenericKernel<<<ag, kAttnThreads, 0, st>>>(aa);
+      if (s->d == 64) LaunchPdl(AttnDecodeKernel<64>, ag, dim3(kAttnThreads), AttnSmemBytes(64), st, aa);
+      else if (s->d == 32) LaunchPdl(AttnDecodeKernel<32>, ag, dim3(kAttnThreads), AttnSmemBytes(32), st, aa);
+      else if (s->d == 128) LaunchPdl(AttnDecodeKernel<128>, ag, dim3(kAttnThreads), AttnSmemBytes(128), st, aa);
+      else LaunchPdl(AttnDecodeGenericKernel, ag, dim3(kAttnThreads), 0, st, aa);
     });
     // summed per-head Wo + residual (CachedForward.ts:81-84)
     const LinearArgs lo = Lin(s->ctx, hd, s->ctxb, s->HDp, R, M, hd, s->HDp, Ly.w_o, s->E, eps, nullptr, nullptr);
@@ -283,9 +295,11 @@ int EnqueueStep(ShahdSession* s, const StepPlan& p, cudaStream_t st) {
     Timed(s, st, kProfLinear, LinearBytes(M, s->E, s->Ep, s->V),
           [&] { LaunchLinear(norm, lh, EpiLogits{p.logits, s->head_bias}, st); });
   }
-  FinishArgs f{M, p.slot, s->d_pos, s->d_seq_len, p.head ? s->am_val : nullptr, s->am_idx, nblk, p.next_ids,
-               p.cur_tok, p.out_ids, p.out_ld, s->d_gen_count, nullptr};
-  Timed(s, st, kProfOther, 16.0 * M, [&] { FinishKernel<<<CeilDiv(M, 128), 128, 0, st>>>(f); });
+  if (p.finish) {
+    FinishArgs f{M, p.slot, s->d_pos, s->d_seq_len, p.head ? s->am_val : nullptr, s->am_idx, nblk, p.next_ids,
+                 p.cur_tok, p.out_ids, p.out_ld, s->d_gen_count, nullptr};
+    Timed(s, st, kProfOther, 16.0 * M, [&] { LaunchPdl(FinishKernel, dim3(CeilDiv(M, 4)), dim3(128), 0, st, f); });
+  }
   return (int)(s->launches - before);
 }
 
@@ -306,7 +320,7 @@ int RunStep(ShahdSession* s, const StepPlan& p, int kind) {
     EnqueueStep(s, p, s->stream);
     return CheckLaunch("step");
   }
-  GraphKey key{kind, p.M, p.slot, p.tok, p.poff, p.prompt, p.out_ids, p.out_ld, g_umma_min_rows};
+  GraphKey key{kind, p.M, p.slot, p.tok, p.poff, p.prompt, p.out_ids, p.out_ld, g_umma_min_rows * 2 + (int)g_use_pdl};
   auto it = s->graphs.find(key);
   if (it == s->graphs.end()) {
     EnqueueStep(s, p, s->stream);
@@ -411,18 +425,65 @@ __global__ void SetLengths(int* seq_len, const int* slots, int n, int value) {
   if (i < n) seq_len[slots[i]] = value;
 }
 
-// Prefill rows (already reset, lengths 0, pages assigned) by cached steps over their contexts: row i of
-// the plan takes ids[poff_i + t] at step t while t < len_i. Rows are ordered by descending length.
-int PrefillBySteps(ShahdSession* s, const int* d_slots, const int* d_poff, const int* d_prompt,
-                   const std::vector<int>& lens_desc, const std::vector<int>& slots_desc) {
-  if (lens_desc.empty() || lens_desc[0] == 0) return SHAHD_OK;
-  for (int t = 0; t < lens_desc[0]; t++) {
-    int M = 0;
-    while (M < (int)lens_desc.size() && lens_desc[M] > t) M++;
-    StepPlan p{M, d_slots, nullptr, d_poff, d_prompt, false, nullptr, nullptr, nullptr, nullptr, 0, (long long)M * (t + 1)};
-    SHAHD_TRY(RunStep(s, p, 0));
+// Expands per-sequence prefill plans into rows: sequence i of [i0, i1) contributes rows
+// (row_off[i] - row_off[i0]) + t for t < len[i], each with its slot, position t and gather offset.
+__global__ void ExpandPrefillRows(const int* plan, int max_seqs, int i0, int i1, int* row_slot, int* row_pos,
+                                  int* row_poff) {
+  const int i = i0 + blockIdx.x;
+  if (i >= i1) return;
+  const int slot = plan[i], start = plan[max_seqs + i], len = plan[2 * max_seqs + i];
+  const int off = plan[3 * max_seqs + i] - plan[3 * max_seqs + i0];
+  for (int t = threadIdx.x; t < len; t += blockDim.x) {
+    row_slot[off + t] = slot;
+    row_pos[off + t] = t;
+    row_poff[off + t] = start;
   }
-  for (size_t i = 0; i < slots_desc.size(); i++) s->h_len[slots_desc[i]] = lens_desc[i];
+}
+
+// PrefillCache (CachedForward.ts:100-110) for several slots at once: every prompt position of every
+// sequence is one row of a batched blocks-only step (no LM head); QKV writes each row's K/V at its
+// position before the attention of the same step reads positions 0..t of the row's slot, which is the
+// causal mask of the reference's tensor forward. Sequences go in chunks of whole sequences of at most
+// rows_cap rows. Slots must be reset with pages assigned; ids of sequence i are d_prompt[start_i + t].
+int PrefillBatched(ShahdSession* s, const int* d_prompt, const std::vector<int>& slots, const std::vector<int>& starts,
+                   const std::vector<int>& lens) {
+  const int n = (int)slots.size(), R = s->max_seqs;
+  int* h = Staging(s, 8);  // rows 8..11: slot, start, len, row offset
+  long long off = 0;
+  for (int i = 0; i < n; i++) {
+    h[i] = slots[i];
+    h[R + i] = starts[i];
+    h[2 * R + i] = lens[i];
+    h[3 * R + i] = (int)off;
+    off += lens[i];
+  }
+  if (off > 0) {
+    SHAHD_CUDA_TRY(cudaMemcpyAsync(s->d_seq_plan, h, sizeof(int) * 4 * (size_t)R, cudaMemcpyHostToDevice, s->stream));
+    for (int i0 = 0; i0 < n;) {
+      int i1 = i0, rows = 0;
+      long long attended = 0;
+      while (i1 < n && rows + lens[i1] <= s->rows_cap) {
+        rows += lens[i1];
+        attended += (long long)lens[i1] * (lens[i1] + 1) / 2;
+        i1++;
+      }
+      if (i1 == i0) {  // a sequence longer than a chunk: rows_cap >= block_size rules this out
+        SetError("PrefillCache: %d tokens exceed the prefill chunk of %d rows", lens[i0], s->rows_cap);
+        return SHAHD_EINVAL;
+      }
+      if (rows > 0) {
+        ExpandPrefillRows<<<i1 - i0, 128, 0, s->stream>>>(s->d_seq_plan, R, i0, i1, s->d_row_slot, s->d_row_pos,
+                                                           s->d_row_poff);
+        s->launches++;
+        StepPlan p{rows, s->d_row_pos, false, s->d_row_slot, nullptr, s->d_row_poff, d_prompt, false, nullptr, nullptr,
+                   nullptr, nullptr, 0, attended};
+        SHAHD_TRY(RunStep(s, p, 0));
+      }
+      i0 = i1;
+    }
+  }
+  for (int i = 0; i < n; i++) s->h_len[slots[i]] = lens[i];
+  SHAHD_TRY(UploadLengths(s));
   return CheckLaunch("prefill");
 }
 
@@ -481,49 +542,38 @@ int GenerateCore(ShahdSession* s, const int* d_prompt_packed, const std::vector<
   }
   const int C = s->C;
   // CachedDecoder constructor: Context = prompt.slice(-BlockSize); prefill all but its last id.
-  std::vector<int> plen(n), pstart(n), full_len(n);
+  std::vector<int> plen(n), pstart(n), full_len(n), slots(n);
   for (int i = 0; i < n; i++) {
     full_len[i] = offs[i + 1] - offs[i];
     const int ctx = std::min(full_len[i], C);
     pstart[i] = offs[i + 1] - ctx;
     plen[i] = ctx - 1;
+    slots[i] = i;
   }
   SHAHD_CUDA_TRY(cudaStreamSynchronize(s->stream));  // pinned staging and tables are rewritten below
   for (int i = 0; i < n; i++) ResetSlot(s, i);
   // Pages for the whole run up front: positions reach min(plen + max_new, C).
   for (int i = 0; i < n; i++) SHAHD_TRY(EnsurePages(s, i, std::min(plen[i] + max_new, C)));
   SHAHD_TRY(UploadTables(s));
-  SHAHD_TRY(UploadLengths(s));
 
-  std::vector<int> order(n);
-  std::iota(order.begin(), order.end(), 0);
-  std::stable_sort(order.begin(), order.end(), [&](int a, int b) { return plen[a] > plen[b]; });
-  std::vector<int> lens_desc(n), slots_desc(n);
-  int *h_pf_slot = Staging(s, 0), *h_pf_poff = Staging(s, 1), *h_slot = Staging(s, 2), *h_ends = Staging(s, 3),
-      *h_starts = Staging(s, 4), *h_full = Staging(s, 5);
+  int *h_slot = Staging(s, 2), *h_ends = Staging(s, 3), *h_starts = Staging(s, 4), *h_full = Staging(s, 5);
   for (int i = 0; i < n; i++) {
-    h_pf_slot[i] = order[i];
-    h_pf_poff[i] = pstart[order[i]];
-    lens_desc[i] = plen[order[i]];
-    slots_desc[i] = order[i];
     h_slot[i] = i;
     h_ends[i] = offs[i + 1];
     h_starts[i] = offs[i];
     h_full[i] = full_len[i];
   }
-  SHAHD_CUDA_TRY(cudaMemcpyAsync(s->d_pf_slot, h_pf_slot, sizeof(int) * n, cudaMemcpyHostToDevice, s->stream));
-  SHAHD_CUDA_TRY(cudaMemcpyAsync(s->d_pf_poff, h_pf_poff, sizeof(int) * n, cudaMemcpyHostToDevice, s->stream));
   SHAHD_CUDA_TRY(cudaMemcpyAsync(s->d_slot, h_slot, sizeof(int) * n, cudaMemcpyHostToDevice, s->stream));
   SHAHD_CUDA_TRY(cudaMemcpyAsync(s->d_ends, h_ends, sizeof(int) * n, cudaMemcpyHostToDevice, s->stream));
   SHAHD_CUDA_TRY(cudaMemcpyAsync(s->d_starts, h_starts, sizeof(int) * n, cudaMemcpyHostToDevice, s->stream));
   SHAHD_CUDA_TRY(cudaMemcpyAsync(s->d_full_len, h_full, sizeof(int) * n, cudaMemcpyHostToDevice, s->stream));
   SHAHD_CUDA_TRY(cudaMemsetAsync(s->d_gen_count, 0, sizeof(int) * n, s->stream));
 
-  SHAHD_TRY(PrefillBySteps(s, s->d_pf_slot, s->d_pf_poff, d_prompt_packed, lens_desc, slots_desc));
+  SHAHD_TRY(PrefillBatched(s, d_prompt_packed, slots, pstart, plen));
   GatherLastTokens<<<CeilDiv(n, 128), 128, 0, s->stream>>>(d_prompt_packed, s->d_ends, n, s->d_tok);
   s->launches++;
   // the decode loop: step k consumes the last context id (k = 0) or the id sampled at k-1
-  StepPlan p{n, s->d_slot, s->d_tok, nullptr, nullptr, true, nullptr, nullptr, s->d_tok, d_out, max_new, 0};
+  StepPlan p{n, nullptr, true, s->d_slot, s->d_tok, nullptr, nullptr, true, nullptr, nullptr, s->d_tok, d_out, max_new, 0};
   for (int k = 0; k < max_new; k++) {
     // rows whose window is full rebuild it from their last C-1 ids first (CachedForward.ts:135-141)
     std::vector<int> slide;
@@ -532,22 +582,18 @@ int GenerateCore(ShahdSession* s, const int* d_prompt_packed, const std::vector<
     if (!slide.empty()) {
       const int keep = C - 1;
       const int ns = (int)slide.size();
-      SHAHD_CUDA_TRY(cudaStreamSynchronize(s->stream));  // staging rows 0, 1 and 6 are rewritten
-      int *h_rows = Staging(s, 6), *h_woff = Staging(s, 1);
+      SHAHD_CUDA_TRY(cudaStreamSynchronize(s->stream));  // staging rows 6, 7 and 8-11 are rewritten
+      int* h_rows = Staging(s, 6);
+      std::vector<int> wstart(ns), wlen(ns, keep);
       for (int i = 0; i < ns; i++) {
         h_rows[i] = slide[i];
-        h_woff[i] = i * keep;  // gather offsets into the window buffer
-        s->h_len[slide[i]] = 0;
+        wstart[i] = i * keep;  // gather offsets into the window buffer
       }
       SHAHD_CUDA_TRY(cudaMemcpyAsync(s->d_rows, h_rows, sizeof(int) * ns, cudaMemcpyHostToDevice, s->stream));
       GatherWindow<<<ns, 128, 0, s->stream>>>(d_prompt_packed, s->d_starts, s->d_full_len, d_out, max_new, s->d_rows,
                                               ns, k - 1, keep, s->d_window);
-      SetLengths<<<CeilDiv(ns, 128), 128, 0, s->stream>>>(s->d_seq_len, s->d_rows, ns, 0);
-      s->launches += 2;
-      SHAHD_CUDA_TRY(cudaMemcpyAsync(s->d_pf_poff, h_woff, sizeof(int) * ns, cudaMemcpyHostToDevice, s->stream));
-      SHAHD_CUDA_TRY(cudaMemcpyAsync(s->d_pf_slot, h_rows, sizeof(int) * ns, cudaMemcpyHostToDevice, s->stream));
-      std::vector<int> lens(ns, keep);
-      SHAHD_TRY(PrefillBySteps(s, s->d_pf_slot, s->d_pf_poff, s->d_window, lens, slide));
+      s->launches++;
+      SHAHD_TRY(PrefillBatched(s, s->d_window, slide, wstart, wlen));
     }
     p.attended = 0;
     for (int i = 0; i < n; i++) p.attended += s->h_len[i] + 1;
@@ -640,6 +686,8 @@ extern "C" int shahd_session_create(const ShahdModelCfg* cfg, const void* params
   s->Nup = cfg->mlp_kind == 0 ? s->F : 2 * s->F;
   s->device = opts->device;
   s->max_seqs = opts->max_seqs;
+  s->rows_cap = std::max(s->max_seqs, std::max(kPrefillRows, s->C));
+  cudaDeviceGetAttribute(&s->num_sms, cudaDevAttrMultiProcessorCount, opts->device);
   s->max_blocks = CeilDiv(s->C, kPageTokens);
   s->kv_pages = opts->kv_pages > 0 ? opts->kv_pages : s->max_seqs * s->max_blocks;
   s->page_elems = (size_t)s->L * s->Hk * 2 * kPageTokens * d;
@@ -713,15 +761,16 @@ extern "C" int shahd_session_create(const ShahdModelCfg* cfg, const void* params
   s->h_len.assign(R, 0);
 
   // ---- per-row scratch ----
-  s->am_stride = std::max(CeilDiv(s->V, kSimtCols), UmmaGridN(s->V));
+  s->am_stride = std::max(CeilDiv(s->V, kSimtCols), UmmaGridN(s->V));  // argmax partials per decode row
   const size_t hd = (size_t)s->H * d;
-  if ((rc = DevAlloc(s, &s->x, (size_t)R * s->E)) != SHAHD_OK ||
-      (rc = DevAlloc(s, &s->xb, (size_t)R * s->Ep)) != SHAHD_OK ||
-      (rc = DevAlloc(s, &s->q, (size_t)R * hd)) != SHAHD_OK ||
-      (rc = DevAlloc(s, &s->ctx, (size_t)R * hd)) != SHAHD_OK ||
-      (rc = DevAlloc(s, &s->ctxb, (size_t)R * s->HDp)) != SHAHD_OK ||
-      (rc = DevAlloc(s, &s->act, (size_t)R * s->F)) != SHAHD_OK ||
-      (rc = DevAlloc(s, &s->actb, (size_t)R * s->Fp)) != SHAHD_OK ||
+  const size_t RC = (size_t)s->rows_cap;  // activation rows (decode rows or one prefill chunk)
+  if ((rc = DevAlloc(s, &s->x, RC * s->E)) != SHAHD_OK ||
+      (rc = DevAlloc(s, &s->xb, RC * s->Ep)) != SHAHD_OK ||
+      (rc = DevAlloc(s, &s->q, RC * hd)) != SHAHD_OK ||
+      (rc = DevAlloc(s, &s->ctx, RC * hd)) != SHAHD_OK ||
+      (rc = DevAlloc(s, &s->ctxb, RC * s->HDp)) != SHAHD_OK ||
+      (rc = DevAlloc(s, &s->act, RC * s->F)) != SHAHD_OK ||
+      (rc = DevAlloc(s, &s->actb, RC * s->Fp)) != SHAHD_OK ||
       (rc = DevAlloc(s, &s->logits, (size_t)R * s->V)) != SHAHD_OK ||
       (rc = DevAlloc(s, &s->am_val, (size_t)R * s->am_stride)) != SHAHD_OK ||
       (rc = DevAlloc(s, &s->am_idx, (size_t)R * s->am_stride)) != SHAHD_OK ||
@@ -736,14 +785,19 @@ extern "C" int shahd_session_create(const ShahdModelCfg* cfg, const void* params
       (rc = DevAlloc(s, &s->d_starts, (size_t)R)) != SHAHD_OK ||
       (rc = DevAlloc(s, &s->d_full_len, (size_t)R)) != SHAHD_OK ||
       (rc = DevAlloc(s, &s->d_rows, (size_t)R)) != SHAHD_OK ||
-      (rc = DevAlloc(s, &s->d_pf_slot, (size_t)R)) != SHAHD_OK ||
-      (rc = DevAlloc(s, &s->d_pf_poff, (size_t)R)) != SHAHD_OK ||
+      (rc = DevAlloc(s, &s->d_seq_plan, (size_t)4 * R)) != SHAHD_OK ||
+      (rc = DevAlloc(s, &s->d_row_slot, (size_t)s->rows_cap)) != SHAHD_OK ||
+      (rc = DevAlloc(s, &s->d_row_pos, (size_t)s->rows_cap)) != SHAHD_OK ||
+      (rc = DevAlloc(s, &s->d_row_poff, (size_t)s->rows_cap)) != SHAHD_OK ||
       (rc = DevAlloc(s, &s->d_window, (size_t)R * s->C)) != SHAHD_OK)
     return fail(rc);
   // bf16 operand rows are read over their padded width: padding columns must stay zero
-  cudaMemset(s->xb, 0, sizeof(bf16) * (size_t)R * s->Ep);
-  cudaMemset(s->ctxb, 0, sizeof(bf16) * (size_t)R * s->HDp);
-  cudaMemset(s->actb, 0, sizeof(bf16) * (size_t)R * s->Fp);
+  cudaMemset(s->xb, 0, sizeof(bf16) * RC * s->Ep);
+  cudaMemset(s->ctxb, 0, sizeof(bf16) * RC * s->HDp);
+  cudaMemset(s->actb, 0, sizeof(bf16) * RC * s->Fp);
+  cudaFuncSetAttribute(AttnDecodeKernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, AttnSmemBytes(32));
+  cudaFuncSetAttribute(AttnDecodeKernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, AttnSmemBytes(64));
+  cudaFuncSetAttribute(AttnDecodeKernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, AttnSmemBytes(128));
   cudaMemset(s->attn_counter, 0, sizeof(int) * (size_t)R * s->Hk);
   cudaMemset(s->d_seq_len, 0, sizeof(int) * R);
   if (cudaDeviceSynchronize() != cudaSuccess) {
@@ -827,28 +881,18 @@ extern "C" int shahd_prefill(ShahdSession* s, const int32_t* slots, const int32_
   SHAHD_TRY(ValidateIds(s, ids, total, "PrefillCache"));
   SHAHD_CUDA_TRY(cudaStreamSynchronize(s->stream));
   for (int i = 0; i < n; i++) ResetSlot(s, slots[i]);
-  std::vector<int> order(n);
-  std::iota(order.begin(), order.end(), 0);
-  std::stable_sort(order.begin(), order.end(),
-                   [&](int a, int b) { return offsets[a + 1] - offsets[a] > offsets[b + 1] - offsets[b]; });
-  std::vector<int> lens(n), sl(n);
-  int *h_sl = Staging(s, 0), *h_po = Staging(s, 1);
+  std::vector<int> sl(slots, slots + n), starts(n), lens(n);
   for (int i = 0; i < n; i++) {
-    lens[i] = offsets[order[i] + 1] - offsets[order[i]];
-    sl[i] = slots[order[i]];
-    h_sl[i] = sl[i];
-    h_po[i] = offsets[order[i]];
+    starts[i] = offsets[i];
+    lens[i] = offsets[i + 1] - offsets[i];
     SHAHD_TRY(EnsurePages(s, sl[i], lens[i]));
   }
   SHAHD_TRY(UploadTables(s));
-  SHAHD_TRY(UploadLengths(s));
   if (total > 0) {
     SHAHD_TRY(GrowPrompt(s, total));
     SHAHD_CUDA_TRY(cudaMemcpyAsync(s->d_prompt, ids, sizeof(int) * total, cudaMemcpyHostToDevice, s->stream));
-    SHAHD_CUDA_TRY(cudaMemcpyAsync(s->d_pf_slot, h_sl, sizeof(int) * n, cudaMemcpyHostToDevice, s->stream));
-    SHAHD_CUDA_TRY(cudaMemcpyAsync(s->d_pf_poff, h_po, sizeof(int) * n, cudaMemcpyHostToDevice, s->stream));
-    SHAHD_TRY(PrefillBySteps(s, s->d_pf_slot, s->d_pf_poff, s->d_prompt, lens, sl));
   }
+  SHAHD_TRY(PrefillBatched(s, s->d_prompt, sl, starts, lens));
   SHAHD_CUDA_TRY(cudaStreamSynchronize(s->stream));
   return SHAHD_OK;
 }
@@ -882,7 +926,8 @@ extern "C" int shahd_step(ShahdSession* s, const int32_t* slots, const int32_t* 
   std::copy(tokens, tokens + n, h_tk);
   SHAHD_CUDA_TRY(cudaMemcpyAsync(s->d_slot, h_sl, sizeof(int) * n, cudaMemcpyHostToDevice, s->stream));
   SHAHD_CUDA_TRY(cudaMemcpyAsync(s->d_tok, h_tk, sizeof(int) * n, cudaMemcpyHostToDevice, s->stream));
-  StepPlan p{n, s->d_slot, s->d_tok, nullptr, nullptr, true, logits ? s->logits : nullptr, s->d_next, nullptr, nullptr, 0, 0};
+  StepPlan p{n, nullptr, true, s->d_slot, s->d_tok, nullptr, nullptr, true, logits ? s->logits : nullptr, s->d_next, nullptr,
+             nullptr, 0, 0};
   for (int i = 0; i < n; i++) p.attended += s->h_len[slots[i]] + 1;
   EnqueueStep(s, p, s->stream);
   SHAHD_TRY(CheckLaunch("shahd_step"));

@@ -25,7 +25,6 @@ namespace shahd {
 
 constexpr int kUmmaBM = 128;
 constexpr int kUmmaBK = 64;
-constexpr int kUmmaStages = 4;
 constexpr int kUmmaThreads = 128;
 
 // Rows at which a projection switches from the SIMT (CUDA-core) kernel to tensor-core tiles. Settable
@@ -34,19 +33,25 @@ extern int g_umma_min_rows;
 #define kUmmaMinRows (::shahd::g_umma_min_rows)
 
 __host__ inline int UmmaBN(int M, int N) {
-  if (M > kUmmaBM) return 128;
+  if (M > kUmmaBM) return 128;  // prefill-sized row counts: wide tiles
+  if (N <= 512) return 16;      // narrow decode projections: more CTAs
   return N <= 1024 ? 32 : 64;
 }
-__host__ inline int UmmaGridN(int N) { return CeilDiv(N, 32); }  // upper bound of N tiles (BN >= 32)
+__host__ inline int UmmaGridN(int N) { return CeilDiv(N, 16); }  // upper bound of N tiles (BN >= 16)
 
 inline bool UmmaLinearSupported(const LinearArgs& la) { return la.Kp % 8 == 0 && la.N >= 1 && la.ab != nullptr; }
 
+// Pipeline depth by tile width: narrow tiles keep a whole decode-sized K in flight.
+__host__ __device__ constexpr int UmmaStages(int BN) { return BN <= 32 ? 8 : (BN <= 64 ? 6 : 4); }
+
 template <int BN>
 struct UmmaSmem {
+  static constexpr int kStages = UmmaStages(BN);
   static constexpr int kA = kUmmaBM * kUmmaBK * 2;  // 16 KB
   static constexpr int kB = BN * kUmmaBK * 2;
   static constexpr int kStage = kA + kB;
-  static constexpr int kBytes = kUmmaStages * kStage + 1024 /*align*/ + 256 /*barriers*/;
+  static constexpr int kBytes = kStages * kStage + 1024 /*align*/ + 256 /*barriers*/;
+  static constexpr int kTmemCols = BN < 32 ? 32 : BN;
 };
 
 // ---- host: TMA descriptor for a bf16 row-major [rows, cols] matrix, box [box_rows, 64] ------------
@@ -119,24 +124,24 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
     LinearUmmaKernel(LinearArgs la, Epi epi, const __grid_constant__ CUtensorMap tmap_a,
                      const __grid_constant__ CUtensorMap tmap_w) {
   using L = UmmaSmem<BN>;
+  constexpr int S = L::kStages;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kUmmaStages * L::kStage);
-  uint64_t* empty = full + kUmmaStages;
-  uint64_t* final_bar = empty + kUmmaStages;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + S * L::kStage);
+  uint64_t* empty = full + S;
+  uint64_t* final_bar = empty + S;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(final_bar + 1);
   volatile int* s_abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n0 = blockIdx.x * BN;
   const int m0 = blockIdx.y * kUmmaBM;
-  const int rows = min(kUmmaBM, la.M - m0);
   const int nk = CeilDiv(la.Kp, kUmmaBK);
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kUmmaStages; s++) {
-      MbarInit(&full[s], 1);
-      MbarInit(&empty[s], 1);
+    for (int st = 0; st < S; st++) {
+      MbarInit(&full[st], 1);
+      MbarInit(&empty[st], 1 + kUmmaThreads / 32);  // the MMA commit + one arrival per warp
     }
     MbarInit(final_bar, 1);
     *s_abort = 0;
@@ -146,7 +151,7 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
   }
   __syncwarp();
   if (warp == 0) {
-    TmemAlloc(tmem_slot, BN);
+    TmemAlloc(tmem_slot, L::kTmemCols);
     TmemRelinquish();
   }
   TcgenFenceBefore();
@@ -154,74 +159,78 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
   TcgenFenceAfter();
   const uint32_t tmem = *tmem_slot;
 
-  // producer prologue: fill the pipeline
+  // Weights do not depend on earlier kernels: start their loads before waiting for the predecessor.
   if (threadIdx.x == 0) {
-    for (int kb = 0; kb < nk && kb < kUmmaStages; kb++) {
+    for (int kb = 0; kb < nk && kb < S; kb++) {
       uint8_t* sa = smem + kb * L::kStage;
       MbarArriveExpectTx(&full[kb], L::kStage);
-      TmaLoad2D(sa, &tmap_a, &full[kb], kb * kUmmaBK, m0);
       TmaLoad2D(sa + L::kA, &tmap_w, &full[kb], kb * kUmmaBK, n0);
     }
   }
-
-  // row statistics of the norm from the bf16 rows the MMA consumes (thread = row), overlapping the loads
-  const int r = warp * 32 + lane;
-  float mu = 0.f, is = 1.f;
-  if (NORM != kNormNone && r < rows) {
-    const bf16* src = la.ab + (size_t)(m0 + r) * la.ldab;
-    float s1 = 0.f, s2 = 0.f;
-#pragma unroll 8
-    for (int k = 0; k < la.K; k += 8) {
-      float f[8];
-      Bf16x8ToFloat(LoadNc16(src + k), f);
-#pragma unroll
-      for (int j = 0; j < 8; j++) {
-        const float v = (k + j < la.K) ? f[j] : 0.f;
-        s1 += v;
-        s2 += v * v;
-      }
-    }
-    if (NORM == kNormRms) {
-      is = 1.0f / sqrtf(s2 / la.K + la.eps);
-    } else {
-      mu = s1 / la.K;
-      const float var = fmaxf(s2 / la.K - mu * mu, 0.f);
-      is = 1.0f / sqrtf(var + la.eps);
-    }
+  GridDepWait();
+  GridDepLaunch();
+  if (threadIdx.x == 0) {
+    for (int kb = 0; kb < nk && kb < S; kb++) TmaLoad2D(smem + kb * L::kStage, &tmap_a, &full[kb], kb * kUmmaBK, m0);
   }
 
-  // MMA issue (one thread): consume stage kb, then refill it with kb + kUmmaStages
-  if (threadIdx.x == 0) {
-    const uint32_t idesc = UmmaIdescBf16(kUmmaBM, BN);
-    for (int kb = 0; kb < nk; kb++) {
-      const int st = kb % kUmmaStages;
-      const uint32_t ph = (kb / kUmmaStages) & 1;
-      if (!MbarWaitBounded(&full[st], ph, kWaitLimit)) {
-        atomicCAS(&g_shahd_device_error, 0, kDevErrUmmaTimeout);
-        *s_abort = 1;
-        break;
+  // Main loop. Every thread waits for each stage and (for a norm) accumulates its own row's statistics
+  // from the staged bf16 tile; thread 0 issues the MMAs and refills the stage once the MMAs and the four
+  // warps are done with it.
+  const int r = warp * 32 + lane;
+  float s1 = 0.f, s2 = 0.f;
+  const uint32_t idesc = UmmaIdescBf16(kUmmaBM, BN);
+  for (int kb = 0; kb < nk; kb++) {
+    const int st = kb % S;
+    const uint32_t ph = (kb / S) & 1;
+    uint8_t* sa = smem + st * L::kStage;
+    // warp-uniform outcome, so a lane never leaves the loop while its warp-mates wait in __syncwarp
+    if (!__all_sync(0xffffffffu, MbarWaitBounded(&full[st], ph, kWaitLimit))) {
+      if (lane == 0) atomicCAS(&g_shahd_device_error, 0, kDevErrUmmaTimeout);
+      *s_abort = 1;
+      break;
+    }
+    if (NORM != kNormNone) {
+#pragma unroll
+      for (int c = 0; c < 8; c++) {
+        float f[8];
+        Bf16x8ToFloat(*reinterpret_cast<const uint4*>(sa + Sw128Offset(r, c)), f);
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+          s1 += f[j];
+          s2 += f[j] * f[j];
+        }
       }
+    }
+    __syncwarp();
+    if (lane == 0) MbarArrive(&empty[st]);
+    if (threadIdx.x == 0) {
       TcgenFenceAfter();
-      uint8_t* sa = smem + st * L::kStage;
       const uint64_t ad = SmemDescSw128(SmemAddr(sa));
       const uint64_t bd = SmemDescSw128(SmemAddr(sa + L::kA));
 #pragma unroll
       for (int kk = 0; kk < kUmmaBK / 16; kk++)
         UmmaBf16(tmem, ad + (uint64_t)(kk * 2), bd + (uint64_t)(kk * 2), idesc, (kb > 0 || kk > 0) ? 1u : 0u);
       UmmaCommit(&empty[st]);
-      if (kb + kUmmaStages < nk) {
+      if (kb + S < nk) {
         if (!MbarWaitBounded(&empty[st], ph, kWaitLimit)) {
           atomicCAS(&g_shahd_device_error, 0, kDevErrUmmaTimeout);
           *s_abort = 1;
-          break;
+        } else {
+          const int kn = kb + S;
+          MbarArriveExpectTx(&full[st], L::kStage);
+          TmaLoad2D(sa, &tmap_a, &full[st], kn * kUmmaBK, m0);
+          TmaLoad2D(sa + L::kA, &tmap_w, &full[st], kn * kUmmaBK, n0);
         }
-        const int kn = kb + kUmmaStages;
-        MbarArriveExpectTx(&full[st], L::kStage);
-        TmaLoad2D(sa, &tmap_a, &full[st], kn * kUmmaBK, m0);
-        TmaLoad2D(sa + L::kA, &tmap_w, &full[st], kn * kUmmaBK, n0);
       }
     }
-    if (!*s_abort) UmmaCommit(final_bar);
+  }
+  if (threadIdx.x == 0 && !*s_abort) UmmaCommit(final_bar);
+  float mu = 0.f, is = 1.f;
+  if (NORM == kNormRms) {
+    is = 1.0f / sqrtf(s2 / la.K + la.eps);
+  } else if (NORM == kNormLayer) {
+    mu = s1 / la.K;
+    is = 1.0f / sqrtf(fmaxf(s2 / la.K - mu * mu, 0.f) + la.eps);
   }
   __syncthreads();
   if (!*s_abort && !MbarWaitBounded(final_bar, 0, kWaitLimit)) {
@@ -232,7 +241,7 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
   TcgenFenceAfter();
   if (!*s_abort) {
     // Epilogue: thread = row (m0 + 32*warp + lane), 16 consecutive accumulator columns per TMEM load.
-    const bool row_ok = r < rows;
+    const bool row_ok = m0 + r < la.M;
     float bv = -INFINITY;
     int bi = 0x7fffffff;
 #pragma unroll 1
@@ -272,7 +281,7 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
   TcgenFenceBefore();
   __syncthreads();
   __syncwarp();
-  if (warp == 0) TmemDealloc(tmem, BN);
+  if (warp == 0) TmemDealloc(tmem, L::kTmemCols);
 }
 
 template <int NORM, class Epi, int BN>
@@ -287,13 +296,14 @@ void LaunchUmmaLinearBN(const LinearArgs& la, const Epi& epi, cudaStream_t st) {
     configured = true;
   }
   dim3 grid(CeilDiv(la.N, BN), CeilDiv(la.M, kUmmaBM));
-  LinearUmmaKernel<NORM, Epi, BN><<<grid, kUmmaThreads, UmmaSmem<BN>::kBytes, st>>>(la, epi, ta, tw);
+  LaunchPdl(LinearUmmaKernel<NORM, Epi, BN>, grid, dim3(kUmmaThreads), UmmaSmem<BN>::kBytes, st, la, epi, ta, tw);
 }
 
 template <int NORM, class Epi>
 void LaunchUmmaLinear(const LinearArgs& la, const Epi& epi, cudaStream_t st) {
   const int bn = UmmaBN(la.M, la.N);
-  if (bn == 32) LaunchUmmaLinearBN<NORM, Epi, 32>(la, epi, st);
+  if (bn == 16) LaunchUmmaLinearBN<NORM, Epi, 16>(la, epi, st);
+  else if (bn == 32) LaunchUmmaLinearBN<NORM, Epi, 32>(la, epi, st);
   else if (bn == 64) LaunchUmmaLinearBN<NORM, Epi, 64>(la, epi, st);
   else LaunchUmmaLinearBN<NORM, Epi, 128>(la, epi, st);
 }

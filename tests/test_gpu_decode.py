@@ -167,6 +167,24 @@ def test_phase2_shape_parity():
     _teacher_forced_shape(pkg.configs.PHASE2, nseq=2, prompt_len=16, steps=4)
 
 
+def test_launch_modes_give_identical_ids():
+    # programmatic dependent launch only changes scheduling: ids must be bit-identical with it off
+    w = pkg.configs.MICROCHAT
+    cfg = w.model
+    p = pkg.init_params(cfg, w.weight_seed)
+    prompts = np.stack([O.uniform_ids(40, cfg.vocab_size, seed=500 + i) for i in range(8)])
+    lib = pkg.load()
+    with pkg.Session(cfg, p, max_seqs=8) as sess:
+        a = sess.generate(prompts, 20)
+        lib.ShahdSetProgrammaticLaunch(0)
+        try:
+            b = sess.generate(prompts, 20)
+        finally:
+            lib.ShahdSetProgrammaticLaunch(1)
+    assert np.array_equal(a, b)
+    assert lib.ShahdDeviceErrorFlag() == 0
+
+
 def test_microchat_generate_spot_check_and_determinism():
     w = pkg.configs.MICROCHAT
     cfg = w.model
