@@ -166,6 +166,11 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
     w = pkg.configs.WORKLOADS[args.workload]
     cfg = w.model
     params = pkg.init_params(cfg, w.weight_seed)
+    lib = pkg.load()
+    if args.chains:
+        lib.ShahdSetDecodeChains(args.chains)
+    if args.tc_min_rows:
+        lib.ShahdSetTensorCoreMinRows(args.tc_min_rows)
     sess = pkg.Session(cfg, params, max_seqs=w.seqs, device=local_rank)
     prompts = prompts_for(w, rank)
     offs = np.arange(0, (w.seqs + 1) * w.prompt_len, w.prompt_len, dtype=np.int32)
@@ -220,7 +225,8 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
         if dist is not None:
             dist.destroy_process_group()
         if rank == 0:
-            print(json.dumps({"ms_per_step": ms_per_step, "value": value, "gpu_launches": int(launches)}), flush=True)
+            print(json.dumps({"ms_per_step": ms_per_step, "value": value, "gpu_launches": int(launches),
+                              "chains": args.chains, "tc_min_rows": args.tc_min_rows}), flush=True)
         return
 
     # gather per-rank output checksums (the only collective, outside the timed region)
@@ -311,6 +317,8 @@ def main() -> None:
     ap.add_argument("--workload", default="microchat", choices=sorted(pkg.configs.WORKLOADS))
     ap.add_argument("--no-extras", action="store_true",
                     help="time the steps only (no e2e, profile or CPU legs): the profiling command line")
+    ap.add_argument("--chains", type=int, default=0, help="concurrent decode chains (0 = library default)")
+    ap.add_argument("--tc-min-rows", type=int, default=0, help="rows from which projections use tensor cores (0 = default)")
     ap.add_argument("--new-tokens", type=int, default=None,
                     help="override the workload's new tokens per sequence (small ncu captures only)")
     args = ap.parse_args()

@@ -68,6 +68,10 @@ void ShahdSetTensorCoreMinRows(int rows);
  * while its predecessor drains and overlaps its setup and weight loads. Process-wide; no counterpart in
  * the reference. */
 void ShahdSetProgrammaticLaunch(int enable);
+/* Concurrent chains a batched decode step is split into (independent sequences on their own streams,
+ * joined in one CUDA graph); 0 = automatic (one per 16 sequences, at most 4). Process-wide tuning hook;
+ * no counterpart in the reference. Results do not depend on it. */
+void ShahdSetDecodeChains(int chains);
 /* First error code a kernel recorded for a bounded device-side wait that gave up (0 = none). */
 int ShahdDeviceErrorFlag(void);
 /* Device-pointer MatMulNT on the tensor cores: out[M,N] (+)= a[M,K] @ btᵀ with a, bt bf16 row-major

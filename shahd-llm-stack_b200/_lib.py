@@ -60,6 +60,7 @@ SIGNATURES = {
     "ShahdSetTensorCoreMinRows": (None, [ctypes.c_int]),
     "ShahdDeviceErrorFlag": (ctypes.c_int, []),
     "ShahdSetProgrammaticLaunch": (None, [ctypes.c_int]),
+    "ShahdSetDecodeChains": (None, [ctypes.c_int]),
     "ShahdMatMulNTBF16Device": (ctypes.c_int, [_vp, _vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, _vp]),
     "shahd_param_count": (_i64, [ctypes.POINTER(ShahdModelCfg)]),
     "shahd_init_params": (ctypes.c_int, [ctypes.POINTER(ShahdModelCfg), _u32, _fp, _i64]),

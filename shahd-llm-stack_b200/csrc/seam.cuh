@@ -13,6 +13,7 @@ namespace shahd {
 
 int g_umma_min_rows = 17;
 bool g_use_pdl = true;
+int g_decode_chains = 0;  // 0 = automatic
 
 // ---- thread-local last error --------------------------------------------------------------------
 static thread_local std::string t_error;
@@ -392,6 +393,8 @@ const char* ShahdLastError(void) { return GetError(); }
 void ShahdSetTensorCoreMinRows(int rows) { g_umma_min_rows = rows < 1 ? 1 : rows; }
 
 void ShahdSetProgrammaticLaunch(int enable) { g_use_pdl = enable != 0; }
+
+void ShahdSetDecodeChains(int chains) { g_decode_chains = chains < 0 ? 0 : chains; }
 
 int ShahdDeviceErrorFlag(void) {
   int v = 0;

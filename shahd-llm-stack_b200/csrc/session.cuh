@@ -30,7 +30,7 @@ struct Layer {
 
 // Everything a captured step bakes in.
 struct GraphKey {
-  int kind;  // 0 = prefill step, 1 = decode step
+  int kind;  // 16 * (0 = prefill step, 1 = decode step) + number of concurrent chains
   int M;
   const void *slot, *tok, *poff, *prompt, *out;
   int out_ld;
@@ -57,6 +57,9 @@ struct ShahdSession {
   int max_seqs;
   int rows_cap;  // rows of the activation buffers: max(max_seqs, prefill chunk)
   int num_sms;
+  int chains_hint = 1;  // decode chains running concurrently (attention splits share the GPU among them)
+  cudaStream_t side[7] = {};  // extra streams of the concurrent decode chains
+  cudaEvent_t fork_ev = nullptr, chain_ev[7] = {};
   cudaStream_t stream = nullptr;
   cudaEvent_t join_in = nullptr, join_out = nullptr;
   std::mutex mu;
@@ -117,6 +120,7 @@ namespace {
 // 7 lengths, 8-11 the prefill plan.
 constexpr int kStagingRows = 12;
 constexpr int kPrefillRows = 8192;  // rows of one batched prefill chunk (whole sequences per chunk)
+constexpr int kMaxChains = 8;
 
 template <class T>
 int DevAlloc(ShahdSession* s, T** p, size_t count) {
@@ -240,31 +244,56 @@ LinearArgs Lin(const float* a, int lda, const bf16* ab, int ldab, int rows_cap, 
 
 // Enqueue one batched cached step (AdvanceOneToken + HeadLogitsRow for M rows) on `st`; returns the
 // number of kernels it launched.
-int EnqueueStep(ShahdSession* s, const StepPlan& p, cudaStream_t st) {
+int EnqueueStep(ShahdSession* s, const StepPlan& p, cudaStream_t st, int r0 = 0) {
+  // Row-indexed buffers: activations and positions hold rows_cap rows, the LM-head / finish / attention
+  // split scratch holds max_seqs rows. This step uses rows [r0, r0 + M) of them (a decode chain's window).
+  // A step beyond either is a caller bug, not a device fault.
+  if (p.M < 1 || r0 < 0 || r0 + p.M > s->rows_cap || ((p.head || p.finish) && r0 + p.M > s->max_seqs)) {
+    SetError("internal: step of rows [%d, %d) exceeds the session's row buffers", r0, r0 + p.M);
+    return -1;
+  }
   const long long before = s->launches;
-  const int M = p.M, R = s->rows_cap;
+  const int M = p.M, R = s->rows_cap - r0;  // rows addressable from the window base (TMA map height)
   const int norm = s->cfg.norm_kind == 1 ? kNormRms : kNormLayer;
   const float eps = (float)s->cfg.layer_norm_eps;
+  const int hd = s->H * s->d;
+  float* x = s->x + (size_t)r0 * s->E;
+  bf16* xb = s->xb + (size_t)r0 * s->Ep;
+  float* q = s->q + (size_t)r0 * hd;
+  float* ctx = s->ctx + (size_t)r0 * hd;
+  bf16* ctxb = s->ctxb + (size_t)r0 * s->HDp;
+  float* act = s->act + (size_t)r0 * s->F;
+  bf16* actb = s->actb + (size_t)r0 * s->Fp;
+  int* pos = s->d_pos + r0;
+  // scratch that exists for decode rows only (r0 + M <= max_seqs when used)
+  const size_t rd = (size_t)std::min(r0, s->max_seqs);
+  float* am_val = s->am_val + rd * s->am_stride;
+  int* am_idx = s->am_idx + rd * s->am_stride;
+  int* gen_count = s->d_gen_count + rd;
+  float* part_o = s->part_o + rd * s->H * s->max_blocks * s->d;
+  float* part_m = s->part_m + rd * s->H * s->max_blocks;
+  float* part_l = s->part_l + rd * s->H * s->max_blocks;
+  int* counter = s->attn_counter + rd * s->Hk;
   Timed(s, st, kProfOther, 8.0 * M * s->E, [&] {
-    EmbedArgs e{p.pos_in, p.slot, p.tok, p.prompt, p.poff, s->d_seq_len, s->d_pos, s->wte, s->wpe, s->x, s->xb, s->E, s->Ep};
+    EmbedArgs e{p.pos_in, p.slot, p.tok, p.prompt, p.poff, s->d_seq_len, pos, s->wte, s->wpe, x, xb, s->E, s->Ep};
     LaunchPdl(EmbedKernel, dim3(M), dim3(128), 0, st, e);
   });
   KvView kv{s->kv_pool, s->d_block_table, s->max_blocks, s->Hk, s->d, s->page_elems};
-  const int hd = s->H * s->d;
   // K and V rows read (bf16) + q read and ctx written (fp32 + bf16)
   const double attn_bytes = 4.0 * s->Hk * s->d * (double)p.attended + 10.0 * M * hd;
+  // splits per (row, kv head): enough CTAs to fill the GPU; one split (no partials) beyond max_seqs rows
+  int nsplit = 1;
+  if (r0 + M <= s->max_seqs)
+    nsplit = std::max(1, std::min(s->max_blocks, CeilDiv(3 * s->num_sms / std::max(1, s->chains_hint), M * s->Hk)));
   for (int l = 0; l < s->L; l++) {
     const Layer& Ly = s->layers[l];
     // norm1 + QKV + RoPE + KV append (CachedForward.ts:66-73, :78-79)
-    const LinearArgs la = Lin(s->x, s->E, s->xb, s->Ep, R, M, s->E, s->Ep, Ly.w_qkv, s->Nqkv, eps, Ly.qkv_c1, Ly.qkv_c2);
-    const EpiQKV eq{s->q, kv, l, s->d_pos, p.slot, s->rope_cos, s->rope_sin, s->H, s->Hk, s->d};
+    const LinearArgs la = Lin(x, s->E, xb, s->Ep, R, M, s->E, s->Ep, Ly.w_qkv, s->Nqkv, eps, Ly.qkv_c1, Ly.qkv_c2);
+    const EpiQKV eq{q, kv, l, pos, p.slot, s->rope_cos, s->rope_sin, s->H, s->Hk, s->d};
     Timed(s, st, kProfLinear, LinearBytes(M, s->E, s->Ep, s->Nqkv), [&] { LaunchLinear(norm, la, eq, st); });
     // attention over the cache (CachedForward.ts:76-80)
-    AttnArgs aa{s->q, s->ctx, s->ctxb, s->HDp, kv, l, s->d_pos, p.slot, s->H, s->Hk, s->G, s->d,
-                (float)(1.0 / std::sqrt((double)s->d)), s->max_blocks, s->part_o, s->part_m, s->part_l, s->attn_counter};
-    // splits per (row, kv head): enough CTAs to fill the GPU; one split (no partials) beyond max_seqs rows
-    int nsplit = 1;
-    if (M <= s->max_seqs) nsplit = std::max(1, std::min(s->max_blocks, CeilDiv(3 * s->num_sms, M * s->Hk)));
+    AttnArgs aa{q, ctx, ctxb, s->HDp, kv, l, pos, p.slot, s->H, s->Hk, s->G, s->d,
+                (float)(1.0 / std::sqrt((double)s->d)), s->max_blocks, part_o, part_m, part_l, counter};
     dim3 ag(nsplit, s->Hk, M);
     Timed(s, st, kProfAttention, attn_bytes, [&] {
       if (s->d == 64) LaunchPdl(AttnDecodeKernel<64>, ag, dim3(kAttnThreads), AttnSmemBytes(64), st, aa);
@@ -273,34 +302,41 @@ int EnqueueStep(ShahdSession* s, const StepPlan& p, cudaStream_t st) {
       else LaunchPdl(AttnDecodeGenericKernel, ag, dim3(kAttnThreads), 0, st, aa);
     });
     // summed per-head Wo + residual (CachedForward.ts:81-84)
-    const LinearArgs lo = Lin(s->ctx, hd, s->ctxb, s->HDp, R, M, hd, s->HDp, Ly.w_o, s->E, eps, nullptr, nullptr);
+    const LinearArgs lo = Lin(ctx, hd, ctxb, s->HDp, R, M, hd, s->HDp, Ly.w_o, s->E, eps, nullptr, nullptr);
     Timed(s, st, kProfLinear, LinearBytes(M, hd, s->HDp, s->E),
-          [&] { LaunchLinear(kNormNone, lo, EpiResid{s->x, s->xb, s->E, s->Ep, nullptr}, st); });
+          [&] { LaunchLinear(kNormNone, lo, EpiResid{x, xb, s->E, s->Ep, nullptr}, st); });
     // norm2 + MLP + residual (CachedForward.ts:86-87)
-    const LinearArgs lu = Lin(s->x, s->E, s->xb, s->Ep, R, M, s->E, s->Ep, Ly.w_up, s->Nup, eps, Ly.up_c1, Ly.up_c2);
+    const LinearArgs lu = Lin(x, s->E, xb, s->Ep, R, M, s->E, s->Ep, Ly.w_up, s->Nup, eps, Ly.up_c1, Ly.up_c2);
     Timed(s, st, kProfLinear, LinearBytes(M, s->E, s->Ep, s->Nup), [&] {
-      if (s->cfg.mlp_kind == 0) LaunchLinear(norm, lu, EpiReluFc{s->act, s->actb, s->F, s->Fp, Ly.b_fc}, st);
-      else LaunchLinear(norm, lu, EpiGated{s->act, s->actb, s->F, s->Fp, s->cfg.mlp_kind == 2}, st);
+      if (s->cfg.mlp_kind == 0) LaunchLinear(norm, lu, EpiReluFc{act, actb, s->F, s->Fp, Ly.b_fc}, st);
+      else LaunchLinear(norm, lu, EpiGated{act, actb, s->F, s->Fp, s->cfg.mlp_kind == 2}, st);
     });
-    const LinearArgs ld = Lin(s->act, s->F, s->actb, s->Fp, R, M, s->F, s->Fp, Ly.w_down, s->E, eps, nullptr, nullptr);
+    const LinearArgs ld = Lin(act, s->F, actb, s->Fp, R, M, s->F, s->Fp, Ly.w_down, s->E, eps, nullptr, nullptr);
     Timed(s, st, kProfLinear, LinearBytes(M, s->F, s->Fp, s->E),
-          [&] { LaunchLinear(kNormNone, ld, EpiResid{s->x, s->xb, s->E, s->Ep, Ly.b_proj}, st); });
+          [&] { LaunchLinear(kNormNone, ld, EpiResid{x, xb, s->E, s->Ep, Ly.b_proj}, st); });
   }
   int nblk = 0;
   if (p.head) {
     // final norm + LM head + argmax partials (HeadLogitsRow, CachedRowMath.ts:117-137)
     nblk = HeadBlocks(s, M);
-    const LinearArgs lh = Lin(s->x, s->E, s->xb, s->Ep, R, M, s->E, s->Ep, s->w_head, s->V, eps, s->head_c1, s->head_c2,
-                              s->am_val, s->am_idx);
+    const LinearArgs lh = Lin(x, s->E, xb, s->Ep, R, M, s->E, s->Ep, s->w_head, s->V, eps, s->head_c1, s->head_c2,
+                              am_val, am_idx);
     Timed(s, st, kProfLinear, LinearBytes(M, s->E, s->Ep, s->V),
           [&] { LaunchLinear(norm, lh, EpiLogits{p.logits, s->head_bias}, st); });
   }
   if (p.finish) {
-    FinishArgs f{M, p.slot, s->d_pos, s->d_seq_len, p.head ? s->am_val : nullptr, s->am_idx, nblk, p.next_ids,
-                 p.cur_tok, p.out_ids, p.out_ld, s->d_gen_count, nullptr};
+    FinishArgs f{M, p.slot, pos, s->d_seq_len, p.head ? am_val : nullptr, am_idx, nblk, p.next_ids,
+                 p.cur_tok, p.out_ids, p.out_ld, gen_count, nullptr};
     Timed(s, st, kProfOther, 16.0 * M, [&] { LaunchPdl(FinishKernel, dim3(CeilDiv(M, 4)), dim3(128), 0, st, f); });
   }
   return (int)(s->launches - before);
+}
+
+// Concurrent decode chains for n rows: the process-wide setting, or automatically one chain per 16 rows
+// up to 4 (16-row chains keep each kernel short while four of them fill the GPU).
+int DecodeChains(int n) {
+  int c = g_decode_chains > 0 ? g_decode_chains : std::min(4, std::max(1, n / 16));
+  return std::max(1, std::min(std::min(c, kMaxChains), n));
 }
 
 int CheckLaunch(const char* what) {
@@ -312,18 +348,52 @@ int CheckLaunch(const char* what) {
   return SHAHD_OK;
 }
 
-// Run a step through a cached CUDA graph. The first use of a shape runs eagerly (lazy host-side setup
-// such as kernel attributes and TMA descriptors stays out of capture), the second captures it, every
-// later one replays it. Profiling runs eagerly so each kernel can be bracketed with events.
-int RunStep(ShahdSession* s, const StepPlan& p, int kind) {
+// Enqueue several steps as concurrent chains: chain c runs on its own stream over its own row window
+// (r0[c]), forked from and joined back into the session stream with events. Returns the kernels launched.
+int EnqueueChains(ShahdSession* s, const StepPlan* plans, const int* r0, int nchain) {
+  int total = 0;
+  if (nchain > 1) {
+    cudaEventRecord(s->fork_ev, s->stream);
+    for (int c = 1; c < nchain; c++) cudaStreamWaitEvent(s->side[c - 1], s->fork_ev, 0);
+  }
+  for (int c = 0; c < nchain; c++) total += EnqueueStep(s, plans[c], c == 0 ? s->stream : s->side[c - 1], r0[c]);
+  if (nchain > 1) {
+    for (int c = 1; c < nchain; c++) {
+      cudaEventRecord(s->chain_ev[c - 1], s->side[c - 1]);
+      cudaStreamWaitEvent(s->stream, s->chain_ev[c - 1], 0);
+    }
+  }
+  return total;
+}
+
+bool ChainsFit(ShahdSession* s, const StepPlan* plans, const int* r0, int nchain) {
+  for (int c = 0; c < nchain; c++) {
+    const StepPlan& p = plans[c];
+    if (p.M < 1 || r0[c] < 0 || r0[c] + p.M > s->rows_cap || ((p.head || p.finish) && r0[c] + p.M > s->max_seqs)) {
+      SetError("internal: step of rows [%d, %d) exceeds the session's row buffers", r0[c], r0[c] + p.M);
+      return false;
+    }
+  }
+  return true;
+}
+
+// Run a step (or concurrent chains of steps) through a cached CUDA graph. The first use of a shape runs
+// eagerly (lazy host-side setup such as kernel attributes and TMA descriptors stays out of capture), the
+// second captures it, every later one replays it. Profiling runs eagerly so each kernel can be bracketed
+// with events.
+int RunStep(ShahdSession* s, const StepPlan* plans, const int* r0, int nchain, int kind) {
+  if (!ChainsFit(s, plans, r0, nchain)) return SHAHD_EINVAL;
+  s->chains_hint = nchain;
   if (s->prof) {
-    EnqueueStep(s, p, s->stream);
+    EnqueueChains(s, plans, r0, nchain);
     return CheckLaunch("step");
   }
-  GraphKey key{kind, p.M, p.slot, p.tok, p.poff, p.prompt, p.out_ids, p.out_ld, g_umma_min_rows * 2 + (int)g_use_pdl};
+  const StepPlan& p = plans[0];
+  GraphKey key{kind * 16 + nchain, p.M, p.slot, p.tok, p.poff, p.prompt, p.out_ids, p.out_ld,
+               g_umma_min_rows * 2 + (int)g_use_pdl};
   auto it = s->graphs.find(key);
   if (it == s->graphs.end()) {
-    EnqueueStep(s, p, s->stream);
+    EnqueueChains(s, plans, r0, nchain);
     SHAHD_TRY(CheckLaunch("step"));
     s->graphs.emplace(key, StepGraph{nullptr, 0});
     return SHAHD_OK;
@@ -332,7 +402,7 @@ int RunStep(ShahdSession* s, const StepPlan& p, int kind) {
     cudaGraph_t g = nullptr;
     SHAHD_CUDA_TRY(cudaStreamBeginCapture(s->stream, cudaStreamCaptureModeThreadLocal));
     const long long saved = s->launches;
-    const int n = EnqueueStep(s, p, s->stream);
+    const int n = EnqueueChains(s, plans, r0, nchain);
     s->launches = saved;
     cudaError_t e = cudaStreamEndCapture(s->stream, &g);
     if (e != cudaSuccess) {
@@ -351,6 +421,11 @@ int RunStep(ShahdSession* s, const StepPlan& p, int kind) {
   SHAHD_CUDA_TRY(cudaGraphLaunch(it->second.exec, s->stream));
   s->launches += it->second.launches;
   return SHAHD_OK;
+}
+
+int RunStep(ShahdSession* s, const StepPlan& p, int kind) {
+  const int r0 = 0;
+  return RunStep(s, &p, &r0, 1, kind);
 }
 
 // ---- KV page management (host mirror of the block table) ---------------------------------------
@@ -572,8 +647,17 @@ int GenerateCore(ShahdSession* s, const int* d_prompt_packed, const std::vector<
   SHAHD_TRY(PrefillBatched(s, d_prompt_packed, slots, pstart, plen));
   GatherLastTokens<<<CeilDiv(n, 128), 128, 0, s->stream>>>(d_prompt_packed, s->d_ends, n, s->d_tok);
   s->launches++;
-  // the decode loop: step k consumes the last context id (k = 0) or the id sampled at k-1
-  StepPlan p{n, nullptr, true, s->d_slot, s->d_tok, nullptr, nullptr, true, nullptr, nullptr, s->d_tok, d_out, max_new, 0};
+  // the decode loop: step k consumes the last context id (k = 0) or the id sampled at k-1. Rows are split
+  // into concurrent chains (independent sequences) so several latency-bound kernel chains share the GPU.
+  const int nchain = DecodeChains(n);
+  StepPlan plans[kMaxChains];
+  int r0[kMaxChains];
+  for (int c = 0; c < nchain; c++) {
+    r0[c] = c * n / nchain;
+    const int rows = (c + 1) * n / nchain - r0[c];
+    plans[c] = StepPlan{rows, nullptr, true, s->d_slot + r0[c], s->d_tok + r0[c], nullptr, nullptr, true, nullptr,
+                        nullptr, s->d_tok + r0[c], d_out + (size_t)r0[c] * max_new, max_new, 0};
+  }
   for (int k = 0; k < max_new; k++) {
     // rows whose window is full rebuild it from their last C-1 ids first (CachedForward.ts:135-141)
     std::vector<int> slide;
@@ -595,9 +679,11 @@ int GenerateCore(ShahdSession* s, const int* d_prompt_packed, const std::vector<
       s->launches++;
       SHAHD_TRY(PrefillBatched(s, s->d_window, slide, wstart, wlen));
     }
-    p.attended = 0;
-    for (int i = 0; i < n; i++) p.attended += s->h_len[i] + 1;
-    SHAHD_TRY(RunStep(s, p, 1));
+    for (int c = 0; c < nchain; c++) {
+      plans[c].attended = 0;
+      for (int i = r0[c]; i < r0[c] + plans[c].M; i++) plans[c].attended += s->h_len[i] + 1;
+    }
+    SHAHD_TRY(RunStep(s, plans, r0, nchain, 1));
     for (int i = 0; i < n; i++) s->h_len[i] += 1;
   }
   return CheckLaunch("generate");
@@ -695,9 +781,14 @@ extern "C" int shahd_session_create(const ShahdModelCfg* cfg, const void* params
     shahd_session_destroy(s);
     return rc;
   };
-  if (cudaStreamCreateWithFlags(&s->stream, cudaStreamNonBlocking) != cudaSuccess ||
-      cudaEventCreateWithFlags(&s->join_in, cudaEventDisableTiming) != cudaSuccess ||
-      cudaEventCreateWithFlags(&s->join_out, cudaEventDisableTiming) != cudaSuccess) {
+  bool streams_ok = cudaStreamCreateWithFlags(&s->stream, cudaStreamNonBlocking) == cudaSuccess &&
+                    cudaEventCreateWithFlags(&s->join_in, cudaEventDisableTiming) == cudaSuccess &&
+                    cudaEventCreateWithFlags(&s->join_out, cudaEventDisableTiming) == cudaSuccess &&
+                    cudaEventCreateWithFlags(&s->fork_ev, cudaEventDisableTiming) == cudaSuccess;
+  for (int c = 0; c < kMaxChains - 1 && streams_ok; c++)
+    streams_ok = cudaStreamCreateWithFlags(&s->side[c], cudaStreamNonBlocking) == cudaSuccess &&
+                 cudaEventCreateWithFlags(&s->chain_ev[c], cudaEventDisableTiming) == cudaSuccess;
+  if (!streams_ok) {
     SetError("cudaStreamCreate/cudaEventCreate failed");
     return fail(SHAHD_ECUDA);
   }
@@ -779,7 +870,8 @@ extern "C" int shahd_session_create(const ShahdModelCfg* cfg, const void* params
       (rc = DevAlloc(s, &s->part_l, (size_t)R * s->H * s->max_blocks)) != SHAHD_OK ||
       (rc = DevAlloc(s, &s->attn_counter, (size_t)R * s->Hk)) != SHAHD_OK ||
       (rc = DevAlloc(s, &s->d_slot, (size_t)R)) != SHAHD_OK || (rc = DevAlloc(s, &s->d_tok, (size_t)R)) != SHAHD_OK ||
-      (rc = DevAlloc(s, &s->d_pos, (size_t)R)) != SHAHD_OK || (rc = DevAlloc(s, &s->d_next, (size_t)R)) != SHAHD_OK ||
+      (rc = DevAlloc(s, &s->d_pos, RC)) != SHAHD_OK ||  // one position per row, prefill rows included
+      (rc = DevAlloc(s, &s->d_next, (size_t)R)) != SHAHD_OK ||
       (rc = DevAlloc(s, &s->d_gen_count, (size_t)R)) != SHAHD_OK ||
       (rc = DevAlloc(s, &s->d_ends, (size_t)R)) != SHAHD_OK ||
       (rc = DevAlloc(s, &s->d_starts, (size_t)R)) != SHAHD_OK ||
@@ -818,6 +910,11 @@ extern "C" int shahd_session_destroy(ShahdSession* s) {
   for (void* p : s->allocs) cudaFree(p);
   if (s->h_block_table) cudaFreeHost(s->h_block_table);
   if (s->h_pinned_rows) cudaFreeHost(s->h_pinned_rows);
+  for (int c = 0; c < kMaxChains - 1; c++) {
+    if (s->side[c]) cudaStreamSynchronize(s->side[c]), cudaStreamDestroy(s->side[c]);
+    if (s->chain_ev[c]) cudaEventDestroy(s->chain_ev[c]);
+  }
+  if (s->fork_ev) cudaEventDestroy(s->fork_ev);
   if (s->join_in) cudaEventDestroy(s->join_in);
   if (s->join_out) cudaEventDestroy(s->join_out);
   if (s->stream) cudaStreamDestroy(s->stream);
@@ -929,7 +1026,7 @@ extern "C" int shahd_step(ShahdSession* s, const int32_t* slots, const int32_t* 
   StepPlan p{n, nullptr, true, s->d_slot, s->d_tok, nullptr, nullptr, true, logits ? s->logits : nullptr, s->d_next, nullptr,
              nullptr, 0, 0};
   for (int i = 0; i < n; i++) p.attended += s->h_len[slots[i]] + 1;
-  EnqueueStep(s, p, s->stream);
+  if (EnqueueStep(s, p, s->stream) < 0) return SHAHD_EINVAL;
   SHAHD_TRY(CheckLaunch("shahd_step"));
   for (int i = 0; i < n; i++) s->h_len[slots[i]] += 1;
   if (logits)

@@ -30,6 +30,7 @@ constexpr int kUmmaThreads = 128;
 // Rows at which a projection switches from the SIMT (CUDA-core) kernel to tensor-core tiles. Settable
 // through ShahdSetTensorCoreMinRows / SetScalarKernels (test hooks, process-wide).
 extern int g_umma_min_rows;
+extern int g_decode_chains;
 #define kUmmaMinRows (::shahd::g_umma_min_rows)
 
 __host__ inline int UmmaBN(int M, int N) {
