@@ -64,12 +64,12 @@ const char* ShahdLastError(void);
 /* Row count from which decode projections use tcgen05 tiles instead of the SIMT kernel (default 17;
  * 1 forces tensor cores everywhere). Process-wide tuning/test hook; no counterpart in the reference. */
 void ShahdSetTensorCoreMinRows(int rows);
-/* Programmatic dependent launch between the kernels of a step (default 1): each kernel is scheduled
+/* Programmatic dependent launch between the kernels of a step (default 0): each kernel is scheduled
  * while its predecessor drains and overlaps its setup and weight loads. Process-wide; no counterpart in
  * the reference. */
 void ShahdSetProgrammaticLaunch(int enable);
 /* Concurrent chains a batched decode step is split into (independent sequences on their own streams,
- * joined in one CUDA graph); 0 = automatic (one per 16 sequences, at most 4). Process-wide tuning hook;
+ * joined in one CUDA graph); 0 = automatic (one chain). Process-wide tuning hook;
  * no counterpart in the reference. Results do not depend on it. */
 void ShahdSetDecodeChains(int chains);
 /* First error code a kernel recorded for a bounded device-side wait that gave up (0 = none). */

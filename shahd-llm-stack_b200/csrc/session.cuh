@@ -332,10 +332,10 @@ int EnqueueStep(ShahdSession* s, const StepPlan& p, cudaStream_t st, int r0 = 0)
   return (int)(s->launches - before);
 }
 
-// Concurrent decode chains for n rows: the process-wide setting, or automatically one chain per 16 rows
-// up to 4 (16-row chains keep each kernel short while four of them fill the GPU).
+// Concurrent decode chains for n rows: the process-wide setting, else one chain (measured: a step's time
+// is its serial kernel latency, which splitting the rows does not shorten).
 int DecodeChains(int n) {
-  int c = g_decode_chains > 0 ? g_decode_chains : std::min(4, std::max(1, n / 16));
+  int c = g_decode_chains > 0 ? g_decode_chains : 1;
   return std::max(1, std::min(std::min(c, kMaxChains), n));
 }
 

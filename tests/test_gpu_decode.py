@@ -176,11 +176,11 @@ def test_launch_modes_give_identical_ids():
     lib = pkg.load()
     with pkg.Session(cfg, p, max_seqs=8) as sess:
         a = sess.generate(prompts, 20)
-        lib.ShahdSetProgrammaticLaunch(0)
+        lib.ShahdSetProgrammaticLaunch(1)
         try:
             b = sess.generate(prompts, 20)
         finally:
-            lib.ShahdSetProgrammaticLaunch(1)
+            lib.ShahdSetProgrammaticLaunch(0)
     assert np.array_equal(a, b)
     assert lib.ShahdDeviceErrorFlag() == 0
 
