@@ -79,6 +79,19 @@ int ShahdDeviceErrorFlag(void);
  * pointers 16-byte aligned. stream may be 0. Returns a status code.  (MatMulNtInto/MatMulNtAcc of
  * ComputeBackend.ts:29-36 for device-resident operands.) */
 int ShahdMatMulNTBF16Device(const void* a, const void* bt, float* out, int m, int k, int n, int acc, void* stream);
+/* MatMulNTF32 that never allocates or frees device memory; no counterpart in the reference.
+ * out[M,N] (+)= a[M,K] @ btᵀ with the same kernel and the same results as MatMulNTF32, but the
+ * operands are staged in one fixed 16 MiB array per device that is part of the library's device image
+ * instead of a workspace grown by cudaMalloc/cudaFree. For callers that cannot allocate: a process whose
+ * device memory is already committed (a session KV pool sized to fill HBM), or one that must not let a
+ * cudaFree wait on the whole device while other streams run decode steps.
+ * Limit: 4*(round64(M*K) + round64(N*K) + M*N) <= 16 MiB; larger calls return SHAHD_EINVAL with a
+ * message naming the size and the limit. The first call on each device does the set-up (looks up the
+ * array's device address, which may load the library's device module): make that first call before
+ * any stream capture begins. All calls on a device share the one array: calls that overlap in time
+ * (from several host threads) race on it, so such callers must serialize them. Synchronous; runs on the
+ * calling thread's per-thread default stream. Returns a status code. */
+int ShahdMatMulNTF32NoAlloc(const float* a, const float* bt, float* out, int m, int k, int n, int acc);
 
 /* ================================================================================================
  * 2. Decode-level session API (new surface; nothing in the reference plays this role — its decode

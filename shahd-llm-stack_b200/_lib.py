@@ -62,6 +62,7 @@ SIGNATURES = {
     "ShahdSetProgrammaticLaunch": (None, [ctypes.c_int]),
     "ShahdSetDecodeChains": (None, [ctypes.c_int]),
     "ShahdMatMulNTBF16Device": (ctypes.c_int, [_vp, _vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, _vp]),
+    "ShahdMatMulNTF32NoAlloc": (ctypes.c_int, [_fp, _fp, _fp, _i32, _i32, _i32, _i32]),
     "shahd_param_count": (_i64, [ctypes.POINTER(ShahdModelCfg)]),
     "shahd_init_params": (ctypes.c_int, [ctypes.POINTER(ShahdModelCfg), _u32, _fp, _i64]),
     "shahd_session_create": (ctypes.c_int, [ctypes.POINTER(ShahdModelCfg), _vp, _i32, _i64,
