@@ -163,8 +163,12 @@ int shahd_step(ShahdSession* s, const int32_t* slots, const int32_t* tokens, int
                int32_t* next_ids);
 
 /* CachedGenerate (CachedForward.ts:153-171) for n independent sequences, slots 0..n-1 (reset first).
- * prompts packed with offsets (n+1 entries); out_ids receives [n, max_new] new ids; rng_states [n]
- * (SeededRng states, one per sequence; read and written back; unused when greedy). */
+ * prompts packed with offsets (n+1 entries); out_ids receives [n, max_new] new ids.
+ * opts NULL or temperature <= 0: greedy (first index of the max). temperature > 0: SampleFromLogits
+ * (Sampler.ts:16-27) on the device — temperature softmax, top-k, top-p over the renormalized top-k
+ * mass, one SeededRng draw per new token, inverse CDF in index order (Distribution.ts:35-104).
+ * rng_states [n]: SeededRng.GetState() of each sequence's sampling stream; required when
+ * temperature > 0, read at entry and written back advanced by max_new draws; unused when greedy. */
 int shahd_generate(ShahdSession* s, const int32_t* prompts, const int32_t* offsets, int32_t n, int32_t max_new,
                    const ShahdSampling* opts, uint32_t* rng_states, int32_t* out_ids);
 
@@ -190,6 +194,13 @@ int shahd_profile(ShahdSession* s, int32_t enable);
  * LM head), 2 = embed/finish. total_ms sums the launches' event times; bytes sums their algorithmic
  * bytes (weights once + activations + KV rows read). */
 int shahd_profile_read(ShahdSession* s, int32_t kind, double* total_ms, int64_t* launches, double* bytes);
+
+/* SampleFromLogits (Sampler.ts:16-27) for `rows` independent logits rows on the current device: the
+ * sampler of shahd_generate applied to caller logits [rows, vocab] (host, f32). opts NULL or
+ * temperature <= 0: first index of the max, rng_states unused; else rng_states [rows] are read and
+ * written back advanced by one draw each. out_ids [rows]. Synchronous. */
+int shahd_sample_logits(const float* logits, int32_t rows, int32_t vocab, const ShahdSampling* opts,
+                        uint32_t* rng_states, int32_t* out_ids);
 
 const char* shahd_last_error(void);
 

@@ -10,7 +10,8 @@ Import with importlib (the directory name has dashes): importlib.import_module("
 """
 from . import _lib, backend, build, configs, decode  # noqa: F401
 from .backend import GpuBackend  # noqa: F401
-from .decode import GREEDY, CachedDecoder, ModelConfig, Sampling, Session, cached_generate, init_params  # noqa: F401
+from .decode import (  # noqa: F401
+    GREEDY, CachedDecoder, ModelConfig, Sampling, Session, cached_generate, init_params, sample_from_logits)
 
 
 def load():

@@ -79,6 +79,7 @@ SIGNATURES = {
     "shahd_kernel_launches": (_i64, [_vp]),
     "shahd_profile": (ctypes.c_int, [_vp, _i32]),
     "shahd_profile_read": (ctypes.c_int, [_vp, _i32, _dp, ctypes.POINTER(_i64), _dp]),
+    "shahd_sample_logits": (ctypes.c_int, [_fp, _i32, _i32, ctypes.POINTER(ShahdSampling), _up, _ip]),
     "shahd_last_error": (ctypes.c_char_p, []),
 }
 

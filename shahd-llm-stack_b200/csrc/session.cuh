@@ -19,6 +19,7 @@
 #include "../../include/shahd_b200.h"
 #include "decode_kernels.cuh"
 #include "params.h"
+#include "sampling.cuh"
 #include "umma_linear.cuh"
 
 namespace shahd {
@@ -35,9 +36,12 @@ struct GraphKey {
   const void *slot, *tok, *poff, *prompt, *out;
   int out_ld;
   int min_rows;
+  double temperature, top_p;  // sampling knobs baked into the sampler launch (temperature 0 = greedy)
+  int top_k;
   bool operator<(const GraphKey& o) const {
-    return std::tie(kind, M, slot, tok, poff, prompt, out, out_ld, min_rows) <
-           std::tie(o.kind, o.M, o.slot, o.tok, o.poff, o.prompt, o.out, o.out_ld, o.min_rows);
+    return std::tie(kind, M, slot, tok, poff, prompt, out, out_ld, min_rows, temperature, top_p, top_k) <
+           std::tie(o.kind, o.M, o.slot, o.tok, o.poff, o.prompt, o.out, o.out_ld, o.min_rows, o.temperature, o.top_p,
+                    o.top_k);
   }
 };
 
@@ -87,6 +91,8 @@ struct ShahdSession {
   float *part_o, *part_m, *part_l;
   int* attn_counter;
   int *d_slot, *d_tok, *d_pos, *d_next, *d_gen_count, *d_ends, *d_starts, *d_full_len, *d_rows;
+  uint32_t* d_rng;  // [max_seqs] SeededRng state per slot while a stochastic generate runs
+  int* d_sampled;   // [max_seqs] ids the sampler chose this step
   int *d_seq_plan;                              // [4][max_seqs]: prefill slot, context start, length, row offset
   int *d_row_slot, *d_row_pos, *d_row_poff;     // [rows_cap] expanded prefill rows
   int* d_prompt = nullptr;
@@ -203,6 +209,7 @@ struct StepPlan {
   int* out_ids;      // device [M, out_ld] or nullptr
   int out_ld;
   long long attended;  // sum over rows of (position + 1): cached positions the attention reads
+  ShahdSampling sampling;  // temperature > 0: seeded sampling from `logits` instead of the greedy argmax
 };
 
 // ---- measurement hooks: kernel classes timed with CUDA events on the launching stream ---------------
@@ -324,9 +331,18 @@ int EnqueueStep(ShahdSession* s, const StepPlan& p, cudaStream_t st, int r0 = 0)
     Timed(s, st, kProfLinear, LinearBytes(M, s->E, s->Ep, s->V),
           [&] { LaunchLinear(norm, lh, EpiLogits{p.logits, s->head_bias}, st); });
   }
+  int* sampled = nullptr;
+  if (p.head && p.finish && p.sampling.temperature > 0) {
+    // SampleFromLogits with Temperature > 0 (Sampler.ts:16-27): one CTA per row over its logits
+    sampled = s->d_sampled + rd;
+    const SampleArgs sa{p.logits, s->V, p.slot, s->d_rng, (float)p.sampling.temperature, p.sampling.top_k,
+                        p.sampling.top_p, sampled};
+    Timed(s, st, kProfOther, 4.0 * M * s->V,
+          [&] { LaunchPdl(SampleKernel, dim3(M), dim3(kSampleThreads), 0, st, sa); });
+  }
   if (p.finish) {
     FinishArgs f{M, p.slot, pos, s->d_seq_len, p.head ? am_val : nullptr, am_idx, nblk, p.next_ids,
-                 p.cur_tok, p.out_ids, p.out_ld, gen_count, nullptr};
+                 p.cur_tok, p.out_ids, p.out_ld, gen_count, sampled};
     Timed(s, st, kProfOther, 16.0 * M, [&] { LaunchPdl(FinishKernel, dim3(CeilDiv(M, 4)), dim3(128), 0, st, f); });
   }
   return (int)(s->launches - before);
@@ -390,7 +406,8 @@ int RunStep(ShahdSession* s, const StepPlan* plans, const int* r0, int nchain, i
   }
   const StepPlan& p = plans[0];
   GraphKey key{kind * 16 + nchain, p.M, p.slot, p.tok, p.poff, p.prompt, p.out_ids, p.out_ld,
-               g_umma_min_rows * 2 + (int)g_use_pdl};
+               g_umma_min_rows * 2 + (int)g_use_pdl, p.sampling.temperature > 0 ? p.sampling.temperature : 0.0,
+               p.sampling.temperature > 0 ? p.sampling.top_p : 1.0, p.sampling.temperature > 0 ? p.sampling.top_k : 0};
   auto it = s->graphs.find(key);
   if (it == s->graphs.end()) {
     EnqueueChains(s, plans, r0, nchain);
@@ -611,10 +628,7 @@ int GrowOut(ShahdSession* s, size_t count) {
 // prompts on the device; offs their host offsets. Output ids land in d_out [n, max_new].
 int GenerateCore(ShahdSession* s, const int* d_prompt_packed, const std::vector<int>& offs, int n, int max_new,
                  const ShahdSampling* o, int* d_out) {
-  if (o && o->temperature > 0) {
-    SetError("shahd_generate: stochastic sampling (temperature > 0) is not supported by this build");
-    return SHAHD_EINVAL;
-  }
+  const bool sample = o && o->temperature > 0;
   const int C = s->C;
   // CachedDecoder constructor: Context = prompt.slice(-BlockSize); prefill all but its last id.
   std::vector<int> plen(n), pstart(n), full_len(n), slots(n);
@@ -657,6 +671,10 @@ int GenerateCore(ShahdSession* s, const int* d_prompt_packed, const std::vector<
     const int rows = (c + 1) * n / nchain - r0[c];
     plans[c] = StepPlan{rows, nullptr, true, s->d_slot + r0[c], s->d_tok + r0[c], nullptr, nullptr, true, nullptr,
                         nullptr, s->d_tok + r0[c], d_out + (size_t)r0[c] * max_new, max_new, 0};
+    if (sample) {
+      plans[c].logits = s->logits + (size_t)r0[c] * s->V;  // the sampler reads the head's logits
+      plans[c].sampling = *o;
+    }
   }
   for (int k = 0; k < max_new; k++) {
     // rows whose window is full rebuild it from their last C-1 ids first (CachedForward.ts:135-141)
@@ -877,6 +895,7 @@ extern "C" int shahd_session_create(const ShahdModelCfg* cfg, const void* params
       (rc = DevAlloc(s, &s->d_starts, (size_t)R)) != SHAHD_OK ||
       (rc = DevAlloc(s, &s->d_full_len, (size_t)R)) != SHAHD_OK ||
       (rc = DevAlloc(s, &s->d_rows, (size_t)R)) != SHAHD_OK ||
+      (rc = DevAlloc(s, &s->d_rng, (size_t)R)) != SHAHD_OK || (rc = DevAlloc(s, &s->d_sampled, (size_t)R)) != SHAHD_OK ||
       (rc = DevAlloc(s, &s->d_seq_plan, (size_t)4 * R)) != SHAHD_OK ||
       (rc = DevAlloc(s, &s->d_row_slot, (size_t)s->rows_cap)) != SHAHD_OK ||
       (rc = DevAlloc(s, &s->d_row_pos, (size_t)s->rows_cap)) != SHAHD_OK ||
@@ -1057,6 +1076,24 @@ static int ValidateGenerate(ShahdSession* s, const int32_t* offsets, int32_t n, 
   return SHAHD_OK;
 }
 
+// Seeded sampling needs one SeededRng state per sequence and knobs the sampler can honour.
+int ValidateSampling(ShahdSession* s, const ShahdSampling* o, const void* rng, const char* op) {
+  if (!o || !(o->temperature > 0)) return SHAHD_OK;  // greedy (Temperature <= 0) draws nothing
+  if (!std::isfinite(o->temperature) || std::isnan(o->top_p)) {
+    SetError("%s: sampling temperature must be finite and top_p a number", op);
+    return SHAHD_EINVAL;
+  }
+  if (!rng) {
+    SetError("%s: temperature > 0 needs one SeededRng state per sequence (rng_states is null)", op);
+    return SHAHD_EINVAL;
+  }
+  if (s->V > (1 << 22)) {
+    SetError("%s: seeded sampling supports vocabularies up to %d ids, got %d", op, 1 << 22, s->V);
+    return SHAHD_EINVAL;
+  }
+  return SHAHD_OK;
+}
+
 extern "C" int shahd_generate(ShahdSession* s, const int32_t* prompts, const int32_t* offsets, int32_t n, int32_t max_new,
                               const ShahdSampling* opts, uint32_t* rng_states, int32_t* out_ids) {
   ClearError();
@@ -1069,16 +1106,25 @@ extern "C" int shahd_generate(ShahdSession* s, const int32_t* prompts, const int
   SHAHD_TRY(ValidateGenerate(s, offsets, n, max_new));
   const size_t total = offsets[n];
   SHAHD_TRY(ValidateIds(s, prompts, total, "CachedGenerate"));
+  SHAHD_TRY(ValidateSampling(s, opts, rng_states, "shahd_generate"));
   if (max_new == 0) return SHAHD_OK;  // CachedGenerate returns the prompt untouched, no prefill
+  const bool sample = opts && opts->temperature > 0;
   std::vector<int> offs(offsets, offsets + n + 1);
   SHAHD_CUDA_TRY(cudaStreamSynchronize(s->stream));
   SHAHD_TRY(GrowPrompt(s, total));
   SHAHD_TRY(GrowOut(s, (size_t)n * max_new));
   SHAHD_CUDA_TRY(cudaMemcpyAsync(s->d_prompt, prompts, sizeof(int) * total, cudaMemcpyHostToDevice, s->stream));
+  uint32_t* h_rng = reinterpret_cast<uint32_t*>(Staging(s, 0));  // staging row 0: free during a generate
+  if (sample) {
+    std::memcpy(h_rng, rng_states, sizeof(uint32_t) * n);
+    SHAHD_CUDA_TRY(cudaMemcpyAsync(s->d_rng, h_rng, sizeof(uint32_t) * n, cudaMemcpyHostToDevice, s->stream));
+  }
   SHAHD_TRY(GenerateCore(s, s->d_prompt, offs, n, max_new, opts, s->d_out));
   SHAHD_CUDA_TRY(cudaMemcpyAsync(out_ids, s->d_out, sizeof(int) * (size_t)n * max_new, cudaMemcpyDeviceToHost, s->stream));
+  if (sample)
+    SHAHD_CUDA_TRY(cudaMemcpyAsync(h_rng, s->d_rng, sizeof(uint32_t) * n, cudaMemcpyDeviceToHost, s->stream));
   SHAHD_CUDA_TRY(cudaStreamSynchronize(s->stream));
-  (void)rng_states;
+  if (sample) std::memcpy(rng_states, h_rng, sizeof(uint32_t) * n);  // states advanced by one draw per token
   return SHAHD_OK;
 }
 
@@ -1093,12 +1139,23 @@ extern "C" int shahd_generate_device(ShahdSession* s, const int32_t* d_prompts, 
   std::lock_guard<std::mutex> g(s->mu);
   cudaSetDevice(s->device);
   SHAHD_TRY(ValidateGenerate(s, host_offsets, n, max_new));
+  SHAHD_TRY(ValidateSampling(s, opts, d_rng_states, "shahd_generate_device"));
   if (max_new == 0) return SHAHD_OK;
+  const bool sample = opts && opts->temperature > 0;
   std::vector<int> offs(host_offsets, host_offsets + n + 1);
   cudaStream_t caller = stream ? static_cast<cudaStream_t>(stream) : s->stream;
-  (void)d_rng_states;
   JoinIn(s, caller);
-  const int rc = GenerateCore(s, d_prompts, offs, n, max_new, opts, d_out_ids);
+  if (sample)
+    SHAHD_CUDA_TRY(cudaMemcpyAsync(s->d_rng, d_rng_states, sizeof(uint32_t) * n, cudaMemcpyDeviceToDevice, s->stream));
+  int rc = GenerateCore(s, d_prompts, offs, n, max_new, opts, d_out_ids);
+  if (rc == SHAHD_OK && sample) {
+    const cudaError_t e =
+        cudaMemcpyAsync(d_rng_states, s->d_rng, sizeof(uint32_t) * n, cudaMemcpyDeviceToDevice, s->stream);
+    if (e != cudaSuccess) {
+      SetError("shahd_generate_device: copying the RNG states back failed: %s", cudaGetErrorString(e));
+      rc = SHAHD_ECUDA;
+    }
+  }
   JoinOut(s, caller);
   return rc;
 }
@@ -1156,5 +1213,64 @@ extern "C" int shahd_profile_read(ShahdSession* s, int32_t kind, double* total_m
 }
 
 extern "C" int64_t shahd_kernel_launches(ShahdSession* s) { return s ? (int64_t)s->launches : -1; }
+
+extern "C" int shahd_sample_logits(const float* logits, int32_t rows, int32_t vocab, const ShahdSampling* opts,
+                                   uint32_t* rng_states, int32_t* out_ids) {
+  const char* op = "shahd_sample_logits";
+  ClearError();
+  if (!logits || !out_ids || rows < 1 || vocab < 1) {
+    SetError("%s: need logits and out_ids and rows, vocab >= 1 (got rows=%d vocab=%d)", op, rows, vocab);
+    return SHAHD_EINVAL;
+  }
+  const bool sample = opts && opts->temperature > 0;
+  if (sample) {
+    if (!std::isfinite(opts->temperature) || std::isnan(opts->top_p) || !rng_states) {
+      SetError("%s: temperature > 0 needs a finite temperature, a numeric top_p and rng_states", op);
+      return SHAHD_EINVAL;
+    }
+    if (vocab > (1 << 22)) {
+      SetError("%s: seeded sampling supports vocabularies up to %d ids, got %d", op, 1 << 22, vocab);
+      return SHAHD_EINVAL;
+    }
+  }
+  if (!DeviceOk()) {
+    SetError("%s: no usable sm_100 device", op);
+    return SHAHD_ENODEV;
+  }
+  int dev = 0;
+  SHAHD_CUDA_TRY(cudaGetDevice(&dev));
+  Workspace& w = WorkspaceFor(dev);
+  std::lock_guard<std::mutex> g(w.mu);
+  // [rows, vocab] f32 logits | rows rng states | rows ids | rows slots, each 256-byte aligned
+  const auto align256 = [](size_t b) { return (b + 255) / 256 * 256; };
+  const size_t nl = align256((size_t)rows * vocab * 4), nr = align256((size_t)rows * 4);
+  const size_t need = nl + 3 * nr;
+  if (w.cap < need) {
+    if (w.buf) cudaFree(w.buf);
+    w.buf = nullptr;
+    w.cap = 0;
+    SHAHD_CUDA_TRY(cudaMalloc(&w.buf, need));
+    w.cap = need;
+  }
+  if (!w.stream) SHAHD_CUDA_TRY(cudaStreamCreateWithFlags(&w.stream, cudaStreamNonBlocking));
+  uint8_t* base = static_cast<uint8_t*>(w.buf);
+  float* d_logits = reinterpret_cast<float*>(base);
+  uint32_t* d_rng = reinterpret_cast<uint32_t*>(base + nl);
+  int* d_ids = reinterpret_cast<int*>(base + nl + nr);
+  int* d_slot = reinterpret_cast<int*>(base + nl + 2 * nr);
+  std::vector<int> slots(rows);
+  std::iota(slots.begin(), slots.end(), 0);
+  SHAHD_CUDA_TRY(cudaMemcpyAsync(d_logits, logits, (size_t)rows * vocab * 4, cudaMemcpyHostToDevice, w.stream));
+  SHAHD_CUDA_TRY(cudaMemcpyAsync(d_slot, slots.data(), (size_t)rows * 4, cudaMemcpyHostToDevice, w.stream));
+  if (sample) SHAHD_CUDA_TRY(cudaMemcpyAsync(d_rng, rng_states, (size_t)rows * 4, cudaMemcpyHostToDevice, w.stream));
+  const SampleArgs sa{d_logits, vocab, d_slot, d_rng, sample ? (float)opts->temperature : 0.f, sample ? opts->top_k : 0,
+                      sample ? opts->top_p : 1.0, d_ids};
+  SampleKernel<<<rows, kSampleThreads, 0, w.stream>>>(sa);
+  SHAHD_CUDA_TRY(cudaGetLastError());
+  SHAHD_CUDA_TRY(cudaMemcpyAsync(out_ids, d_ids, (size_t)rows * 4, cudaMemcpyDeviceToHost, w.stream));
+  if (sample) SHAHD_CUDA_TRY(cudaMemcpyAsync(rng_states, d_rng, (size_t)rows * 4, cudaMemcpyDeviceToHost, w.stream));
+  SHAHD_CUDA_TRY(cudaStreamSynchronize(w.stream));
+  return SHAHD_OK;
+}
 
 extern "C" const char* shahd_last_error(void) { return GetError(); }

@@ -167,7 +167,10 @@ class Session:
         return logits, nxt
 
     def generate(self, prompts, max_new: int, sampling: Sampling = GREEDY, rng_states=None) -> np.ndarray:
-        """CachedGenerate for each prompt (slots 0..n-1): returns the new ids [n, max_new]."""
+        """CachedGenerate for each prompt (slots 0..n-1): returns the new ids [n, max_new].
+
+        With sampling.temperature > 0, rng_states (uint32 [n], one SeededRng state per sequence) is
+        required; a uint32 array is advanced in place, as the reference's Rng object is."""
         flat, offs = _pack(prompts)
         n = offs.size - 1
         out = np.zeros((n, max(max_new, 0)), dtype=np.int32)
@@ -175,6 +178,8 @@ class Session:
         o = sampling.to_c()
         _lib.check(self.lib.shahd_generate(self.handle, flat.ctypes.data_as(_ip), offs.ctypes.data_as(_ip), n, max_new,
                                            ctypes.byref(o), st.ctypes.data_as(_up), out.ctypes.data_as(_ip)))
+        if isinstance(rng_states, np.ndarray) and st is not rng_states:
+            rng_states[...] = st  # SeededRng.SetState: the streams advanced by one draw per sampled token
         return out
 
     def generate_device(self, d_prompts: int, host_offsets: np.ndarray, max_new: int, d_out: int,
@@ -239,6 +244,26 @@ class CachedDecoder:
             self.s.prefill([self.slot], [keep])
             self.window = list(keep)
         self.logits = self._step(int(token))
+
+
+def sample_from_logits(logits, sampling: Sampling = GREEDY, rng_states=None) -> np.ndarray:
+    """SampleFromLogits (Sampler.ts:16-27) for each row of logits [rows, vocab] on the GPU.
+
+    With sampling.temperature > 0, rng_states (uint32 [rows]) is required and advanced in place by one
+    draw per row. Returns the chosen ids [rows]."""
+    lg = np.ascontiguousarray(logits, dtype=np.float32)
+    if lg.ndim == 1:
+        lg = lg[None, :]
+    rows, vocab = lg.shape
+    out = np.zeros(rows, dtype=np.int32)
+    st = None if rng_states is None else np.ascontiguousarray(rng_states, dtype=np.uint32)
+    o = sampling.to_c()
+    lib = _lib.load()
+    _lib.check(lib.shahd_sample_logits(lg.ctypes.data_as(_fp), rows, vocab, ctypes.byref(o),
+                                       st.ctypes.data_as(_up) if st is not None else None, out.ctypes.data_as(_ip)))
+    if isinstance(rng_states, np.ndarray) and st is not rng_states:
+        rng_states[...] = st
+    return out
 
 
 def cached_generate(session: Session, prompt_ids, max_new: int, sampling: Sampling = GREEDY, rng_state: int = 1):

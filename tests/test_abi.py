@@ -119,3 +119,9 @@ def test_no_device_is_an_error_not_a_fallback():
     assert e.value.code == pkg._lib.SHAHD_ENODEV
     with pytest.raises(RuntimeError, match="sm_100"):
         pkg.GpuBackend()
+    # the batch sampler checks its arguments, then refuses without a device
+    with pytest.raises(pkg._lib.ShahdError) as e:
+        pkg.sample_from_logits(np.zeros((2, 8), np.float32), pkg.GREEDY)
+    assert e.value.code == pkg._lib.SHAHD_ENODEV
+    with pytest.raises(pkg._lib.ShahdError, match="rng_states"):
+        pkg.sample_from_logits(np.zeros((2, 8), np.float32), pkg.Sampling(1.0, 0, 1.0), None)
