@@ -64,7 +64,7 @@ const char* ShahdLastError(void);
 /* Row count from which decode projections use tcgen05 tiles instead of the SIMT kernel (default 17;
  * 1 forces tensor cores everywhere). Process-wide tuning/test hook; no counterpart in the reference. */
 void ShahdSetTensorCoreMinRows(int rows);
-/* Programmatic dependent launch between the kernels of a step (default 0): each kernel is scheduled
+/* Programmatic dependent launch between the kernels of a step (default 1): each kernel is scheduled
  * while its predecessor drains and overlaps its setup and weight loads. Process-wide; no counterpart in
  * the reference. */
 void ShahdSetProgrammaticLaunch(int enable);

@@ -97,6 +97,9 @@ __device__ __forceinline__ void ArgmaxMerge(float& bv, int& bi, float v, int i) 
 __device__ __forceinline__ void GridDepWait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 // Allow the dependent grid to be scheduled; it still waits for this grid's completion in GridDepWait.
 __device__ __forceinline__ void GridDepLaunch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+// Orders this thread's later async-proxy reads (TMA, bulk copies) after generic-proxy writes it may now
+// observe, such as a predecessor grid's stores seen through GridDepWait.
+__device__ __forceinline__ void FenceProxyAsyncGlobal() { asm volatile("fence.proxy.async.global;" ::: "memory"); }
 
 // ---- shared-memory address, mbarrier, TMA, tcgen05 (inline PTX, sm_100a) -------------------------
 

@@ -60,9 +60,46 @@ __device__ __forceinline__ void StoreBf16x2(bf16* p, float a, float b) {
   *reinterpret_cast<__nv_bfloat162*>(p) = __floats2bfloat162_rn(a, b);
 }
 
+// 16 consecutive floats / bf16 to and from memory in 16-byte pieces (callers check alignment).
+__device__ __forceinline__ void Load16f(const float* p, float (&v)[16]) {
+#pragma unroll
+  for (int i = 0; i < 4; i++) {
+    const float4 t = reinterpret_cast<const float4*>(p)[i];
+    v[4 * i] = t.x;
+    v[4 * i + 1] = t.y;
+    v[4 * i + 2] = t.z;
+    v[4 * i + 3] = t.w;
+  }
+}
+template <int N>
+__device__ __forceinline__ void StoreNf(float* p, const float* v) {
+#pragma unroll
+  for (int i = 0; i < N / 4; i++)
+    reinterpret_cast<float4*>(p)[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+}
+template <int N>
+__device__ __forceinline__ void StoreNbf(bf16* p, const float* v) {
+#pragma unroll
+  for (int i = 0; i < N / 8; i++) {
+    uint4 u;
+    uint32_t* w = reinterpret_cast<uint32_t*>(&u);
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+      const __nv_bfloat162 h = __floats2bfloat162_rn(v[8 * i + 2 * j], v[8 * i + 2 * j + 1]);
+      w[j] = *reinterpret_cast<const uint32_t*>(&h);
+    }
+    reinterpret_cast<uint4*>(p)[i] = u;
+  }
+}
+
 // ---- epilogues: apply(m, n, v0, v1) gets the final values of output columns n and n+1 (n even) of row
 // m (norm already applied). Pairs keep RoPE's interleaved (2i, 2i+1) rotation (RotaryEmbedding.ts:42-60)
 // and the gate/up columns of the interleaved W1|W3 layout in one thread.
+//
+// The tensor-core kernel also has a 16-column form for a chunk n..n+15 (n a multiple of 16) when
+// vec_ok(N): load16 issues every global read the chunk needs (residual, bias, RoPE table, KV page lookup)
+// and can run before the accumulator is ready; store16 then only computes and writes, with 16-byte
+// stores. Reads never depend on this launch's own writes, so no load waits behind a store.
 
 // Q/K/V projection: RoPE on q and k at the row's position, q to fp32 scratch, k/v appended to the cache.
 struct EpiQKV {
@@ -94,6 +131,53 @@ struct EpiQKV {
     if (off < 0) return;
     StoreBf16x2(kv.pool + off + j, v0, v1);
   }
+  struct Pre {
+    float c[8], s[8];
+    float* qdst;  // q row chunk, or nullptr for k/v
+    bf16* kvdst;  // KV page row chunk, or nullptr (q, or no page)
+  };
+  __device__ __forceinline__ bool vec_ok(int N) const { return d % 16 == 0 && (H * d) % 4 == 0; }
+  __device__ __forceinline__ Pre load16(int m, int n) const {
+    Pre pr;
+    const int hd = H * d, j = n % d, p = pos[m];
+    const bool rope = n < hd + Hk * d && rope_cos != nullptr;
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+      pr.c[i] = 1.f;
+      pr.s[i] = 0.f;
+    }
+    if (rope) {
+      const float* cp = rope_cos + p * (d >> 1) + (j >> 1);
+      const float* sp = rope_sin + p * (d >> 1) + (j >> 1);
+#pragma unroll
+      for (int i = 0; i < 2; i++) {
+        const float4 c4 = reinterpret_cast<const float4*>(cp)[i], s4 = reinterpret_cast<const float4*>(sp)[i];
+        pr.c[4 * i] = c4.x; pr.c[4 * i + 1] = c4.y; pr.c[4 * i + 2] = c4.z; pr.c[4 * i + 3] = c4.w;
+        pr.s[4 * i] = s4.x; pr.s[4 * i + 1] = s4.y; pr.s[4 * i + 2] = s4.z; pr.s[4 * i + 3] = s4.w;
+      }
+    }
+    pr.qdst = nullptr;
+    pr.kvdst = nullptr;
+    if (n < hd) {
+      pr.qdst = q + (size_t)m * hd + n;
+    } else {
+      const int kvsel = n < hd + Hk * d ? 0 : 1;
+      const int g = (n - hd - kvsel * Hk * d) / d;
+      const long long off = kv.Offset(slot[m], p, layer, g, kvsel);
+      if (off >= 0) pr.kvdst = kv.pool + off + j;
+    }
+    return pr;
+  }
+  __device__ __forceinline__ void store16(int m, int n, float (&v)[16], const Pre& pr) const {
+#pragma unroll
+    for (int i = 0; i < 8; i++) {  // identity rotation (c = 1, s = 0) where RoPE does not apply
+      const float a = v[2 * i], b = v[2 * i + 1];
+      v[2 * i] = a * pr.c[i] - b * pr.s[i];
+      v[2 * i + 1] = a * pr.s[i] + b * pr.c[i];
+    }
+    if (pr.qdst) StoreNf<16>(pr.qdst, v);
+    else if (pr.kvdst) StoreNbf<16>(pr.kvdst, v);
+  }
 };
 
 // Residual update x += v (+ bias), bf16 copy refreshed: the attention output projection (summed
@@ -118,6 +202,27 @@ struct EpiResid {
     }
     StoreBf16x2(xb + (size_t)m * ldxb + n, a, b);
   }
+  struct Pre {
+    float x[16];  // residual (+ bias)
+  };
+  __device__ __forceinline__ bool vec_ok(int N) const { return ldx % 4 == 0 && ldxb % 8 == 0; }
+  __device__ __forceinline__ Pre load16(int m, int n) const {
+    Pre pr;
+    Load16f(x + (size_t)m * ldx + n, pr.x);
+    if (bias) {
+      float b[16];
+      Load16f(bias + n, b);
+#pragma unroll
+      for (int i = 0; i < 16; i++) pr.x[i] += b[i];
+    }
+    return pr;
+  }
+  __device__ __forceinline__ void store16(int m, int n, float (&v)[16], const Pre& pr) const {
+#pragma unroll
+    for (int i = 0; i < 16; i++) v[i] += pr.x[i];
+    StoreNf<16>(x + (size_t)m * ldx + n, v);
+    StoreNbf<16>(xb + (size_t)m * ldxb + n, v);
+  }
 };
 
 // Gated MLP hidden: act[j] = Act(x·W1[:,j]) * (x·W3[:,j]) with W1/W3 interleaved per column pair
@@ -138,6 +243,26 @@ struct EpiGated {
     const float h = a * u;
     act[(size_t)m * F + (n >> 1)] = h;
     actb[(size_t)m * ldb + (n >> 1)] = __float2bfloat16_rn(h);
+  }
+  struct Pre {};
+  __device__ __forceinline__ bool vec_ok(int N) const { return F % 4 == 0 && ldb % 8 == 0; }
+  __device__ __forceinline__ Pre load16(int, int) const { return Pre{}; }
+  __device__ __forceinline__ void store16(int m, int n, float (&v)[16], const Pre&) const {
+    float h[8];
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+      const float g = v[2 * i], u = v[2 * i + 1];
+      float a;
+      if (gelu) {
+        const float c = 0.7978845608028654f;  // sqrt(2/pi)
+        a = 0.5f * g * (1.0f + tanhf(c * (g + 0.044715f * g * g * g)));
+      } else {
+        a = g * (1.0f / (1.0f + __expf(-g)));
+      }
+      h[i] = a * u;
+    }
+    StoreNf<8>(act + (size_t)m * F + (n >> 1), h);
+    StoreNbf<8>(actb + (size_t)m * ldb + (n >> 1), h);
   }
 };
 
@@ -161,6 +286,24 @@ struct EpiReluFc {
     }
     StoreBf16x2(actb + (size_t)m * ldb + n, v0, v1);
   }
+  struct Pre {
+    float b[16];
+  };
+  __device__ __forceinline__ bool vec_ok(int N) const { return F % 4 == 0 && ldb % 8 == 0; }
+  __device__ __forceinline__ Pre load16(int, int n) const {
+    Pre pr;
+    Load16f(bias + n, pr.b);
+    return pr;
+  }
+  __device__ __forceinline__ void store16(int m, int n, float (&v)[16], const Pre& pr) const {
+#pragma unroll
+    for (int i = 0; i < 16; i++) {
+      const float t = v[i] + pr.b[i];
+      v[i] = t > 0.f ? t : 0.f;
+    }
+    StoreNf<16>(act + (size_t)m * F + n, v);
+    StoreNbf<16>(actb + (size_t)m * ldb + n, v);
+  }
 };
 
 // LM head: logits = xf·Wteᵀ + bias (HeadLogitsRow, CachedRowMath.ts:117-137); also feeds argmax.
@@ -175,6 +318,22 @@ struct EpiLogits {
       p[0] = v0;
       if (n + 1 < N) p[1] = v1;
     }
+  }
+  int V;  // row stride of logits (= N of the head launch)
+  struct Pre {
+    float b[16];
+  };
+  __device__ __forceinline__ bool vec_ok(int N) const { return N % 4 == 0; }
+  __device__ __forceinline__ Pre load16(int, int n) const {
+    Pre pr;
+    Load16f(bias + n, pr.b);
+    return pr;
+  }
+  // adds the bias in place, so the caller's argmax sees the final logits
+  __device__ __forceinline__ void store16(int m, int n, float (&v)[16], const Pre& pr) const {
+#pragma unroll
+    for (int i = 0; i < 16; i++) v[i] += pr.b[i];
+    if (logits) StoreNf<16>(logits + (size_t)m * V + n, v);
   }
 };
 
@@ -529,8 +688,10 @@ __global__ void __launch_bounds__(kAttnThreads) AttnDecodeKernel(AttnArgs aa) {
     BulkCopyG2S(ring + (size_t)b * 2 * PAGE, kb, bytes, &bar[b]);
     BulkCopyG2S(ring + (size_t)b * 2 * PAGE + PAGE, vb, bytes, &bar[b]);
   };
-  if (threadIdx.x == 0)
+  if (threadIdx.x == 0) {
+    FenceProxyAsyncGlobal();
     for (int pg = pb; pg < pe && pg < pb + kAttnRing; pg++) issue(pg, (pg - pb) % kAttnRing);
+  }
 
   float o[kMaxGroup][JPL];
 #pragma unroll

@@ -12,7 +12,7 @@
 namespace shahd {
 
 int g_umma_min_rows = 17;
-bool g_use_pdl = false;
+bool g_use_pdl = true;
 int g_decode_chains = 0;  // 0 = automatic
 
 // ---- thread-local last error --------------------------------------------------------------------

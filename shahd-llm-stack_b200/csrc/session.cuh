@@ -122,9 +122,11 @@ namespace shahd {
 namespace {
 
 // Pinned staging rows (each max_seqs ints). A row is rewritten only after the stream has drained the
-// copies that read it: 0-1 per-call slots/tokens, 2-5 generate plan, 6 window-rebuild rows,
+// copies that read it, so no two uses between two stream synchronizations may share a row:
+// 0-1 per-call slots/tokens (or a generate's RNG states), 2-5 generate plan, 6 window-rebuild rows,
 // 7 lengths, 8-11 the prefill plan.
 constexpr int kStagingRows = 12;
+constexpr int kStagingLengths = 7;
 constexpr int kPrefillRows = 8192;  // rows of one batched prefill chunk (whole sequences per chunk)
 constexpr int kMaxChains = 8;
 
@@ -329,7 +331,7 @@ int EnqueueStep(ShahdSession* s, const StepPlan& p, cudaStream_t st, int r0 = 0)
     const LinearArgs lh = Lin(x, s->E, xb, s->Ep, R, M, s->E, s->Ep, s->w_head, s->V, eps, s->head_c1, s->head_c2,
                               am_val, am_idx);
     Timed(s, st, kProfLinear, LinearBytes(M, s->E, s->Ep, s->V),
-          [&] { LaunchLinear(norm, lh, EpiLogits{p.logits, s->head_bias}, st); });
+          [&] { LaunchLinear(norm, lh, EpiLogits{p.logits, s->head_bias, s->V}, st); });
   }
   int* sampled = nullptr;
   if (p.head && p.finish && p.sampling.temperature > 0) {
@@ -487,7 +489,7 @@ int UploadTables(ShahdSession* s) {
 int* Staging(ShahdSession* s, int row) { return s->h_pinned_rows + (size_t)row * s->max_seqs; }
 
 int UploadLengths(ShahdSession* s) {
-  int* h = Staging(s, kStagingRows - 1);
+  int* h = Staging(s, kStagingLengths);  // not a prefill-plan row: that copy may still be pending
   std::copy(s->h_len.begin(), s->h_len.end(), h);
   SHAHD_CUDA_TRY(cudaMemcpyAsync(s->d_seq_len, h, sizeof(int) * s->max_seqs, cudaMemcpyHostToDevice, s->stream));
   return SHAHD_OK;

@@ -45,6 +45,11 @@ inline bool UmmaLinearSupported(const LinearArgs& la) { return la.Kp % 8 == 0 &&
 // Pipeline depth by tile width: narrow tiles keep a whole decode-sized K in flight.
 __host__ __device__ constexpr int UmmaStages(int BN) { return BN <= 32 ? 8 : (BN <= 64 ? 6 : 4); }
 
+// Rows of the activation tile fetched per stage: the 8-row multiple covering M (at most 128). The MMA
+// always reads 128 rows; the rows past the box hold stale shared memory and only feed accumulator rows
+// that are never stored.
+__host__ inline int UmmaBoxRows(int M) { return M >= kUmmaBM ? kUmmaBM : RoundUp(M, 8); }
+
 template <int BN>
 struct UmmaSmem {
   static constexpr int kStages = UmmaStages(BN);
@@ -123,9 +128,12 @@ inline void ForgetTmaRange(const void* lo, const void* hi) { (void)lo; (void)hi;
 template <int NORM, class Epi, int BN>
 __global__ void __launch_bounds__(kUmmaThreads, 1)
     LinearUmmaKernel(LinearArgs la, Epi epi, const __grid_constant__ CUtensorMap tmap_a,
-                     const __grid_constant__ CUtensorMap tmap_w) {
+                     const __grid_constant__ CUtensorMap tmap_w, int a_box_rows) {
   using L = UmmaSmem<BN>;
   constexpr int S = L::kStages;
+  constexpr int kChunks = BN / 16;
+  constexpr bool kEarly = BN <= 32;  // epilogue reads issued before the main loop (registers allow it)
+  const uint32_t stage_tx = (uint32_t)a_box_rows * kUmmaBK * 2 + (uint32_t)L::kB;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + S * L::kStage);
@@ -164,20 +172,31 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
   if (threadIdx.x == 0) {
     for (int kb = 0; kb < nk && kb < S; kb++) {
       uint8_t* sa = smem + kb * L::kStage;
-      MbarArriveExpectTx(&full[kb], L::kStage);
+      MbarArriveExpectTx(&full[kb], stage_tx);
       TmaLoad2D(sa + L::kA, &tmap_w, &full[kb], kb * kUmmaBK, n0);
     }
   }
   GridDepWait();
   GridDepLaunch();
   if (threadIdx.x == 0) {
+    FenceProxyAsyncGlobal();
     for (int kb = 0; kb < nk && kb < S; kb++) TmaLoad2D(smem + kb * L::kStage, &tmap_a, &full[kb], kb * kUmmaBK, m0);
+  }
+  const int r = warp * 32 + lane;
+  const bool row_ok = m0 + r < la.M;
+  const bool vec = epi.vec_ok(la.N);
+  // the epilogue's global reads (residual, bias, RoPE table, KV page lookup) overlap the main loop
+  typename Epi::Pre pre[kEarly ? kChunks : 1];
+  if (kEarly && vec && row_ok) {
+#pragma unroll
+    for (int ch = 0; ch < (kEarly ? kChunks : 1); ch++)
+      if (n0 + 16 * ch + 16 <= la.N) pre[ch] = epi.load16(m0 + r, n0 + 16 * ch);
   }
 
   // Main loop. Every thread waits for each stage and (for a norm) accumulates its own row's statistics
-  // from the staged bf16 tile; thread 0 issues the MMAs and refills the stage once the MMAs and the four
-  // warps are done with it.
-  const int r = warp * 32 + lane;
+  // from the staged bf16 tile; thread 0 issues the MMAs of a stage and then refills the stage of the
+  // previous iteration once its MMAs and the four warps are done with it, so the tensor pipe always has
+  // the next stage's MMAs queued while thread 0 waits.
   float s1 = 0.f, s2 = 0.f;
   const uint32_t idesc = UmmaIdescBf16(kUmmaBM, BN);
   for (int kb = 0; kb < nk; kb++) {
@@ -212,15 +231,17 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
       for (int kk = 0; kk < kUmmaBK / 16; kk++)
         UmmaBf16(tmem, ad + (uint64_t)(kk * 2), bd + (uint64_t)(kk * 2), idesc, (kb > 0 || kk > 0) ? 1u : 0u);
       UmmaCommit(&empty[st]);
-      if (kb + S < nk) {
-        if (!MbarWaitBounded(&empty[st], ph, kWaitLimit)) {
+      const int kp = kb - 1;  // refill the previous iteration's stage with block kp + S
+      if (kp >= 0 && kp + S < nk) {
+        const int sp = kp % S;
+        if (!MbarWaitBounded(&empty[sp], (kp / S) & 1, kWaitLimit)) {
           atomicCAS(&g_shahd_device_error, 0, kDevErrUmmaTimeout);
           *s_abort = 1;
         } else {
-          const int kn = kb + S;
-          MbarArriveExpectTx(&full[st], L::kStage);
-          TmaLoad2D(sa, &tmap_a, &full[st], kn * kUmmaBK, m0);
-          TmaLoad2D(sa + L::kA, &tmap_w, &full[st], kn * kUmmaBK, n0);
+          uint8_t* sb = smem + sp * L::kStage;
+          MbarArriveExpectTx(&full[sp], stage_tx);
+          TmaLoad2D(sb, &tmap_a, &full[sp], (kp + S) * kUmmaBK, m0);
+          TmaLoad2D(sb + L::kA, &tmap_w, &full[sp], (kp + S) * kUmmaBK, n0);
         }
       }
     }
@@ -242,15 +263,39 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
   TcgenFenceAfter();
   if (!*s_abort) {
     // Epilogue: thread = row (m0 + 32*warp + lane), 16 consecutive accumulator columns per TMEM load.
-    const bool row_ok = m0 + r < la.M;
     float bv = -INFINITY;
     int bi = 0x7fffffff;
-#pragma unroll 1
-    for (int c = 0; c < BN; c += 16) {
+#pragma unroll
+    for (int ch = 0; ch < kChunks; ch++) {
+      const int c = 16 * ch;
       uint32_t u[16];
       TmemLoad16(tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)c, u);
       TmemWaitLd();
-      if (row_ok) {
+      if (row_ok && vec && n0 + c + 16 <= la.N) {
+        const int nb = n0 + c;
+        float v[16];
+#pragma unroll
+        for (int j = 0; j < 16; j++) v[j] = __uint_as_float(u[j]);
+        if (NORM == kNormRms) {
+#pragma unroll
+          for (int j = 0; j < 16; j++) v[j] *= is;
+        } else if (NORM == kNormLayer) {
+          float c1[16], c2[16];
+          Load16f(la.c1 + nb, c1);
+          Load16f(la.c2 + nb, c2);
+#pragma unroll
+          for (int j = 0; j < 16; j++) v[j] = is * (v[j] - mu * c1[j]) + c2[j];
+        }
+        if constexpr (kEarly) {
+          epi.store16(m0 + r, nb, v, pre[ch]);
+        } else {
+          epi.store16(m0 + r, nb, v, epi.load16(m0 + r, nb));
+        }
+        if constexpr (IsLogits<Epi>::value) {
+#pragma unroll
+          for (int j = 0; j < 16; j++) ArgmaxMerge(bv, bi, v[j], nb + j);
+        }
+      } else if (row_ok) {
 #pragma unroll
         for (int j = 0; j < 16; j += 2) {
           const int n = n0 + c + j;
@@ -288,7 +333,8 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
 template <int NORM, class Epi, int BN>
 void LaunchUmmaLinearBN(const LinearArgs& la, const Epi& epi, cudaStream_t st) {
   CUtensorMap tw, ta;
-  if (!MakeTmaBf16(la.w, la.N, la.Kp, la.Kp, BN, &tw) || !MakeTmaBf16(la.ab, la.a_rows, la.Kp, la.ldab, kUmmaBM, &ta))
+  const int box = UmmaBoxRows(la.M);
+  if (!MakeTmaBf16(la.w, la.N, la.Kp, la.Kp, BN, &tw) || !MakeTmaBf16(la.ab, la.a_rows, la.Kp, la.ldab, box, &ta))
     return;  // the missing launch surfaces through the caller's result checks
   static bool configured = false;
   if (!configured) {
@@ -297,7 +343,8 @@ void LaunchUmmaLinearBN(const LinearArgs& la, const Epi& epi, cudaStream_t st) {
     configured = true;
   }
   dim3 grid(CeilDiv(la.N, BN), CeilDiv(la.M, kUmmaBM));
-  LaunchPdl(LinearUmmaKernel<NORM, Epi, BN>, grid, dim3(kUmmaThreads), UmmaSmem<BN>::kBytes, st, la, epi, ta, tw);
+  LaunchPdl(LinearUmmaKernel<NORM, Epi, BN>, grid, dim3(kUmmaThreads), UmmaSmem<BN>::kBytes, st, la, epi, ta, tw,
+            box);
 }
 
 template <int NORM, class Epi>

@@ -176,11 +176,11 @@ def test_launch_modes_give_identical_ids():
     lib = pkg.load()
     with pkg.Session(cfg, p, max_seqs=8) as sess:
         a = sess.generate(prompts, 20)
-        lib.ShahdSetProgrammaticLaunch(1)
+        lib.ShahdSetProgrammaticLaunch(0)
         try:
             b = sess.generate(prompts, 20)
         finally:
-            lib.ShahdSetProgrammaticLaunch(0)
+            lib.ShahdSetProgrammaticLaunch(1)
     assert np.array_equal(a, b)
     assert lib.ShahdDeviceErrorFlag() == 0
 
@@ -218,8 +218,8 @@ def test_microchat_generate_spot_check_and_determinism():
     sess = pkg.Session(cfg, p, max_seqs=w.seqs)
     prompts = np.stack([O.uniform_ids(w.prompt_len, cfg.vocab_size, seed=1000 + i) for i in range(w.seqs)])
     out1 = sess.generate(prompts, 64)
-    out2 = sess.generate(prompts, 64)
-    assert np.array_equal(out1, out2)  # deterministic run to run
+    for _ in range(4):  # deterministic run to run (host staging rows and prefill plans do not race)
+        assert np.array_equal(out1, sess.generate(prompts, 64))
     model = O.Model(oracle_shape(cfg, "F32"), p.astype(np.float64))
     for i in (0, 37):
         odec = O.Decoder(model, prompts[i])
