@@ -364,6 +364,8 @@ struct LinearArgs {
   const float* c2;  // LayerNorm: sum_k beta[k] W[n,k]
   float* am_val;    // argmax partials [M, gridDim.x] (logits only)
   int* am_idx;
+  float* ws;        // split-K partial tiles (tensor-core path, no norm), or nullptr: no split
+  int* ws_cnt;      // [N tiles] arrival counters, zero between launches
 };
 
 // ---- SIMT linear (GEMV regime, few rows): out[m, n] = sum_k xhat[m, k] * W'[n, k] -------------------

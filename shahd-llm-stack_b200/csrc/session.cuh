@@ -90,6 +90,11 @@ struct ShahdSession {
   int am_stride;
   float *part_o, *part_m, *part_l;
   int* attn_counter;
+  // split-K partial tiles of the norm-free projections, one region per decode chain
+  float* split_ws;
+  int* split_cnt;
+  size_t split_ws_floats;
+  int split_cnt_len;
   int *d_slot, *d_tok, *d_pos, *d_next, *d_gen_count, *d_ends, *d_starts, *d_full_len, *d_rows;
   uint32_t* d_rng;  // [max_seqs] SeededRng state per slot while a stochastic generate runs
   int* d_sampled;   // [max_seqs] ids the sampler chose this step
@@ -248,12 +253,13 @@ LinearArgs Lin(const float* a, int lda, const bf16* ab, int ldab, int rows_cap, 
   LinearArgs la;
   la.a = a; la.lda = lda; la.ab = ab; la.ldab = ldab; la.a_rows = rows_cap; la.M = M; la.K = K; la.Kp = Kp;
   la.w = w; la.N = N; la.eps = eps; la.c1 = c1; la.c2 = c2; la.am_val = amv; la.am_idx = ami;
+  la.ws = nullptr; la.ws_cnt = nullptr;
   return la;
 }
 
 // Enqueue one batched cached step (AdvanceOneToken + HeadLogitsRow for M rows) on `st`; returns the
 // number of kernels it launched.
-int EnqueueStep(ShahdSession* s, const StepPlan& p, cudaStream_t st, int r0 = 0) {
+int EnqueueStep(ShahdSession* s, const StepPlan& p, cudaStream_t st, int r0 = 0, int chain = 0) {
   // Row-indexed buffers: activations and positions hold rows_cap rows, the LM-head / finish / attention
   // split scratch holds max_seqs rows. This step uses rows [r0, r0 + M) of them (a decode chain's window).
   // A step beyond either is a caller bug, not a device fault.
@@ -283,6 +289,8 @@ int EnqueueStep(ShahdSession* s, const StepPlan& p, cudaStream_t st, int r0 = 0)
   float* part_m = s->part_m + rd * s->H * s->max_blocks;
   float* part_l = s->part_l + rd * s->H * s->max_blocks;
   int* counter = s->attn_counter + rd * s->Hk;
+  float* split_ws = s->split_ws + (size_t)chain * s->split_ws_floats;
+  int* split_cnt = s->split_cnt + (size_t)chain * s->split_cnt_len;
   Timed(s, st, kProfOther, 8.0 * M * s->E, [&] {
     EmbedArgs e{p.pos_in, p.slot, p.tok, p.prompt, p.poff, s->d_seq_len, pos, s->wte, s->wpe, x, xb, s->E, s->Ep};
     LaunchPdl(EmbedKernel, dim3(M), dim3(128), 0, st, e);
@@ -311,7 +319,9 @@ int EnqueueStep(ShahdSession* s, const StepPlan& p, cudaStream_t st, int r0 = 0)
       else LaunchPdl(AttnDecodeGenericKernel, ag, dim3(kAttnThreads), 0, st, aa);
     });
     // summed per-head Wo + residual (CachedForward.ts:81-84)
-    const LinearArgs lo = Lin(ctx, hd, ctxb, s->HDp, R, M, hd, s->HDp, Ly.w_o, s->E, eps, nullptr, nullptr);
+    LinearArgs lo = Lin(ctx, hd, ctxb, s->HDp, R, M, hd, s->HDp, Ly.w_o, s->E, eps, nullptr, nullptr);
+    lo.ws = split_ws;
+    lo.ws_cnt = split_cnt;
     Timed(s, st, kProfLinear, LinearBytes(M, hd, s->HDp, s->E),
           [&] { LaunchLinear(kNormNone, lo, EpiResid{x, xb, s->E, s->Ep, nullptr}, st); });
     // norm2 + MLP + residual (CachedForward.ts:86-87)
@@ -320,7 +330,9 @@ int EnqueueStep(ShahdSession* s, const StepPlan& p, cudaStream_t st, int r0 = 0)
       if (s->cfg.mlp_kind == 0) LaunchLinear(norm, lu, EpiReluFc{act, actb, s->F, s->Fp, Ly.b_fc}, st);
       else LaunchLinear(norm, lu, EpiGated{act, actb, s->F, s->Fp, s->cfg.mlp_kind == 2}, st);
     });
-    const LinearArgs ld = Lin(act, s->F, actb, s->Fp, R, M, s->F, s->Fp, Ly.w_down, s->E, eps, nullptr, nullptr);
+    LinearArgs ld = Lin(act, s->F, actb, s->Fp, R, M, s->F, s->Fp, Ly.w_down, s->E, eps, nullptr, nullptr);
+    ld.ws = split_ws;
+    ld.ws_cnt = split_cnt;
     Timed(s, st, kProfLinear, LinearBytes(M, s->F, s->Fp, s->E),
           [&] { LaunchLinear(kNormNone, ld, EpiResid{x, xb, s->E, s->Ep, Ly.b_proj}, st); });
   }
@@ -374,7 +386,7 @@ int EnqueueChains(ShahdSession* s, const StepPlan* plans, const int* r0, int nch
     cudaEventRecord(s->fork_ev, s->stream);
     for (int c = 1; c < nchain; c++) cudaStreamWaitEvent(s->side[c - 1], s->fork_ev, 0);
   }
-  for (int c = 0; c < nchain; c++) total += EnqueueStep(s, plans[c], c == 0 ? s->stream : s->side[c - 1], r0[c]);
+  for (int c = 0; c < nchain; c++) total += EnqueueStep(s, plans[c], c == 0 ? s->stream : s->side[c - 1], r0[c], c);
   if (nchain > 1) {
     for (int c = 1; c < nchain; c++) {
       cudaEventRecord(s->chain_ev[c - 1], s->side[c - 1]);
@@ -904,6 +916,12 @@ extern "C" int shahd_session_create(const ShahdModelCfg* cfg, const void* params
       (rc = DevAlloc(s, &s->d_row_poff, (size_t)s->rows_cap)) != SHAHD_OK ||
       (rc = DevAlloc(s, &s->d_window, (size_t)R * s->C)) != SHAHD_OK)
     return fail(rc);
+  s->split_ws_floats = std::max(UmmaKSplitFloats(s->E, s->HDp), UmmaKSplitFloats(s->E, s->Fp));
+  s->split_cnt_len = CeilDiv(s->E, 16);
+  if ((rc = DevAlloc(s, &s->split_ws, s->split_ws_floats * kMaxChains)) != SHAHD_OK ||
+      (rc = DevAlloc(s, &s->split_cnt, (size_t)s->split_cnt_len * kMaxChains)) != SHAHD_OK)
+    return fail(rc);
+  cudaMemset(s->split_cnt, 0, sizeof(int) * (size_t)s->split_cnt_len * kMaxChains);
   // bf16 operand rows are read over their padded width: padding columns must stay zero
   cudaMemset(s->xb, 0, sizeof(bf16) * RC * s->Ep);
   cudaMemset(s->ctxb, 0, sizeof(bf16) * RC * s->HDp);

@@ -15,6 +15,7 @@
 // skips the remaining work, releases its TMEM and returns.
 #pragma once
 
+#include <algorithm>
 #include <map>
 #include <mutex>
 
@@ -33,10 +34,29 @@ extern int g_umma_min_rows;
 extern int g_decode_chains;
 #define kUmmaMinRows (::shahd::g_umma_min_rows)
 
+// Tile width: prefill-sized row counts take wide tiles; decode-sized ones the narrowest tile whose grid
+// still fits one wave of CTAs (more CTAs stream the weights in parallel, each with a shorter queue).
+constexpr int kUmmaWaveCtas = 148;
 __host__ inline int UmmaBN(int M, int N) {
-  if (M > kUmmaBM) return 128;  // prefill-sized row counts: wide tiles
-  if (N <= 512) return 16;      // narrow decode projections: more CTAs
-  return N <= 1024 ? 32 : 64;
+  if (M > kUmmaBM) return 128;
+  for (int bn = 16; bn <= 64; bn *= 2)
+    if (CeilDiv(N, bn) <= kUmmaWaveCtas) return bn;
+  return 128;
+}
+
+// K splits of a decode-sized projection without a norm (the norm needs whole rows): about four k-blocks
+// of 64 per CTA, at most 8 splits and two waves of CTAs. Partial tiles meet in a workspace.
+__host__ inline int UmmaKSplit(int M, int N, int Kp) {
+  if (M > kUmmaBM) return 1;
+  const int nk = CeilDiv(Kp, kUmmaBK), tiles = CeilDiv(N, UmmaBN(M, N));
+  int ks = std::min(8, std::max(1, nk / 4));
+  while (ks > 1 && tiles * ks > 2 * kUmmaWaveCtas) ks--;
+  return ks;
+}
+// Workspace floats for split-K partials of an N-column projection (one launch at a time).
+__host__ inline size_t UmmaKSplitFloats(int N, int Kp) {
+  const int bn = UmmaBN(1, N);
+  return (size_t)CeilDiv(N, bn) * bn * UmmaKSplit(1, N, Kp) * kUmmaBM;
 }
 __host__ inline int UmmaGridN(int N) { return CeilDiv(N, 16); }  // upper bound of N tiles (BN >= 16)
 
@@ -132,6 +152,7 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
   using L = UmmaSmem<BN>;
   constexpr int S = L::kStages;
   constexpr int kChunks = BN / 16;
+  constexpr int kGroup = kChunks < 4 ? kChunks : 4;  // TMEM loads in flight before one wait (64 columns)
   constexpr bool kEarly = BN <= 32;  // epilogue reads issued before the main loop (registers allow it)
   const uint32_t stage_tx = (uint32_t)a_box_rows * kUmmaBK * 2 + (uint32_t)L::kB;
   extern __shared__ uint8_t smem_raw[];
@@ -141,11 +162,16 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
   uint64_t* final_bar = empty + S;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(final_bar + 1);
   volatile int* s_abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  volatile int* s_last = s_abort + 1;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n0 = blockIdx.x * BN;
   const int m0 = blockIdx.y * kUmmaBM;
-  const int nk = CeilDiv(la.Kp, kUmmaBK);
+  // split-K: this CTA reduces k-blocks [kb0, kb0 + nk) of the row; gridDim.z CTAs share an output tile
+  const int nk_all = CeilDiv(la.Kp, kUmmaBK);
+  const int ks = gridDim.z, kz = blockIdx.z;
+  const int kb0 = kz * nk_all / ks;
+  const int nk = (kz + 1) * nk_all / ks - kb0;
 
   if (threadIdx.x == 0) {
     for (int st = 0; st < S; st++) {
@@ -154,6 +180,7 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
     }
     MbarInit(final_bar, 1);
     *s_abort = 0;
+    *s_last = 1;
     FenceMbarInit();
     PrefetchTmaDesc(&tmap_a);
     PrefetchTmaDesc(&tmap_w);
@@ -173,14 +200,15 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
     for (int kb = 0; kb < nk && kb < S; kb++) {
       uint8_t* sa = smem + kb * L::kStage;
       MbarArriveExpectTx(&full[kb], stage_tx);
-      TmaLoad2D(sa + L::kA, &tmap_w, &full[kb], kb * kUmmaBK, n0);
+      TmaLoad2D(sa + L::kA, &tmap_w, &full[kb], (kb0 + kb) * kUmmaBK, n0);
     }
   }
   GridDepWait();
   GridDepLaunch();
   if (threadIdx.x == 0) {
     FenceProxyAsyncGlobal();
-    for (int kb = 0; kb < nk && kb < S; kb++) TmaLoad2D(smem + kb * L::kStage, &tmap_a, &full[kb], kb * kUmmaBK, m0);
+    for (int kb = 0; kb < nk && kb < S; kb++)
+      TmaLoad2D(smem + kb * L::kStage, &tmap_a, &full[kb], (kb0 + kb) * kUmmaBK, m0);
   }
   const int r = warp * 32 + lane;
   const bool row_ok = m0 + r < la.M;
@@ -240,8 +268,8 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
         } else {
           uint8_t* sb = smem + sp * L::kStage;
           MbarArriveExpectTx(&full[sp], stage_tx);
-          TmaLoad2D(sb, &tmap_a, &full[sp], (kp + S) * kUmmaBK, m0);
-          TmaLoad2D(sb + L::kA, &tmap_w, &full[sp], (kp + S) * kUmmaBK, n0);
+          TmaLoad2D(sb, &tmap_a, &full[sp], (kb0 + kp + S) * kUmmaBK, m0);
+          TmaLoad2D(sb + L::kA, &tmap_w, &full[sp], (kb0 + kp + S) * kUmmaBK, n0);
         }
       }
     }
@@ -261,57 +289,110 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
   }
   __syncthreads();
   TcgenFenceAfter();
-  if (!*s_abort) {
-    // Epilogue: thread = row (m0 + 32*warp + lane), 16 consecutive accumulator columns per TMEM load.
+  const uint32_t trow = tmem + ((uint32_t)(warp * 32) << 16);  // this warp's 32 TMEM lanes
+  if (!*s_abort && ks > 1) {
+    // split-K: every CTA parks its partial tile in the workspace; the last CTA of the tile sums the
+    // partials in split order (the result does not depend on which CTA finishes last) and runs the epilogue
+    float* part = la.ws + ((size_t)(blockIdx.x * ks + kz) * kUmmaBM + r) * BN;
+#pragma unroll
+    for (int g = 0; g < kChunks; g += kGroup) {
+      uint32_t u[kGroup][16];
+#pragma unroll
+      for (int q = 0; q < kGroup; q++) TmemLoad16(trow + (uint32_t)(16 * (g + q)), u[q]);
+      TmemWaitLd();
+      if (row_ok) {
+#pragma unroll
+        for (int q = 0; q < kGroup; q++) StoreNf<16>(part + 16 * (g + q), reinterpret_cast<const float*>(u[q]));
+      }
+    }
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) *s_last = atomicAdd(la.ws_cnt + blockIdx.x, 1) == ks - 1;
+    __syncthreads();
+    if (*s_last) __threadfence();
+  }
+  if (!*s_abort && *s_last) {
+    // Epilogue: thread = row (m0 + 32*warp + lane), 16 consecutive accumulator columns per chunk; the
+    // TMEM loads of up to four chunks are in flight before one wait.
     float bv = -INFINITY;
     int bi = 0x7fffffff;
 #pragma unroll
-    for (int ch = 0; ch < kChunks; ch++) {
-      const int c = 16 * ch;
-      uint32_t u[16];
-      TmemLoad16(tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)c, u);
-      TmemWaitLd();
-      if (row_ok && vec && n0 + c + 16 <= la.N) {
-        const int nb = n0 + c;
-        float v[16];
+    for (int g = 0; g < kChunks; g += kGroup) {
+      float vg[kGroup][16];
+      if (ks > 1) {
+        if (row_ok) {
 #pragma unroll
-        for (int j = 0; j < 16; j++) v[j] = __uint_as_float(u[j]);
-        if (NORM == kNormRms) {
+          for (int q = 0; q < kGroup; q++) {
 #pragma unroll
-          for (int j = 0; j < 16; j++) v[j] *= is;
-        } else if (NORM == kNormLayer) {
-          float c1[16], c2[16];
-          Load16f(la.c1 + nb, c1);
-          Load16f(la.c2 + nb, c2);
+            for (int j = 0; j < 16; j++) vg[q][j] = 0.f;
+            for (int z = 0; z < ks; z++) {
+              const float4* src =
+                  reinterpret_cast<const float4*>(la.ws + ((size_t)(blockIdx.x * ks + z) * kUmmaBM + r) * BN + 16 * (g + q));
 #pragma unroll
-          for (int j = 0; j < 16; j++) v[j] = is * (v[j] - mu * c1[j]) + c2[j];
-        }
-        if constexpr (kEarly) {
-          epi.store16(m0 + r, nb, v, pre[ch]);
-        } else {
-          epi.store16(m0 + r, nb, v, epi.load16(m0 + r, nb));
-        }
-        if constexpr (IsLogits<Epi>::value) {
-#pragma unroll
-          for (int j = 0; j < 16; j++) ArgmaxMerge(bv, bi, v[j], nb + j);
-        }
-      } else if (row_ok) {
-#pragma unroll
-        for (int j = 0; j < 16; j += 2) {
-          const int n = n0 + c + j;
-          if (n < la.N) {
-            float v0 = __uint_as_float(u[j]), v1 = __uint_as_float(u[j + 1]);
-            if (NORM == kNormRms) {
-              v0 *= is;
-              v1 *= is;
-            } else if (NORM == kNormLayer) {
-              v0 = is * (v0 - mu * la.c1[n]) + la.c2[n];
-              if (n + 1 < la.N) v1 = is * (v1 - mu * la.c1[n + 1]) + la.c2[n + 1];
+              for (int i = 0; i < 4; i++) {
+                const float4 t = __ldcg(src + i);
+                vg[q][4 * i] += t.x;
+                vg[q][4 * i + 1] += t.y;
+                vg[q][4 * i + 2] += t.z;
+                vg[q][4 * i + 3] += t.w;
+              }
             }
-            epi.apply(m0 + r, n, v0, v1, la.N);
-            if constexpr (IsLogits<Epi>::value) {
-              ArgmaxMerge(bv, bi, v0, n);
-              if (n + 1 < la.N) ArgmaxMerge(bv, bi, v1, n + 1);
+          }
+        }
+      } else {
+        uint32_t u[kGroup][16];
+#pragma unroll
+        for (int q = 0; q < kGroup; q++) TmemLoad16(trow + (uint32_t)(16 * (g + q)), u[q]);
+        TmemWaitLd();
+#pragma unroll
+        for (int q = 0; q < kGroup; q++)
+#pragma unroll
+          for (int j = 0; j < 16; j++) vg[q][j] = __uint_as_float(u[q][j]);
+      }
+      if (!row_ok) continue;
+#pragma unroll
+      for (int q = 0; q < kGroup; q++) {
+        const int ch = g + q;
+        const int nb = n0 + 16 * ch;
+        float (&v)[16] = vg[q];
+        if (vec && nb + 16 <= la.N) {
+          if (NORM == kNormRms) {
+#pragma unroll
+            for (int j = 0; j < 16; j++) v[j] *= is;
+          } else if (NORM == kNormLayer) {
+            float c1[16], c2[16];
+            Load16f(la.c1 + nb, c1);
+            Load16f(la.c2 + nb, c2);
+#pragma unroll
+            for (int j = 0; j < 16; j++) v[j] = is * (v[j] - mu * c1[j]) + c2[j];
+          }
+          if constexpr (kEarly) {
+            epi.store16(m0 + r, nb, v, pre[ch]);
+          } else {
+            epi.store16(m0 + r, nb, v, epi.load16(m0 + r, nb));
+          }
+          if constexpr (IsLogits<Epi>::value) {
+#pragma unroll
+            for (int j = 0; j < 16; j++) ArgmaxMerge(bv, bi, v[j], nb + j);
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < 16; j += 2) {
+            const int n = nb + j;
+            if (n < la.N) {
+              float v0 = v[j], v1 = v[j + 1];
+              if (NORM == kNormRms) {
+                v0 *= is;
+                v1 *= is;
+              } else if (NORM == kNormLayer) {
+                v0 = is * (v0 - mu * la.c1[n]) + la.c2[n];
+                if (n + 1 < la.N) v1 = is * (v1 - mu * la.c1[n + 1]) + la.c2[n + 1];
+              }
+              epi.apply(m0 + r, n, v0, v1, la.N);
+              if constexpr (IsLogits<Epi>::value) {
+                ArgmaxMerge(bv, bi, v0, n);
+                if (n + 1 < la.N) ArgmaxMerge(bv, bi, v1, n + 1);
+              }
             }
           }
         }
@@ -323,6 +404,7 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
         la.am_idx[(size_t)(m0 + r) * gridDim.x + blockIdx.x] = bi;
       }
     }
+    if (ks > 1 && threadIdx.x == 0) la.ws_cnt[blockIdx.x] = 0;  // ready for the next launch
   }
   TcgenFenceBefore();
   __syncthreads();
@@ -342,7 +424,8 @@ void LaunchUmmaLinearBN(const LinearArgs& la, const Epi& epi, cudaStream_t st) {
                          UmmaSmem<BN>::kBytes);
     configured = true;
   }
-  dim3 grid(CeilDiv(la.N, BN), CeilDiv(la.M, kUmmaBM));
+  const int ks = (NORM == kNormNone && la.ws != nullptr) ? UmmaKSplit(la.M, la.N, la.Kp) : 1;
+  dim3 grid(CeilDiv(la.N, BN), CeilDiv(la.M, kUmmaBM), ks);
   LaunchPdl(LinearUmmaKernel<NORM, Epi, BN>, grid, dim3(kUmmaThreads), UmmaSmem<BN>::kBytes, st, la, epi, ta, tw,
             box);
 }
