@@ -260,7 +260,8 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
     flush.zero_()
     step()
     torch.cuda.synchronize(dev)
-    prof = {k: sess.profile_read(k) for k in ("attention", "linear", "other")}
+    prof = {k: sess.profile_read(k) for k in ("attention", "linear", "other", "prefill_attention", "prefill_linear",
+                                                 "prefill_other")}
     sess.profile(False)
 
     if dist is not None:
@@ -283,7 +284,15 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
                 "frac": achieved / peaks["hbm_gbs"], "traffic": traffic, "kernel": dom, "peak_source": peak_kind,
                 "avg_launch_us": p["ms"] * 1000.0 / max(p["launches"], 1), "launches_profiled": p["launches"],
                 "algorithmic_bytes_per_launch": p["bytes"] / max(p["launches"], 1),
-                "share_of_step": p["ms"] / max(sum(v["ms"] for v in prof.values()), 1e-9)}
+                "share_of_step": p["ms"] / max(sum(prof[k]["ms"] for k in ("attention", "linear", "other")), 1e-9),
+                "scope": "decode-step launches (prefill launches are reported apart)",
+                # both HBM-bound kernel classes, measured the same way (event nodes around each kernel)
+                "classes": {k: {"avg_launch_us": prof[k]["ms"] * 1000.0 / max(prof[k]["launches"], 1),
+                                "achieved_gbs": prof[k]["bytes"] / (prof[k]["ms"] / 1000.0) / 1e9 if prof[k]["ms"] else 0.0,
+                                "frac": (prof[k]["bytes"] / (prof[k]["ms"] / 1000.0) / 1e9 / peaks["hbm_gbs"]
+                                         if prof[k]["ms"] else 0.0),
+                                "ms_per_job": prof[k]["ms"]}
+                            for k in ("attention", "linear")}}
     cpu = None
     if world == 1:
         threads = os.cpu_count() or 1

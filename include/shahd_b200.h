@@ -187,11 +187,13 @@ int32_t shahd_step_launches(ShahdSession* s, int32_t n);
 /* Every kernel this session has launched so far. */
 int64_t shahd_kernel_launches(ShahdSession* s);
 /* Measurement hook (no counterpart in the reference): while enabled, every kernel launch of the session
- * is bracketed by CUDA events on its own stream and tagged with its class and algorithmic bytes.
- * Enabling (or disabling) clears the records. */
+ * is bracketed by CUDA events on its own stream and tagged with its class and algorithmic bytes. Steps
+ * still replay as CUDA graphs (the events are event nodes of the graph, which also keeps consecutive
+ * kernels from overlapping), and each step is waited for so its times can be read. Enabling (or
+ * disabling) clears the totals. */
 int shahd_profile(ShahdSession* s, int32_t enable);
-/* Totals over the records of one class: 0 = decode attention, 1 = projections (GEMV/GEMM incl. the
- * LM head), 2 = embed/finish. total_ms sums the launches' event times; bytes sums their algorithmic
+/* Totals over the records of one class of decode-step launches: 0 = attention, 1 = projections
+ * (GEMV/GEMM incl. the LM head), 2 = embed/sampler/finish; 3-5 = the same classes of prefill launches. total_ms sums the launches' event times; bytes sums their algorithmic
  * bytes (weights once + activations + KV rows read). */
 int shahd_profile_read(ShahdSession* s, int32_t kind, double* total_ms, int64_t* launches, double* bytes);
 

@@ -31,7 +31,7 @@ struct Layer {
 
 // Everything a captured step bakes in.
 struct GraphKey {
-  int kind;  // 16 * (0 = prefill step, 1 = decode step) + number of concurrent chains
+  int kind;  // 16 * (16 * steps per graph + (0 = prefill step, 1 = decode step)) + concurrent chains
   int M;
   const void *slot, *tok, *poff, *prompt, *out;
   int out_ld;
@@ -45,9 +45,19 @@ struct GraphKey {
   }
 };
 
+// One kernel launch bracketed by CUDA events (measurement mode).
+struct ProfRec {
+  int kind;
+  cudaEvent_t e0, e1;
+  double bytes;         // algorithmic bytes, or the part that does not grow with the cached lengths
+  double per_attended;  // graph records: bytes per cached position the step's attention reads
+  int chain, rep;       // which chain and which of the graph's consecutive steps the launch belongs to
+};
+
 struct StepGraph {
   cudaGraphExec_t exec;
   int launches;
+  std::vector<ProfRec> recs;  // event nodes captured with the step (measurement mode only)
 };
 
 }  // namespace shahd
@@ -112,14 +122,14 @@ struct ShahdSession {
   // measurement: kernel launch count, and optional CUDA-event timing per kernel class
   long long launches = 0;
   bool prof = false;
-  std::vector<cudaEvent_t> ev_pool;
+  bool capturing = false;
+  int cur_rep = 0;  // which of a graph's consecutive steps is being enqueued
+  std::vector<cudaEvent_t> ev_pool;       // eager launches (recycled after each harvest)
   size_t ev_used = 0;
-  struct ProfRec {
-    int kind;
-    size_t ev0, ev1;
-    double bytes;
-  };
-  std::vector<ProfRec> prof_recs;
+  std::vector<cudaEvent_t> graph_events;  // owned by captured graphs
+  std::vector<shahd::ProfRec> prof_recs;  // eager records not yet harvested
+  double prof_ms[6] = {}, prof_bytes[6] = {};
+  long long prof_n[6] = {};
 };
 
 namespace shahd {
@@ -134,6 +144,7 @@ constexpr int kStagingRows = 12;
 constexpr int kStagingLengths = 7;
 constexpr int kPrefillRows = 8192;  // rows of one batched prefill chunk (whole sequences per chunk)
 constexpr int kMaxChains = 8;
+constexpr int kStepsPerGraph = 8;  // decode steps captured back to back in one graph
 
 template <class T>
 int DevAlloc(ShahdSession* s, T** p, size_t count) {
@@ -220,29 +231,69 @@ struct StepPlan {
 };
 
 // ---- measurement hooks: kernel classes timed with CUDA events on the launching stream ---------------
-enum ProfKind { kProfAttention = 0, kProfLinear = 1, kProfOther = 2, kProfKinds = 3 };
+// Classes 0-2 are decode-step launches; prefill launches (steps without the finish kernel) land in 3-5.
+enum ProfKind { kProfAttention = 0, kProfLinear = 1, kProfOther = 2, kProfPrefill = 3, kProfKinds = 6 };
 
-size_t ProfEvent(ShahdSession* s, cudaStream_t st) {
+// An event recorded on `st`: inside a stream capture it becomes an event-record node of the graph (each
+// replay records it again), otherwise a plain record from the recycled pool.
+cudaEvent_t ProfEvent(ShahdSession* s, cudaStream_t st) {
+  cudaEvent_t e = nullptr;
+  if (s->capturing) {
+    cudaEventCreate(&e);
+    s->graph_events.push_back(e);
+    cudaEventRecordWithFlags(e, st, cudaEventRecordExternal);
+    return e;
+  }
   if (s->ev_used == s->ev_pool.size()) {
-    cudaEvent_t e;
     cudaEventCreate(&e);
     s->ev_pool.push_back(e);
   }
-  cudaEventRecord(s->ev_pool[s->ev_used], st);
-  return s->ev_used++;
+  e = s->ev_pool[s->ev_used++];
+  cudaEventRecord(e, st);
+  return e;
 }
 
+// `bytes` is the launch's algorithmic traffic; an attention launch also passes the part that grows with
+// the cached lengths (per_attended x attended) so a replayed graph can be charged for the lengths of the
+// step it replays.
 template <class F>
-void Timed(ShahdSession* s, cudaStream_t st, int kind, double bytes, F&& launch) {
+void Timed(ShahdSession* s, cudaStream_t st, int kind, double bytes, F&& launch, double per_attended = 0,
+           double attended = 0, int chain = 0) {
   s->launches++;
   if (!s->prof) {
     launch();
     return;
   }
-  const size_t e0 = ProfEvent(s, st);
+  const cudaEvent_t e0 = ProfEvent(s, st);
   launch();
-  const size_t e1 = ProfEvent(s, st);
-  s->prof_recs.push_back({kind, e0, e1, bytes});
+  const cudaEvent_t e1 = ProfEvent(s, st);
+  if (s->capturing) s->prof_recs.push_back({kind, e0, e1, bytes, per_attended, chain, s->cur_rep});
+  else s->prof_recs.push_back({kind, e0, e1, bytes + per_attended * attended, 0.0, chain, 0});
+}
+
+// Adds the event times of finished records to the per-class totals (the stream must be idle). plans
+// (graph replays) give the cached lengths of the replayed steps: rep j of a chain attends j more
+// positions per row than its first step.
+int Accumulate(ShahdSession* s, const std::vector<ProfRec>& recs, const StepPlan* plans = nullptr) {
+  for (const auto& r : recs) {
+    float t = 0;
+    SHAHD_CUDA_TRY(cudaEventElapsedTime(&t, r.e0, r.e1));
+    double b = r.bytes;
+    if (plans && r.per_attended > 0)
+      b += r.per_attended * ((double)plans[r.chain].attended + (double)r.rep * plans[r.chain].M);
+    s->prof_ms[r.kind] += t;
+    s->prof_bytes[r.kind] += b;
+    s->prof_n[r.kind] += 1;
+  }
+  return SHAHD_OK;
+}
+
+int HarvestEager(ShahdSession* s) {
+  SHAHD_CUDA_TRY(cudaStreamSynchronize(s->stream));
+  SHAHD_TRY(Accumulate(s, s->prof_recs));
+  s->prof_recs.clear();
+  s->ev_used = 0;
+  return SHAHD_OK;
 }
 
 // Algorithmic bytes of one projection: bf16 weights once, bf16 activations in, fp32 results out.
@@ -268,7 +319,8 @@ int EnqueueStep(ShahdSession* s, const StepPlan& p, cudaStream_t st, int r0 = 0,
     return -1;
   }
   const long long before = s->launches;
-  const int M = p.M, R = s->rows_cap - r0;  // rows addressable from the window base (TMA map height)
+  const int M = p.M, R = s->rows_cap - r0;
+  const int pk = p.finish ? 0 : kProfPrefill;  // measurement class offset: decode step or prefill  // rows addressable from the window base (TMA map height)
   const int norm = s->cfg.norm_kind == 1 ? kNormRms : kNormLayer;
   const float eps = (float)s->cfg.layer_norm_eps;
   const int hd = s->H * s->d;
@@ -291,13 +343,13 @@ int EnqueueStep(ShahdSession* s, const StepPlan& p, cudaStream_t st, int r0 = 0,
   int* counter = s->attn_counter + rd * s->Hk;
   float* split_ws = s->split_ws + (size_t)chain * s->split_ws_floats;
   int* split_cnt = s->split_cnt + (size_t)chain * s->split_cnt_len;
-  Timed(s, st, kProfOther, 8.0 * M * s->E, [&] {
+  Timed(s, st, pk + kProfOther, 8.0 * M * s->E, [&] {
     EmbedArgs e{p.pos_in, p.slot, p.tok, p.prompt, p.poff, s->d_seq_len, pos, s->wte, s->wpe, x, xb, s->E, s->Ep};
     LaunchPdl(EmbedKernel, dim3(M), dim3(128), 0, st, e);
   });
   KvView kv{s->kv_pool, s->d_block_table, s->max_blocks, s->Hk, s->d, s->page_elems};
   // K and V rows read (bf16) + q read and ctx written (fp32 + bf16)
-  const double attn_bytes = 4.0 * s->Hk * s->d * (double)p.attended + 10.0 * M * hd;
+  const double attn_fixed = 10.0 * M * hd, attn_per_pos = 4.0 * s->Hk * s->d;
   // splits per (row, kv head): enough CTAs to fill the GPU; one split (no partials) beyond max_seqs rows
   int nsplit = 1;
   if (r0 + M <= s->max_seqs)
@@ -307,33 +359,33 @@ int EnqueueStep(ShahdSession* s, const StepPlan& p, cudaStream_t st, int r0 = 0,
     // norm1 + QKV + RoPE + KV append (CachedForward.ts:66-73, :78-79)
     const LinearArgs la = Lin(x, s->E, xb, s->Ep, R, M, s->E, s->Ep, Ly.w_qkv, s->Nqkv, eps, Ly.qkv_c1, Ly.qkv_c2);
     const EpiQKV eq{q, kv, l, pos, p.slot, s->rope_cos, s->rope_sin, s->H, s->Hk, s->d};
-    Timed(s, st, kProfLinear, LinearBytes(M, s->E, s->Ep, s->Nqkv), [&] { LaunchLinear(norm, la, eq, st); });
+    Timed(s, st, pk + kProfLinear, LinearBytes(M, s->E, s->Ep, s->Nqkv), [&] { LaunchLinear(norm, la, eq, st); });
     // attention over the cache (CachedForward.ts:76-80)
     AttnArgs aa{q, ctx, ctxb, s->HDp, kv, l, pos, p.slot, s->H, s->Hk, s->G, s->d,
                 (float)(1.0 / std::sqrt((double)s->d)), s->max_blocks, part_o, part_m, part_l, counter};
     dim3 ag(nsplit, s->Hk, M);
-    Timed(s, st, kProfAttention, attn_bytes, [&] {
+    Timed(s, st, pk + kProfAttention, attn_fixed, [&] {
       if (s->d == 64) LaunchPdl(AttnDecodeKernel<64>, ag, dim3(kAttnThreads), AttnSmemBytes(64), st, aa);
       else if (s->d == 32) LaunchPdl(AttnDecodeKernel<32>, ag, dim3(kAttnThreads), AttnSmemBytes(32), st, aa);
       else if (s->d == 128) LaunchPdl(AttnDecodeKernel<128>, ag, dim3(kAttnThreads), AttnSmemBytes(128), st, aa);
       else LaunchPdl(AttnDecodeGenericKernel, ag, dim3(kAttnThreads), 0, st, aa);
-    });
+    }, attn_per_pos, (double)p.attended, chain);
     // summed per-head Wo + residual (CachedForward.ts:81-84)
     LinearArgs lo = Lin(ctx, hd, ctxb, s->HDp, R, M, hd, s->HDp, Ly.w_o, s->E, eps, nullptr, nullptr);
     lo.ws = split_ws;
     lo.ws_cnt = split_cnt;
-    Timed(s, st, kProfLinear, LinearBytes(M, hd, s->HDp, s->E),
+    Timed(s, st, pk + kProfLinear, LinearBytes(M, hd, s->HDp, s->E),
           [&] { LaunchLinear(kNormNone, lo, EpiResid{x, xb, s->E, s->Ep, nullptr}, st); });
     // norm2 + MLP + residual (CachedForward.ts:86-87)
     const LinearArgs lu = Lin(x, s->E, xb, s->Ep, R, M, s->E, s->Ep, Ly.w_up, s->Nup, eps, Ly.up_c1, Ly.up_c2);
-    Timed(s, st, kProfLinear, LinearBytes(M, s->E, s->Ep, s->Nup), [&] {
+    Timed(s, st, pk + kProfLinear, LinearBytes(M, s->E, s->Ep, s->Nup), [&] {
       if (s->cfg.mlp_kind == 0) LaunchLinear(norm, lu, EpiReluFc{act, actb, s->F, s->Fp, Ly.b_fc}, st);
       else LaunchLinear(norm, lu, EpiGated{act, actb, s->F, s->Fp, s->cfg.mlp_kind == 2}, st);
     });
     LinearArgs ld = Lin(act, s->F, actb, s->Fp, R, M, s->F, s->Fp, Ly.w_down, s->E, eps, nullptr, nullptr);
     ld.ws = split_ws;
     ld.ws_cnt = split_cnt;
-    Timed(s, st, kProfLinear, LinearBytes(M, s->F, s->Fp, s->E),
+    Timed(s, st, pk + kProfLinear, LinearBytes(M, s->F, s->Fp, s->E),
           [&] { LaunchLinear(kNormNone, ld, EpiResid{x, xb, s->E, s->Ep, Ly.b_proj}, st); });
   }
   int nblk = 0;
@@ -342,7 +394,7 @@ int EnqueueStep(ShahdSession* s, const StepPlan& p, cudaStream_t st, int r0 = 0,
     nblk = HeadBlocks(s, M);
     const LinearArgs lh = Lin(x, s->E, xb, s->Ep, R, M, s->E, s->Ep, s->w_head, s->V, eps, s->head_c1, s->head_c2,
                               am_val, am_idx);
-    Timed(s, st, kProfLinear, LinearBytes(M, s->E, s->Ep, s->V),
+    Timed(s, st, pk + kProfLinear, LinearBytes(M, s->E, s->Ep, s->V),
           [&] { LaunchLinear(norm, lh, EpiLogits{p.logits, s->head_bias, s->V}, st); });
   }
   int* sampled = nullptr;
@@ -351,13 +403,13 @@ int EnqueueStep(ShahdSession* s, const StepPlan& p, cudaStream_t st, int r0 = 0,
     sampled = s->d_sampled + rd;
     const SampleArgs sa{p.logits, s->V, p.slot, s->d_rng, (float)p.sampling.temperature, p.sampling.top_k,
                         p.sampling.top_p, sampled};
-    Timed(s, st, kProfOther, 4.0 * M * s->V,
+    Timed(s, st, pk + kProfOther, 4.0 * M * s->V,
           [&] { LaunchPdl(SampleKernel, dim3(M), dim3(kSampleThreads), 0, st, sa); });
   }
   if (p.finish) {
     FinishArgs f{M, p.slot, pos, s->d_seq_len, p.head ? am_val : nullptr, am_idx, nblk, p.next_ids,
                  p.cur_tok, p.out_ids, p.out_ld, gen_count, sampled};
-    Timed(s, st, kProfOther, 16.0 * M, [&] { LaunchPdl(FinishKernel, dim3(CeilDiv(M, 4)), dim3(128), 0, st, f); });
+    Timed(s, st, pk + kProfOther, 16.0 * M, [&] { LaunchPdl(FinishKernel, dim3(CeilDiv(M, 4)), dim3(128), 0, st, f); });
   }
   return (int)(s->launches - before);
 }
@@ -409,32 +461,46 @@ bool ChainsFit(ShahdSession* s, const StepPlan* plans, const int* r0, int nchain
 
 // Run a step (or concurrent chains of steps) through a cached CUDA graph. The first use of a shape runs
 // eagerly (lazy host-side setup such as kernel attributes and TMA descriptors stays out of capture), the
-// second captures it, every later one replays it. Profiling runs eagerly so each kernel can be bracketed
-// with events.
-int RunStep(ShahdSession* s, const StepPlan* plans, const int* r0, int nchain, int kind) {
+// second captures it, every later one replays it. In measurement mode the graph also holds an event node
+// on each side of every kernel, and each replay is waited for and its kernel times added up.
+int RunStep(ShahdSession* s, const StepPlan* plans, const int* r0, int nchain, int kind, int reps = 1) {
   if (!ChainsFit(s, plans, r0, nchain)) return SHAHD_EINVAL;
+  // `reps` consecutive steps in one graph: every input of a decode step (tokens, positions, outputs) lives
+  // on the device, so back-to-back steps need no host update in between
+  auto enqueue = [&]() {
+    int total = 0;
+    for (int j = 0; j < reps; j++) {
+      s->cur_rep = j;
+      total += EnqueueChains(s, plans, r0, nchain);
+    }
+    s->cur_rep = 0;
+    return total;
+  };
   s->chains_hint = nchain;
-  if (s->prof) {
-    EnqueueChains(s, plans, r0, nchain);
-    return CheckLaunch("step");
-  }
+  if (s->prof) SHAHD_TRY(HarvestEager(s));  // eager records before the step, so graph records stay apart
   const StepPlan& p = plans[0];
-  GraphKey key{kind * 16 + nchain, p.M, p.slot, p.tok, p.poff, p.prompt, p.out_ids, p.out_ld,
-               g_umma_min_rows * 2 + (int)g_use_pdl, p.sampling.temperature > 0 ? p.sampling.temperature : 0.0,
+  GraphKey key{(reps * 16 + kind) * 16 + nchain, p.M, p.slot, p.tok, p.poff, p.prompt, p.out_ids, p.out_ld,
+               g_umma_min_rows * 4 + (int)g_use_pdl * 2 + (int)s->prof,
+               p.sampling.temperature > 0 ? p.sampling.temperature : 0.0,
                p.sampling.temperature > 0 ? p.sampling.top_p : 1.0, p.sampling.temperature > 0 ? p.sampling.top_k : 0};
   auto it = s->graphs.find(key);
   if (it == s->graphs.end()) {
-    EnqueueChains(s, plans, r0, nchain);
+    enqueue();
     SHAHD_TRY(CheckLaunch("step"));
-    s->graphs.emplace(key, StepGraph{nullptr, 0});
+    s->graphs.emplace(key, StepGraph{nullptr, 0, {}});
+    if (s->prof) SHAHD_TRY(HarvestEager(s));
     return SHAHD_OK;
   }
   if (it->second.exec == nullptr) {
     cudaGraph_t g = nullptr;
     SHAHD_CUDA_TRY(cudaStreamBeginCapture(s->stream, cudaStreamCaptureModeThreadLocal));
     const long long saved = s->launches;
-    const int n = EnqueueChains(s, plans, r0, nchain);
+    s->capturing = true;
+    const int n = enqueue();
+    s->capturing = false;
     s->launches = saved;
+    it->second.recs.swap(s->prof_recs);
+    s->prof_recs.clear();
     cudaError_t e = cudaStreamEndCapture(s->stream, &g);
     if (e != cudaSuccess) {
       SetError("step capture failed: %s", cudaGetErrorString(e));
@@ -451,6 +517,10 @@ int RunStep(ShahdSession* s, const StepPlan* plans, const int* r0, int nchain, i
   }
   SHAHD_CUDA_TRY(cudaGraphLaunch(it->second.exec, s->stream));
   s->launches += it->second.launches;
+  if (s->prof) {
+    SHAHD_CUDA_TRY(cudaStreamSynchronize(s->stream));
+    SHAHD_TRY(Accumulate(s, it->second.recs, plans));
+  }
   return SHAHD_OK;
 }
 
@@ -715,8 +785,13 @@ int GenerateCore(ShahdSession* s, const int* d_prompt_packed, const std::vector<
       plans[c].attended = 0;
       for (int i = r0[c]; i < r0[c] + plans[c].M; i++) plans[c].attended += s->h_len[i] + 1;
     }
-    SHAHD_TRY(RunStep(s, plans, r0, nchain, 1));
-    for (int i = 0; i < n; i++) s->h_len[i] += 1;
+    // consecutive steps that need no window rebuild go into one graph
+    int maxlen = 0;
+    for (int i = 0; i < n; i++) maxlen = std::max(maxlen, s->h_len[i]);
+    const int reps = std::max(1, std::min({kStepsPerGraph, max_new - k, C - maxlen}));
+    SHAHD_TRY(RunStep(s, plans, r0, nchain, 1, reps));
+    for (int i = 0; i < n; i++) s->h_len[i] += reps;
+    k += reps - 1;
   }
   return CheckLaunch("generate");
 }
@@ -946,6 +1021,7 @@ extern "C" int shahd_session_destroy(ShahdSession* s) {
   for (auto& kv : s->graphs)
     if (kv.second.exec) cudaGraphExecDestroy(kv.second.exec);
   for (cudaEvent_t e : s->ev_pool) cudaEventDestroy(e);
+  for (cudaEvent_t e : s->graph_events) cudaEventDestroy(e);
   for (void* p : s->allocs) cudaFree(p);
   if (s->h_block_table) cudaFreeHost(s->h_block_table);
   if (s->h_pinned_rows) cudaFreeHost(s->h_pinned_rows);
@@ -1204,6 +1280,10 @@ extern "C" int shahd_profile(ShahdSession* s, int32_t enable) {
   s->prof = enable != 0;
   s->prof_recs.clear();
   s->ev_used = 0;
+  for (int k = 0; k < kProfKinds; k++) {
+    s->prof_ms[k] = s->prof_bytes[k] = 0;
+    s->prof_n[k] = 0;
+  }
   return SHAHD_OK;
 }
 
@@ -1216,16 +1296,9 @@ extern "C" int shahd_profile_read(ShahdSession* s, int32_t kind, double* total_m
   std::lock_guard<std::mutex> g(s->mu);
   cudaSetDevice(s->device);
   SHAHD_CUDA_TRY(cudaDeviceSynchronize());
-  double ms = 0, b = 0;
-  int64_t n = 0;
-  for (const auto& r : s->prof_recs) {
-    if (r.kind != kind) continue;
-    float t = 0;
-    SHAHD_CUDA_TRY(cudaEventElapsedTime(&t, s->ev_pool[r.ev0], s->ev_pool[r.ev1]));
-    ms += t;
-    b += r.bytes;
-    n++;
-  }
+  SHAHD_TRY(HarvestEager(s));
+  const double ms = s->prof_ms[kind], b = s->prof_bytes[kind];
+  const int64_t n = s->prof_n[kind];
   *total_ms = ms;
   *launches = n;
   *bytes = b;

@@ -203,7 +203,8 @@ class Session:
     def profile(self, enable: bool) -> None:
         _lib.check(self.lib.shahd_profile(self.handle, int(enable)))
 
-    PROFILE_KINDS = {"attention": 0, "linear": 1, "other": 2}
+    PROFILE_KINDS = {"attention": 0, "linear": 1, "other": 2,
+                     "prefill_attention": 3, "prefill_linear": 4, "prefill_other": 5}
 
     def profile_read(self, kind: str) -> dict:
         ms = ctypes.c_double()
