@@ -72,6 +72,12 @@ void ShahdSetProgrammaticLaunch(int enable);
  * joined in one CUDA graph); 0 = automatic (one chain). Process-wide tuning hook;
  * no counterpart in the reference. Results do not depend on it. */
 void ShahdSetDecodeChains(int chains);
+/* Opt-in (default 0): batched decode steps of 17-128 rows as one persistent cooperative launch (one CTA
+ * per SM, phases separated by grid-wide barriers) instead of one launch per kernel. Used only where the
+ * model fits it (head_dim 32 or 64, 1, 2 or 4 query heads per kv head) and the GPU holds one such CTA
+ * per SM. At MicroChat size it is slower than the per-kernel path, whose launches overlap. Process-wide;
+ * no counterpart in the reference. Results agree with the per-kernel path within the parity tolerance. */
+void ShahdSetPersistentStep(int enable);
 /* First error code a kernel recorded for a bounded device-side wait that gave up (0 = none). */
 int ShahdDeviceErrorFlag(void);
 /* Device-pointer MatMulNT on the tensor cores: out[M,N] (+)= a[M,K] @ btᵀ with a, bt bf16 row-major

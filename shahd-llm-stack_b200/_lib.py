@@ -61,6 +61,7 @@ SIGNATURES = {
     "ShahdDeviceErrorFlag": (ctypes.c_int, []),
     "ShahdSetProgrammaticLaunch": (None, [ctypes.c_int]),
     "ShahdSetDecodeChains": (None, [ctypes.c_int]),
+    "ShahdSetPersistentStep": (None, [ctypes.c_int]),
     "ShahdMatMulNTBF16Device": (ctypes.c_int, [_vp, _vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, _vp]),
     "ShahdMatMulNTF32NoAlloc": (ctypes.c_int, [_fp, _fp, _fp, _i32, _i32, _i32, _i32]),
     "shahd_param_count": (_i64, [ctypes.POINTER(ShahdModelCfg)]),

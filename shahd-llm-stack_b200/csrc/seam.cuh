@@ -14,6 +14,7 @@ namespace shahd {
 int g_umma_min_rows = 17;
 bool g_use_pdl = true;
 int g_decode_chains = 0;  // 0 = automatic
+int g_persistent_step = 0;  // decode steps as one cooperative launch (opt-in: slower at MicroChat size)
 
 // ---- thread-local last error --------------------------------------------------------------------
 static thread_local std::string t_error;
@@ -395,6 +396,8 @@ void ShahdSetTensorCoreMinRows(int rows) { g_umma_min_rows = rows < 1 ? 1 : rows
 void ShahdSetProgrammaticLaunch(int enable) { g_use_pdl = enable != 0; }
 
 void ShahdSetDecodeChains(int chains) { g_decode_chains = chains < 0 ? 0 : chains; }
+
+void ShahdSetPersistentStep(int enable) { g_persistent_step = enable != 0; }
 
 int ShahdDeviceErrorFlag(void) {
   int v = 0;

@@ -20,6 +20,7 @@
 #include "decode_kernels.cuh"
 #include "params.h"
 #include "sampling.cuh"
+#include "step_kernel.cuh"
 #include "umma_linear.cuh"
 
 namespace shahd {
@@ -100,6 +101,14 @@ struct ShahdSession {
   int am_stride;
   float *part_o, *part_m, *part_l;
   int* attn_counter;
+  // persistent decode step: weight tensor maps and per-layer constants in device memory, activation
+  // tensor maps per row count, the grid-barrier counter and abort flag
+  int step_state = -1;  // -1 not set up yet, 0 unavailable on this device/model, 1 ready
+  int step_bn[5] = {};  // tile widths: qkv, o, up, down, head
+  shahd::StepLayer* d_step_layers = nullptr;
+  CUtensorMap* d_step_wmaps = nullptr;
+  std::map<int, CUtensorMap*> step_amaps;
+  unsigned* d_step_sync = nullptr;  // [barrier counter, abort flag]
   // split-K partial tiles of the norm-free projections, one region per decode chain
   float* split_ws;
   int* split_cnt;
@@ -128,8 +137,8 @@ struct ShahdSession {
   size_t ev_used = 0;
   std::vector<cudaEvent_t> graph_events;  // owned by captured graphs
   std::vector<shahd::ProfRec> prof_recs;  // eager records not yet harvested
-  double prof_ms[6] = {}, prof_bytes[6] = {};
-  long long prof_n[6] = {};
+  double prof_ms[7] = {}, prof_bytes[7] = {};
+  long long prof_n[7] = {};
 };
 
 namespace shahd {
@@ -232,7 +241,8 @@ struct StepPlan {
 
 // ---- measurement hooks: kernel classes timed with CUDA events on the launching stream ---------------
 // Classes 0-2 are decode-step launches; prefill launches (steps without the finish kernel) land in 3-5.
-enum ProfKind { kProfAttention = 0, kProfLinear = 1, kProfOther = 2, kProfPrefill = 3, kProfKinds = 6 };
+// Class 6: the persistent decode step (all of a step's projections and attention in one launch).
+enum ProfKind { kProfAttention = 0, kProfLinear = 1, kProfOther = 2, kProfPrefill = 3, kProfFused = 6, kProfKinds = 7 };
 
 // An event recorded on `st`: inside a stream capture it becomes an event-record node of the graph (each
 // replay records it again), otherwise a plain record from the recycled pool.
@@ -308,6 +318,83 @@ LinearArgs Lin(const float* a, int lda, const bf16* ab, int ldab, int rows_cap, 
   return la;
 }
 
+// ---- persistent decode step (one cooperative launch per step) ------------------------------------
+
+using StepKernelFn = void (*)(StepDesc);
+
+StepKernelFn StepKernelFor(int norm, int d) {
+  if (norm == kNormRms) return d == 64 ? DecodeStepKernel<kNormRms, 64> : DecodeStepKernel<kNormRms, 32>;
+  return d == 64 ? DecodeStepKernel<kNormLayer, 64> : DecodeStepKernel<kNormLayer, 32>;
+}
+
+// One-time set-up: weight tensor maps and per-layer constants in device memory, the sync words, and the
+// check that one CTA with the step's shared memory fits on every SM (a cooperative launch needs all of
+// them resident at once). Returns whether the persistent step can run for this session.
+bool StepSetup(ShahdSession* s) {
+  if (s->step_state >= 0) return s->step_state == 1;
+  s->step_state = 0;
+  if (!(s->d == 64 || s->d == 32) || !(s->G == 1 || s->G == 2 || s->G == 4)) return false;
+  const int norm = s->cfg.norm_kind == 1 ? kNormRms : kNormLayer;
+  const StepKernelFn fn = StepKernelFor(norm, s->d);
+  if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, kStepSmemDyn) != cudaSuccess) {
+    cudaGetLastError();
+    return false;
+  }
+  int per_sm = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, kStepThreads, kStepSmemDyn) != cudaSuccess ||
+      per_sm < 1) {
+    cudaGetLastError();
+    return false;
+  }
+  int coop = 0;
+  cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, s->device);
+  if (!coop) return false;
+  // the persistent kernel's tile widths: 16 for the layer projections, 32 for the LM head
+  s->step_bn[0] = s->step_bn[1] = s->step_bn[2] = s->step_bn[3] = 16;
+  s->step_bn[4] = 32;
+  std::vector<CUtensorMap> wm(4 * s->L + 1);
+  for (int l = 0; l < s->L; l++) {
+    const Layer& Ly = s->layers[l];
+    if (!MakeTmaBf16(Ly.w_qkv, s->Nqkv, s->Ep, s->Ep, s->step_bn[0], &wm[4 * l]) ||
+        !MakeTmaBf16(Ly.w_o, s->E, s->HDp, s->HDp, s->step_bn[1], &wm[4 * l + 1]) ||
+        !MakeTmaBf16(Ly.w_up, s->Nup, s->Ep, s->Ep, s->step_bn[2], &wm[4 * l + 2]) ||
+        !MakeTmaBf16(Ly.w_down, s->E, s->Fp, s->Fp, s->step_bn[3], &wm[4 * l + 3]))
+      return false;
+  }
+  if (!MakeTmaBf16(s->w_head, s->V, s->Ep, s->Ep, s->step_bn[4], &wm[4 * s->L])) return false;
+  std::vector<StepLayer> ly(s->L);
+  for (int l = 0; l < s->L; l++) {
+    const Layer& Ly = s->layers[l];
+    ly[l] = StepLayer{Ly.qkv_c1, Ly.qkv_c2, Ly.up_c1, Ly.up_c2, Ly.b_fc, Ly.b_proj};
+  }
+  if (DevAlloc(s, &s->d_step_wmaps, wm.size()) != SHAHD_OK || DevAlloc(s, &s->d_step_layers, ly.size()) != SHAHD_OK ||
+      DevAlloc(s, &s->d_step_sync, 2) != SHAHD_OK)
+    return false;
+  if (cudaMemcpy(s->d_step_wmaps, wm.data(), sizeof(CUtensorMap) * wm.size(), cudaMemcpyHostToDevice) != cudaSuccess ||
+      cudaMemcpy(s->d_step_layers, ly.data(), sizeof(StepLayer) * ly.size(), cudaMemcpyHostToDevice) != cudaSuccess ||
+      cudaMemset(s->d_step_sync, 0, 2 * sizeof(unsigned)) != cudaSuccess)
+    return false;
+  s->step_state = 1;
+  return true;
+}
+
+// Activation tensor maps (xb, ctxb, actb) with tiles of the rows a step of M rows uses.
+const CUtensorMap* StepActivationMaps(ShahdSession* s, int M) {
+  const int box = UmmaBoxRows(M);
+  auto it = s->step_amaps.find(box);
+  if (it != s->step_amaps.end()) return it->second;
+  CUtensorMap am[3];
+  if (!MakeTmaBf16(s->xb, s->rows_cap, s->Ep, s->Ep, box, &am[0]) ||
+      !MakeTmaBf16(s->ctxb, s->rows_cap, s->HDp, s->HDp, box, &am[1]) ||
+      !MakeTmaBf16(s->actb, s->rows_cap, s->Fp, s->Fp, box, &am[2]))
+    return nullptr;
+  CUtensorMap* d = nullptr;
+  if (DevAlloc(s, &d, 3) != SHAHD_OK) return nullptr;
+  if (cudaMemcpy(d, am, sizeof(am), cudaMemcpyHostToDevice) != cudaSuccess) return nullptr;
+  s->step_amaps[box] = d;
+  return d;
+}
+
 // Enqueue one batched cached step (AdvanceOneToken + HeadLogitsRow for M rows) on `st`; returns the
 // number of kernels it launched.
 int EnqueueStep(ShahdSession* s, const StepPlan& p, cudaStream_t st, int r0 = 0, int chain = 0) {
@@ -319,8 +406,8 @@ int EnqueueStep(ShahdSession* s, const StepPlan& p, cudaStream_t st, int r0 = 0,
     return -1;
   }
   const long long before = s->launches;
-  const int M = p.M, R = s->rows_cap - r0;
-  const int pk = p.finish ? 0 : kProfPrefill;  // measurement class offset: decode step or prefill  // rows addressable from the window base (TMA map height)
+  const int M = p.M, R = s->rows_cap - r0;  // R: rows addressable from the window base (TMA map height)
+  const int pk = p.finish ? 0 : kProfPrefill;  // measurement class offset: decode step or prefill
   const int norm = s->cfg.norm_kind == 1 ? kNormRms : kNormLayer;
   const float eps = (float)s->cfg.layer_norm_eps;
   const int hd = s->H * s->d;
@@ -343,59 +430,111 @@ int EnqueueStep(ShahdSession* s, const StepPlan& p, cudaStream_t st, int r0 = 0,
   int* counter = s->attn_counter + rd * s->Hk;
   float* split_ws = s->split_ws + (size_t)chain * s->split_ws_floats;
   int* split_cnt = s->split_cnt + (size_t)chain * s->split_cnt_len;
-  Timed(s, st, pk + kProfOther, 8.0 * M * s->E, [&] {
-    EmbedArgs e{p.pos_in, p.slot, p.tok, p.prompt, p.poff, s->d_seq_len, pos, s->wte, s->wpe, x, xb, s->E, s->Ep};
-    LaunchPdl(EmbedKernel, dim3(M), dim3(128), 0, st, e);
-  });
-  KvView kv{s->kv_pool, s->d_block_table, s->max_blocks, s->Hk, s->d, s->page_elems};
-  // K and V rows read (bf16) + q read and ctx written (fp32 + bf16)
-  const double attn_fixed = 10.0 * M * hd, attn_per_pos = 4.0 * s->Hk * s->d;
-  // splits per (row, kv head): enough CTAs to fill the GPU; one split (no partials) beyond max_seqs rows
-  int nsplit = 1;
-  if (r0 + M <= s->max_seqs)
-    nsplit = std::max(1, std::min(s->max_blocks, CeilDiv(3 * s->num_sms / std::max(1, s->chains_hint), M * s->Hk)));
-  for (int l = 0; l < s->L; l++) {
-    const Layer& Ly = s->layers[l];
-    // norm1 + QKV + RoPE + KV append (CachedForward.ts:66-73, :78-79)
-    const LinearArgs la = Lin(x, s->E, xb, s->Ep, R, M, s->E, s->Ep, Ly.w_qkv, s->Nqkv, eps, Ly.qkv_c1, Ly.qkv_c2);
-    const EpiQKV eq{q, kv, l, pos, p.slot, s->rope_cos, s->rope_sin, s->H, s->Hk, s->d};
-    Timed(s, st, pk + kProfLinear, LinearBytes(M, s->E, s->Ep, s->Nqkv), [&] { LaunchLinear(norm, la, eq, st); });
-    // attention over the cache (CachedForward.ts:76-80)
-    AttnArgs aa{q, ctx, ctxb, s->HDp, kv, l, pos, p.slot, s->H, s->Hk, s->G, s->d,
-                (float)(1.0 / std::sqrt((double)s->d)), s->max_blocks, part_o, part_m, part_l, counter};
-    dim3 ag(nsplit, s->Hk, M);
-    Timed(s, st, pk + kProfAttention, attn_fixed, [&] {
-      if (s->d == 64) LaunchPdl(AttnDecodeKernel<64>, ag, dim3(kAttnThreads), AttnSmemBytes(64), st, aa);
-      else if (s->d == 32) LaunchPdl(AttnDecodeKernel<32>, ag, dim3(kAttnThreads), AttnSmemBytes(32), st, aa);
-      else if (s->d == 128) LaunchPdl(AttnDecodeKernel<128>, ag, dim3(kAttnThreads), AttnSmemBytes(128), st, aa);
-      else LaunchPdl(AttnDecodeGenericKernel, ag, dim3(kAttnThreads), 0, st, aa);
-    }, attn_per_pos, (double)p.attended, chain);
-    // summed per-head Wo + residual (CachedForward.ts:81-84)
-    LinearArgs lo = Lin(ctx, hd, ctxb, s->HDp, R, M, hd, s->HDp, Ly.w_o, s->E, eps, nullptr, nullptr);
-    lo.ws = split_ws;
-    lo.ws_cnt = split_cnt;
-    Timed(s, st, pk + kProfLinear, LinearBytes(M, hd, s->HDp, s->E),
-          [&] { LaunchLinear(kNormNone, lo, EpiResid{x, xb, s->E, s->Ep, nullptr}, st); });
-    // norm2 + MLP + residual (CachedForward.ts:86-87)
-    const LinearArgs lu = Lin(x, s->E, xb, s->Ep, R, M, s->E, s->Ep, Ly.w_up, s->Nup, eps, Ly.up_c1, Ly.up_c2);
-    Timed(s, st, pk + kProfLinear, LinearBytes(M, s->E, s->Ep, s->Nup), [&] {
-      if (s->cfg.mlp_kind == 0) LaunchLinear(norm, lu, EpiReluFc{act, actb, s->F, s->Fp, Ly.b_fc}, st);
-      else LaunchLinear(norm, lu, EpiGated{act, actb, s->F, s->Fp, s->cfg.mlp_kind == 2}, st);
-    });
-    LinearArgs ld = Lin(act, s->F, actb, s->Fp, R, M, s->F, s->Fp, Ly.w_down, s->E, eps, nullptr, nullptr);
-    ld.ws = split_ws;
-    ld.ws_cnt = split_cnt;
-    Timed(s, st, pk + kProfLinear, LinearBytes(M, s->F, s->Fp, s->E),
-          [&] { LaunchLinear(kNormNone, ld, EpiResid{x, xb, s->E, s->Ep, Ly.b_proj}, st); });
-  }
+  // decode rows of the batched regime: the whole step (embed .. LM head) as one persistent launch
+  const bool fused = g_persistent_step && r0 == 0 && chain == 0 && s->chains_hint <= 1 && p.head && p.finish &&
+                     p.pos_in == nullptr && p.poff == nullptr && p.tok != nullptr && M >= kUmmaMinRows &&
+                     M <= kUmmaBM && StepSetup(s);
   int nblk = 0;
-  if (p.head) {
-    // final norm + LM head + argmax partials (HeadLogitsRow, CachedRowMath.ts:117-137)
-    nblk = HeadBlocks(s, M);
-    const LinearArgs lh = Lin(x, s->E, xb, s->Ep, R, M, s->E, s->Ep, s->w_head, s->V, eps, s->head_c1, s->head_c2,
-                              am_val, am_idx);
-    Timed(s, st, pk + kProfLinear, LinearBytes(M, s->E, s->Ep, s->V),
-          [&] { LaunchLinear(norm, lh, EpiLogits{p.logits, s->head_bias, s->V}, st); });
+  if (fused) {
+    const CUtensorMap* amaps = StepActivationMaps(s, M);
+    if (amaps == nullptr) {
+      SetError("internal: tensor maps of the persistent step could not be made");
+      return -1;
+    }
+    StepDesc d;
+    d.M = M; d.E = s->E; d.Ep = s->Ep; d.H = s->H; d.Hk = s->Hk; d.d = s->d; d.G = s->G; d.F = s->F; d.Fp = s->Fp;
+    d.V = s->V; d.L = s->L; d.HDp = s->HDp; d.Nqkv = s->Nqkv; d.Nup = s->Nup;
+    d.norm = norm; d.mlp_kind = s->cfg.mlp_kind;
+    d.bn_qkv = s->step_bn[0]; d.bn_o = s->step_bn[1]; d.bn_up = s->step_bn[2]; d.bn_down = s->step_bn[3];
+    d.bn_head = s->step_bn[4];
+    d.ks_o = UmmaKSplit(M, s->E, s->HDp);
+    d.ks_down = UmmaKSplit(M, s->E, s->Fp);
+    d.a_box_rows = UmmaBoxRows(M);
+    d.eps = eps;
+    d.scale = (float)(1.0 / std::sqrt((double)s->d));
+    d.x = x; d.q = q; d.ctx = ctx; d.act = act; d.logits = p.logits;
+    d.xb = xb; d.ctxb = ctxb; d.actb = actb;
+    d.pos = pos; d.slot = p.slot; d.tok = p.tok; d.seq_len = s->d_seq_len;
+    d.wte = s->wte; d.wpe = s->wpe; d.rope_cos = s->rope_cos; d.rope_sin = s->rope_sin;
+    d.head_bias = s->head_bias; d.head_c1 = s->head_c1; d.head_c2 = s->head_c2;
+    d.am_val = am_val; d.am_idx = am_idx;
+    d.kv = KvView{s->kv_pool, s->d_block_table, s->max_blocks, s->Hk, s->d, s->page_elems};
+    d.layers = s->d_step_layers; d.wmaps = s->d_step_wmaps; d.amaps = amaps;
+    d.ws = split_ws; d.ws_cnt = split_cnt;
+    d.bar = s->d_step_sync; d.abort_flag = reinterpret_cast<int*>(s->d_step_sync + 1);
+    double bytes = 8.0 * M * s->E + LinearBytes(M, s->E, s->Ep, s->V) + 10.0 * M * hd * s->L;
+    bytes += s->L * (LinearBytes(M, s->E, s->Ep, s->Nqkv) + LinearBytes(M, hd, s->HDp, s->E) +
+                     LinearBytes(M, s->E, s->Ep, s->Nup) + LinearBytes(M, s->F, s->Fp, s->E));
+    cudaMemsetAsync(s->d_step_sync, 0, 2 * sizeof(unsigned), st);
+    const StepKernelFn fn = StepKernelFor(norm, s->d);
+    Timed(s, st, kProfFused, bytes, [&] {
+      cudaLaunchConfig_t lc = {};
+      lc.gridDim = dim3(s->num_sms);
+      lc.blockDim = dim3(kStepThreads);
+      lc.dynamicSmemBytes = kStepSmemDyn;
+      lc.stream = st;
+      cudaLaunchAttribute at[1];
+      at[0].id = cudaLaunchAttributeCooperative;
+      at[0].val.cooperative = 1;
+      lc.attrs = at;
+      lc.numAttrs = 1;
+      cudaLaunchKernelEx(&lc, fn, d);
+    }, 4.0 * s->Hk * s->d * s->L, (double)p.attended, chain);
+    nblk = CeilDiv(s->V, s->step_bn[4]);
+  } else {
+    Timed(s, st, pk + kProfOther, 8.0 * M * s->E, [&] {
+      EmbedArgs e{p.pos_in, p.slot, p.tok, p.prompt, p.poff, s->d_seq_len, pos, s->wte, s->wpe, x, xb, s->E, s->Ep};
+      LaunchPdl(EmbedKernel, dim3(M), dim3(128), 0, st, e);
+    });
+    KvView kv{s->kv_pool, s->d_block_table, s->max_blocks, s->Hk, s->d, s->page_elems};
+    // K and V rows read (bf16) + q read and ctx written (fp32 + bf16)
+    const double attn_fixed = 10.0 * M * hd, attn_per_pos = 4.0 * s->Hk * s->d;
+    // splits per (row, kv head): enough CTAs to fill the GPU; one split (no partials) beyond max_seqs rows
+    int nsplit = 1;
+    if (r0 + M <= s->max_seqs)
+      nsplit = std::max(1, std::min(s->max_blocks, CeilDiv(3 * s->num_sms / std::max(1, s->chains_hint), M * s->Hk)));
+    for (int l = 0; l < s->L; l++) {
+      const Layer& Ly = s->layers[l];
+      // norm1 + QKV + RoPE + KV append (CachedForward.ts:66-73, :78-79)
+      const LinearArgs la = Lin(x, s->E, xb, s->Ep, R, M, s->E, s->Ep, Ly.w_qkv, s->Nqkv, eps, Ly.qkv_c1, Ly.qkv_c2);
+      const EpiQKV eq{q, kv, l, pos, p.slot, s->rope_cos, s->rope_sin, s->H, s->Hk, s->d};
+      Timed(s, st, pk + kProfLinear, LinearBytes(M, s->E, s->Ep, s->Nqkv), [&] { LaunchLinear(norm, la, eq, st); });
+      // attention over the cache (CachedForward.ts:76-80)
+      AttnArgs aa{q, ctx, ctxb, s->HDp, kv, l, pos, p.slot, s->H, s->Hk, s->G, s->d,
+                  (float)(1.0 / std::sqrt((double)s->d)), s->max_blocks, part_o, part_m, part_l, counter};
+      dim3 ag(nsplit, s->Hk, M);
+      Timed(s, st, pk + kProfAttention, attn_fixed, [&] {
+        if (s->d == 64) LaunchPdl(AttnDecodeKernel<64>, ag, dim3(kAttnThreads), AttnSmemBytes(64), st, aa);
+        else if (s->d == 32) LaunchPdl(AttnDecodeKernel<32>, ag, dim3(kAttnThreads), AttnSmemBytes(32), st, aa);
+        else if (s->d == 128) LaunchPdl(AttnDecodeKernel<128>, ag, dim3(kAttnThreads), AttnSmemBytes(128), st, aa);
+        else LaunchPdl(AttnDecodeGenericKernel, ag, dim3(kAttnThreads), 0, st, aa);
+      }, attn_per_pos, (double)p.attended, chain);
+      // summed per-head Wo + residual (CachedForward.ts:81-84)
+      LinearArgs lo = Lin(ctx, hd, ctxb, s->HDp, R, M, hd, s->HDp, Ly.w_o, s->E, eps, nullptr, nullptr);
+      lo.ws = split_ws;
+      lo.ws_cnt = split_cnt;
+      Timed(s, st, pk + kProfLinear, LinearBytes(M, hd, s->HDp, s->E),
+            [&] { LaunchLinear(kNormNone, lo, EpiResid{x, xb, s->E, s->Ep, nullptr}, st); });
+      // norm2 + MLP + residual (CachedForward.ts:86-87)
+      const LinearArgs lu = Lin(x, s->E, xb, s->Ep, R, M, s->E, s->Ep, Ly.w_up, s->Nup, eps, Ly.up_c1, Ly.up_c2);
+      Timed(s, st, pk + kProfLinear, LinearBytes(M, s->E, s->Ep, s->Nup), [&] {
+        if (s->cfg.mlp_kind == 0) LaunchLinear(norm, lu, EpiReluFc{act, actb, s->F, s->Fp, Ly.b_fc}, st);
+        else LaunchLinear(norm, lu, EpiGated{act, actb, s->F, s->Fp, s->cfg.mlp_kind == 2}, st);
+      });
+      LinearArgs ld = Lin(act, s->F, actb, s->Fp, R, M, s->F, s->Fp, Ly.w_down, s->E, eps, nullptr, nullptr);
+      ld.ws = split_ws;
+      ld.ws_cnt = split_cnt;
+      Timed(s, st, pk + kProfLinear, LinearBytes(M, s->F, s->Fp, s->E),
+            [&] { LaunchLinear(kNormNone, ld, EpiResid{x, xb, s->E, s->Ep, Ly.b_proj}, st); });
+    }
+    if (p.head) {
+      // final norm + LM head + argmax partials (HeadLogitsRow, CachedRowMath.ts:117-137)
+      nblk = HeadBlocks(s, M);
+      const LinearArgs lh = Lin(x, s->E, xb, s->Ep, R, M, s->E, s->Ep, s->w_head, s->V, eps, s->head_c1, s->head_c2,
+                                am_val, am_idx);
+      Timed(s, st, pk + kProfLinear, LinearBytes(M, s->E, s->Ep, s->V),
+            [&] { LaunchLinear(norm, lh, EpiLogits{p.logits, s->head_bias, s->V}, st); });
+    }
   }
   int* sampled = nullptr;
   if (p.head && p.finish && p.sampling.temperature > 0) {

@@ -32,6 +32,7 @@ constexpr int kUmmaThreads = 128;
 // through ShahdSetTensorCoreMinRows / SetScalarKernels (test hooks, process-wide).
 extern int g_umma_min_rows;
 extern int g_decode_chains;
+extern int g_persistent_step;
 #define kUmmaMinRows (::shahd::g_umma_min_rows)
 
 // Tile width: prefill-sized row counts take wide tiles; decode-sized ones the narrowest tile whose grid
