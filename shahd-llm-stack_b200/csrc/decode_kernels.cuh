@@ -640,14 +640,12 @@ __host__ __device__ constexpr int AttnSmemBytes(int D) { return kAttnRing * 2 * 
 // ring of K|V page buffers.
 template <int D>
 __global__ void __launch_bounds__(kAttnThreads) AttnDecodeKernel(AttnArgs aa) {
-  constexpr int LPP = D / 8;    // lanes per position (16 B of K each)
-  constexpr int PPW = 32 / LPP; // positions per warp pass
   constexpr int JPL = D / 32;   // output dims per lane
   constexpr int PAGE = kPageTokens * D;  // elements of one K (or V) page
   extern __shared__ __align__(128) uint8_t attn_smem[];
   bf16* ring = reinterpret_cast<bf16*>(attn_smem);  // [kAttnRing][K page | V page]
   __shared__ __align__(8) uint64_t bar[kAttnRing];
-  __shared__ float sq[kMaxGroup][D];
+  __shared__ __align__(16) float sq[kMaxGroup][D];
   __shared__ float ss[kMaxGroup][kPageTokens];
   __shared__ float so[kMaxGroup * D];
   __shared__ float s_m[kMaxGroup], s_l[kMaxGroup], s_scale[kMaxGroup];
@@ -700,7 +698,6 @@ __global__ void __launch_bounds__(kAttnThreads) AttnDecodeKernel(AttnArgs aa) {
   for (int i = 0; i < kMaxGroup; i++)
 #pragma unroll
     for (int jj = 0; jj < JPL; jj++) o[i][jj] = 0.f;
-  const int seg = lane % LPP;
   for (int pg = pb; pg < pe; pg++) {
     const int it = pg - pb, b = it % kAttnRing;
     const bool present = aa.kv.block_table[slot * aa.kv.max_blocks + pg] >= 0;
@@ -713,24 +710,28 @@ __global__ void __launch_bounds__(kAttnThreads) AttnDecodeKernel(AttnArgs aa) {
     const int tv = present ? page_len(pg) : 0;
     const bf16* sk = ring + (size_t)b * 2 * PAGE;
     const bf16* sv = sk + PAGE;
-    // scores s[i][t] = (q_i · k_t) * scale
-#pragma unroll
-    for (int tb = warp * PPW; tb < kPageTokens; tb += kAttnWarps * PPW) {
-      const int t = tb + lane / LPP;
-      float kf[8];
-      if (t < tv) {
-        Bf16x8ToFloat(*reinterpret_cast<const uint4*>(sk + t * D + seg * 8), kf);
-      } else {
-#pragma unroll
-        for (int j = 0; j < 8; j++) kf[j] = 0.f;
-      }
+    // scores s[i][t] = (q_i · k_t) * scale. Warp w scores positions 16w .. 16w + 15, two lanes per
+    // position (each half of the head dimension); lane l starts its half at pair (c + l) mod D/4, so the
+    // 32 lanes read 32 different banks of the K rows and one shuffle joins the halves.
+    {
+      constexpr int HW = D / 4;  // bf16 pairs per half row
+      static_assert(kAttnWarps * 16 == kPageTokens, "one position per lane pair");
+      const int t = warp * 16 + (lane & 15), h = lane >> 4;
+      const __nv_bfloat162* krow = reinterpret_cast<const __nv_bfloat162*>(sk) + t * (D / 2) + h * HW;
       for (int i = 0; i < G; i++) {
-        float part = 0.f;
+        const float2* qh = reinterpret_cast<const float2*>(&sq[i][0]) + h * HW;
+        float a = 0.f, b = 0.f;
 #pragma unroll
-        for (int j = 0; j < 8; j++) part = fmaf(kf[j], sq[i][seg * 8 + j], part);
-#pragma unroll
-        for (int off = LPP / 2; off > 0; off >>= 1) part += __shfl_xor_sync(0xffffffffu, part, off);
-        if (seg == 0 && t < tv) ss[i][t] = part * aa.scale;
+        for (int c = 0; c < HW; c++) {
+          const int wd = (c + lane) & (HW - 1);
+          const float2 kf = __bfloat1622float2(krow[wd]);
+          const float2 qv = qh[wd];
+          a = fmaf(kf.x, qv.x, a);
+          b = fmaf(kf.y, qv.y, b);
+        }
+        a += b;
+        a += __shfl_xor_sync(0xffffffffu, a, 16);
+        if (h == 0 && t < tv) ss[i][t] = a * aa.scale;  // rows past tv hold stale data: never stored
       }
     }
     __syncthreads();
