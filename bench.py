@@ -36,18 +36,8 @@ METRIC = "KV-cached decode tokens/s at MicroChat shape, 1-8 B200; % of HBM roofl
 L2_FLUSH_BYTES = 512 << 20  # > 126 MB L2
 
 
-def uniform_ids(count: int, vocab: int, seed: int) -> np.ndarray:
-    """floor(NextFloat() * vocab) from SeededRng(seed) (Brain/Random/SeededRng.ts:32-40, Scripts/Bench.ts:41-42)."""
-    st = seed & 0xFFFFFFFF
-    out = np.empty(count, dtype=np.int32)
-    for i in range(count):
-        st = (st * 1664525 + 1013904223) & 0xFFFFFFFF
-        out[i] = int(st / 4294967296.0 * vocab)
-    return out
-
-
 def prompts_for(w, rank: int) -> np.ndarray:
-    return np.stack([uniform_ids(w.prompt_len, w.model.vocab_size, seed=1000 + rank * w.seqs + i) for i in range(w.seqs)])
+    return pkg.sharding.shard_prompts(w, rank)
 
 
 def load_peaks() -> tuple[dict, str]:
