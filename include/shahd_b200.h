@@ -185,6 +185,17 @@ int shahd_generate_device(ShahdSession* s, const int32_t* d_prompts, const int32
                           int32_t max_new, const ShahdSampling* opts, uint32_t* d_rng_states, int32_t* d_out_ids,
                           void* stream);
 
+/* The target pass of speculative decoding (SpeculativeDecodeGreedy, Brain/Reasoning/SpeculativeDecode.ts:
+ * 67-72, with the cache instead of a full forward): slot i's tokens tokens[offsets[i] .. offsets[i+1]) are
+ * appended at its cached length and the LM head runs on every appended row; next_ids [rows] receives each
+ * row's greedy argmax (row j predicts the token after tokens[offsets[i] + j]) and logits (nullable)
+ * [rows, vocab]. Positions must stay inside the window; at most the session's prefill chunk of rows. */
+int shahd_verify(ShahdSession* s, const int32_t* slots, const int32_t* tokens, const int32_t* offsets, int32_t n,
+                 float* logits, int32_t* next_ids);
+/* Keep only the first lengths[i] cached positions of slot i (lengths[i] <= its length): drops the rows
+ * of rejected draft tokens after a verify pass. Pages stay assigned to the slot. */
+int shahd_truncate(ShahdSession* s, const int32_t* slots, const int32_t* lengths, int32_t n);
+
 /* Wait for the session's outstanding device work; returns the first recorded device error, if any. */
 int shahd_sync(ShahdSession* s);
 

@@ -8,7 +8,7 @@ ctypes and mirrors the reference's host-side interface over it:
   decode.cached_generate  — CachedGenerate
 Import with importlib (the directory name has dashes): importlib.import_module("shahd-llm-stack_b200").
 """
-from . import _lib, backend, build, checkpoint, configs, decode, sharding  # noqa: F401
+from . import _lib, backend, build, checkpoint, configs, decode, sharding, speculative  # noqa: F401
 from .backend import GpuBackend  # noqa: F401
 from .decode import (  # noqa: F401
     GREEDY, CachedDecoder, ModelConfig, Sampling, Session, cached_generate, init_params, sample_from_logits)

@@ -76,6 +76,8 @@ SIGNATURES = {
     "shahd_generate": (ctypes.c_int, [_vp, _ip, _ip, _i32, _i32, ctypes.POINTER(ShahdSampling), _up, _ip]),
     "shahd_generate_device": (ctypes.c_int, [_vp, _vp, _ip, _i32, _i32, ctypes.POINTER(ShahdSampling), _vp, _vp, _vp]),
     "shahd_sync": (ctypes.c_int, [_vp]),
+    "shahd_verify": (ctypes.c_int, [_vp, _ip, _ip, _ip, _i32, _fp, _ip]),
+    "shahd_truncate": (ctypes.c_int, [_vp, _ip, _ip, _i32]),
     "shahd_step_launches": (_i32, [_vp, _i32]),
     "shahd_kernel_launches": (_i64, [_vp]),
     "shahd_profile": (ctypes.c_int, [_vp, _i32]),

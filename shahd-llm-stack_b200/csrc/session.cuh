@@ -39,10 +39,12 @@ struct GraphKey {
   int min_rows;
   double temperature, top_p;  // sampling knobs baked into the sampler launch (temperature 0 = greedy)
   int top_k;
+  const void* logits;  // head output (verify passes run a head on prefill-style rows)
+  int head;
   bool operator<(const GraphKey& o) const {
-    return std::tie(kind, M, slot, tok, poff, prompt, out, out_ld, min_rows, temperature, top_p, top_k) <
+    return std::tie(kind, M, slot, tok, poff, prompt, out, out_ld, min_rows, temperature, top_p, top_k, logits, head) <
            std::tie(o.kind, o.M, o.slot, o.tok, o.poff, o.prompt, o.out, o.out_ld, o.min_rows, o.temperature, o.top_p,
-                    o.top_k);
+                    o.top_k, o.logits, o.head);
   }
 };
 
@@ -109,6 +111,12 @@ struct ShahdSession {
   CUtensorMap* d_step_wmaps = nullptr;
   std::map<int, CUtensorMap*> step_amaps;
   unsigned* d_step_sync = nullptr;  // [barrier counter, abort flag]
+  // verify passes (speculative decoding): per-row logits, argmax partials and ids, grown on demand
+  float* d_vlogits = nullptr;
+  float* d_vam_val = nullptr;
+  int* d_vam_idx = nullptr;
+  int* d_vids = nullptr;
+  int vrows_cap = 0;
   // split-K partial tiles of the norm-free projections, one region per decode chain
   float* split_ws;
   int* split_cnt;
@@ -117,7 +125,7 @@ struct ShahdSession {
   int *d_slot, *d_tok, *d_pos, *d_next, *d_gen_count, *d_ends, *d_starts, *d_full_len, *d_rows;
   uint32_t* d_rng;  // [max_seqs] SeededRng state per slot while a stochastic generate runs
   int* d_sampled;   // [max_seqs] ids the sampler chose this step
-  int *d_seq_plan;                              // [4][max_seqs]: prefill slot, context start, length, row offset
+  int *d_seq_plan;                              // [5][max_seqs]: slot, token start, length, row offset, base position
   int *d_row_slot, *d_row_pos, *d_row_poff;     // [rows_cap] expanded prefill rows
   int* d_prompt = nullptr;
   size_t prompt_cap = 0;
@@ -148,8 +156,8 @@ namespace {
 // Pinned staging rows (each max_seqs ints). A row is rewritten only after the stream has drained the
 // copies that read it, so no two uses between two stream synchronizations may share a row:
 // 0-1 per-call slots/tokens (or a generate's RNG states), 2-5 generate plan, 6 window-rebuild rows,
-// 7 lengths, 8-11 the prefill plan.
-constexpr int kStagingRows = 12;
+// 7 lengths, 8-12 the prefill plan.
+constexpr int kStagingRows = 13;
 constexpr int kStagingLengths = 7;
 constexpr int kPrefillRows = 8192;  // rows of one batched prefill chunk (whole sequences per chunk)
 constexpr int kMaxChains = 8;
@@ -237,6 +245,8 @@ struct StepPlan {
   int out_ld;
   long long attended;  // sum over rows of (position + 1): cached positions the attention reads
   ShahdSampling sampling;  // temperature > 0: seeded sampling from `logits` instead of the greedy argmax
+  float* am_val = nullptr;  // argmax partials of a head over more rows than max_seqs (verify passes)
+  int* am_idx = nullptr;
 };
 
 // ---- measurement hooks: kernel classes timed with CUDA events on the launching stream ---------------
@@ -401,7 +411,8 @@ int EnqueueStep(ShahdSession* s, const StepPlan& p, cudaStream_t st, int r0 = 0,
   // Row-indexed buffers: activations and positions hold rows_cap rows, the LM-head / finish / attention
   // split scratch holds max_seqs rows. This step uses rows [r0, r0 + M) of them (a decode chain's window).
   // A step beyond either is a caller bug, not a device fault.
-  if (p.M < 1 || r0 < 0 || r0 + p.M > s->rows_cap || ((p.head || p.finish) && r0 + p.M > s->max_seqs)) {
+  if (p.M < 1 || r0 < 0 || r0 + p.M > s->rows_cap ||
+      ((p.finish || (p.head && p.am_val == nullptr)) && r0 + p.M > s->max_seqs)) {
     SetError("internal: step of rows [%d, %d) exceeds the session's row buffers", r0, r0 + p.M);
     return -1;
   }
@@ -421,8 +432,8 @@ int EnqueueStep(ShahdSession* s, const StepPlan& p, cudaStream_t st, int r0 = 0,
   int* pos = s->d_pos + r0;
   // scratch that exists for decode rows only (r0 + M <= max_seqs when used)
   const size_t rd = (size_t)std::min(r0, s->max_seqs);
-  float* am_val = s->am_val + rd * s->am_stride;
-  int* am_idx = s->am_idx + rd * s->am_stride;
+  float* am_val = p.am_val ? p.am_val : s->am_val + rd * s->am_stride;
+  int* am_idx = p.am_idx ? p.am_idx : s->am_idx + rd * s->am_stride;
   int* gen_count = s->d_gen_count + rd;
   float* part_o = s->part_o + rd * s->H * s->max_blocks * s->d;
   float* part_m = s->part_m + rd * s->H * s->max_blocks;
@@ -590,7 +601,8 @@ int EnqueueChains(ShahdSession* s, const StepPlan* plans, const int* r0, int nch
 bool ChainsFit(ShahdSession* s, const StepPlan* plans, const int* r0, int nchain) {
   for (int c = 0; c < nchain; c++) {
     const StepPlan& p = plans[c];
-    if (p.M < 1 || r0[c] < 0 || r0[c] + p.M > s->rows_cap || ((p.head || p.finish) && r0[c] + p.M > s->max_seqs)) {
+    if (p.M < 1 || r0[c] < 0 || r0[c] + p.M > s->rows_cap ||
+        ((p.finish || (p.head && p.am_val == nullptr)) && r0[c] + p.M > s->max_seqs)) {
       SetError("internal: step of rows [%d, %d) exceeds the session's row buffers", r0[c], r0[c] + p.M);
       return false;
     }
@@ -621,7 +633,8 @@ int RunStep(ShahdSession* s, const StepPlan* plans, const int* r0, int nchain, i
   GraphKey key{(reps * 16 + kind) * 16 + nchain, p.M, p.slot, p.tok, p.poff, p.prompt, p.out_ids, p.out_ld,
                g_umma_min_rows * 4 + (int)g_use_pdl * 2 + (int)s->prof,
                p.sampling.temperature > 0 ? p.sampling.temperature : 0.0,
-               p.sampling.temperature > 0 ? p.sampling.top_p : 1.0, p.sampling.temperature > 0 ? p.sampling.top_k : 0};
+               p.sampling.temperature > 0 ? p.sampling.top_p : 1.0, p.sampling.temperature > 0 ? p.sampling.top_k : 0,
+               p.logits, (int)p.head};
   auto it = s->graphs.find(key);
   if (it == s->graphs.end()) {
     enqueue();
@@ -747,11 +760,11 @@ __global__ void ExpandPrefillRows(const int* plan, int max_seqs, int i0, int i1,
   const int i = i0 + blockIdx.x;
   if (i >= i1) return;
   const int slot = plan[i], start = plan[max_seqs + i], len = plan[2 * max_seqs + i];
-  const int off = plan[3 * max_seqs + i] - plan[3 * max_seqs + i0];
+  const int off = plan[3 * max_seqs + i] - plan[3 * max_seqs + i0], base = plan[4 * max_seqs + i];
   for (int t = threadIdx.x; t < len; t += blockDim.x) {
     row_slot[off + t] = slot;
-    row_pos[off + t] = t;
-    row_poff[off + t] = start;
+    row_pos[off + t] = base + t;     // the row's token is prompt[start + t] = prompt[poff + position]
+    row_poff[off + t] = start - base;
   }
 }
 
@@ -760,44 +773,81 @@ __global__ void ExpandPrefillRows(const int* plan, int max_seqs, int i0, int i1,
 // position before the attention of the same step reads positions 0..t of the row's slot, which is the
 // causal mask of the reference's tensor forward. Sequences go in chunks of whole sequences of at most
 // rows_cap rows. Slots must be reset with pages assigned; ids of sequence i are d_prompt[start_i + t].
+// Outputs of a verify pass: a head over every appended row (logits and per-row greedy ids).
+struct VerifyOut {
+  float* logits;  // [rows, V]
+  float* am_val;  // [rows, am_stride] argmax partials
+  int* am_idx;
+  int* ids;       // [rows]
+};
+
+__global__ void ArgmaxRowsKernel(const float* am_val, const int* am_idx, int nblk, int rows, int* ids) {
+  const int r = blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+  if (r >= rows) return;
+  float bv = -INFINITY;
+  int bi = 0x7fffffff;
+  for (int b = lane; b < nblk; b += 32) ArgmaxMerge(bv, bi, am_val[(size_t)r * nblk + b], am_idx[(size_t)r * nblk + b]);
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, bv, off);
+    const int oi = __shfl_xor_sync(0xffffffffu, bi, off);
+    ArgmaxMerge(bv, bi, ov, oi);
+  }
+  if (lane == 0) ids[r] = bi == 0x7fffffff ? 0 : bi;
+}
+
+// Appends slot i's tokens d_prompt[starts[i] + t], t < lens[i], at positions bases[i] + t (0 when bases is
+// null: PrefillCache). With `vo` (a verify pass, one chunk only) the LM head also runs on every row.
 int PrefillBatched(ShahdSession* s, const int* d_prompt, const std::vector<int>& slots, const std::vector<int>& starts,
-                   const std::vector<int>& lens) {
+                   const std::vector<int>& lens, const std::vector<int>* bases = nullptr,
+                   const VerifyOut* vo = nullptr) {
   const int n = (int)slots.size(), R = s->max_seqs;
-  int* h = Staging(s, 8);  // rows 8..11: slot, start, len, row offset
+  int* h = Staging(s, 8);  // rows 8..12: slot, start, len, row offset, base position
   long long off = 0;
   for (int i = 0; i < n; i++) {
     h[i] = slots[i];
     h[R + i] = starts[i];
     h[2 * R + i] = lens[i];
     h[3 * R + i] = (int)off;
+    h[4 * R + i] = bases ? (*bases)[i] : 0;
     off += lens[i];
   }
   if (off > 0) {
-    SHAHD_CUDA_TRY(cudaMemcpyAsync(s->d_seq_plan, h, sizeof(int) * 4 * (size_t)R, cudaMemcpyHostToDevice, s->stream));
+    SHAHD_CUDA_TRY(cudaMemcpyAsync(s->d_seq_plan, h, sizeof(int) * 5 * (size_t)R, cudaMemcpyHostToDevice, s->stream));
     for (int i0 = 0; i0 < n;) {
       int i1 = i0, rows = 0;
       long long attended = 0;
       while (i1 < n && rows + lens[i1] <= s->rows_cap) {
+        const long long b = bases ? (*bases)[i1] : 0;
         rows += lens[i1];
-        attended += (long long)lens[i1] * (lens[i1] + 1) / 2;
+        attended += (long long)lens[i1] * b + (long long)lens[i1] * (lens[i1] + 1) / 2;
         i1++;
       }
-      if (i1 == i0) {  // a sequence longer than a chunk: rows_cap >= block_size rules this out
-        SetError("PrefillCache: %d tokens exceed the prefill chunk of %d rows", lens[i0], s->rows_cap);
+      if (i1 == i0 || (vo && i1 < n)) {  // a sequence longer than a chunk: rows_cap >= block_size rules this out
+        SetError("PrefillCache: %lld tokens exceed the chunk of %d rows", vo ? off : (long long)lens[i0], s->rows_cap);
         return SHAHD_EINVAL;
       }
       if (rows > 0) {
         ExpandPrefillRows<<<i1 - i0, 128, 0, s->stream>>>(s->d_seq_plan, R, i0, i1, s->d_row_slot, s->d_row_pos,
                                                            s->d_row_poff);
         s->launches++;
-        StepPlan p{rows, s->d_row_pos, false, s->d_row_slot, nullptr, s->d_row_poff, d_prompt, false, nullptr, nullptr,
-                   nullptr, nullptr, 0, attended};
+        StepPlan p{rows, s->d_row_pos, false, s->d_row_slot, nullptr, s->d_row_poff, d_prompt, vo != nullptr,
+                   vo ? vo->logits : nullptr, nullptr, nullptr, nullptr, 0, attended};
+        if (vo) {
+          p.am_val = vo->am_val;
+          p.am_idx = vo->am_idx;
+        }
         SHAHD_TRY(RunStep(s, p, 0));
+        if (vo) {
+          ArgmaxRowsKernel<<<CeilDiv(rows, 4), 128, 0, s->stream>>>(vo->am_val, vo->am_idx, HeadBlocks(s, rows), rows,
+                                                                    vo->ids);
+          s->launches++;
+        }
       }
       i0 = i1;
     }
   }
-  for (int i = 0; i < n; i++) s->h_len[slots[i]] = lens[i];
+  for (int i = 0; i < n; i++) s->h_len[slots[i]] = (bases ? (*bases)[i] : 0) + lens[i];
   SHAHD_TRY(UploadLengths(s));
   return CheckLaunch("prefill");
 }
@@ -1124,7 +1174,7 @@ extern "C" int shahd_session_create(const ShahdModelCfg* cfg, const void* params
       (rc = DevAlloc(s, &s->d_full_len, (size_t)R)) != SHAHD_OK ||
       (rc = DevAlloc(s, &s->d_rows, (size_t)R)) != SHAHD_OK ||
       (rc = DevAlloc(s, &s->d_rng, (size_t)R)) != SHAHD_OK || (rc = DevAlloc(s, &s->d_sampled, (size_t)R)) != SHAHD_OK ||
-      (rc = DevAlloc(s, &s->d_seq_plan, (size_t)4 * R)) != SHAHD_OK ||
+      (rc = DevAlloc(s, &s->d_seq_plan, (size_t)5 * R)) != SHAHD_OK ||
       (rc = DevAlloc(s, &s->d_row_slot, (size_t)s->rows_cap)) != SHAHD_OK ||
       (rc = DevAlloc(s, &s->d_row_pos, (size_t)s->rows_cap)) != SHAHD_OK ||
       (rc = DevAlloc(s, &s->d_row_poff, (size_t)s->rows_cap)) != SHAHD_OK ||
@@ -1445,6 +1495,85 @@ extern "C" int shahd_profile_read(ShahdSession* s, int32_t kind, double* total_m
 }
 
 extern "C" int64_t shahd_kernel_launches(ShahdSession* s) { return s ? (int64_t)s->launches : -1; }
+
+extern "C" int shahd_verify(ShahdSession* s, const int32_t* slots, const int32_t* tokens, const int32_t* offsets,
+                            int32_t n, float* logits, int32_t* next_ids) {
+  ClearError();
+  if (!s || n < 1 || !slots || !tokens || !offsets || !next_ids) {
+    SetError("shahd_verify: bad arguments");
+    return SHAHD_EINVAL;
+  }
+  std::lock_guard<std::mutex> g(s->mu);
+  cudaSetDevice(s->device);
+  SHAHD_TRY(ValidateSlots(s, slots, n, "shahd_verify"));
+  if (offsets[0] != 0) {
+    SetError("shahd_verify: offsets must start at 0");
+    return SHAHD_EINVAL;
+  }
+  std::vector<int> sl(slots, slots + n), starts(n), lens(n), bases(n);
+  for (int i = 0; i < n; i++) {
+    lens[i] = offsets[i + 1] - offsets[i];
+    starts[i] = offsets[i];
+    bases[i] = s->h_len[slots[i]];
+    if (lens[i] < 1) {
+      SetError("shahd_verify: sequence %d has no tokens to verify", i);
+      return SHAHD_EINVAL;
+    }
+    if (bases[i] + lens[i] > s->C) {
+      SetError("shahd_verify: slot %d would reach position %d, outside the %d-token window", slots[i],
+               bases[i] + lens[i] - 1, s->C);
+      return SHAHD_EINVAL;
+    }
+  }
+  const int total = offsets[n];
+  if (total > s->rows_cap) {
+    SetError("shahd_verify: %d rows exceed the %d rows of one pass", total, s->rows_cap);
+    return SHAHD_EINVAL;
+  }
+  SHAHD_TRY(ValidateIds(s, tokens, total, "shahd_verify"));
+  SHAHD_CUDA_TRY(cudaStreamSynchronize(s->stream));
+  for (int i = 0; i < n; i++) SHAHD_TRY(EnsurePages(s, sl[i], bases[i] + lens[i]));
+  SHAHD_TRY(UploadTables(s));
+  if (total > s->vrows_cap) {
+    const int cap = std::max(total, 2 * s->vrows_cap);
+    SHAHD_TRY(DevAlloc(s, &s->d_vlogits, (size_t)cap * s->V));
+    SHAHD_TRY(DevAlloc(s, &s->d_vam_val, (size_t)cap * s->am_stride));
+    SHAHD_TRY(DevAlloc(s, &s->d_vam_idx, (size_t)cap * s->am_stride));
+    SHAHD_TRY(DevAlloc(s, &s->d_vids, (size_t)cap));
+    s->vrows_cap = cap;
+  }
+  SHAHD_TRY(GrowPrompt(s, total));
+  SHAHD_CUDA_TRY(cudaMemcpyAsync(s->d_prompt, tokens, sizeof(int) * total, cudaMemcpyHostToDevice, s->stream));
+  const VerifyOut vo{s->d_vlogits, s->d_vam_val, s->d_vam_idx, s->d_vids};
+  SHAHD_TRY(PrefillBatched(s, s->d_prompt, sl, starts, lens, &bases, &vo));
+  SHAHD_CUDA_TRY(cudaMemcpyAsync(next_ids, s->d_vids, sizeof(int) * total, cudaMemcpyDeviceToHost, s->stream));
+  if (logits)
+    SHAHD_CUDA_TRY(
+        cudaMemcpyAsync(logits, s->d_vlogits, sizeof(float) * (size_t)total * s->V, cudaMemcpyDeviceToHost, s->stream));
+  SHAHD_CUDA_TRY(cudaStreamSynchronize(s->stream));
+  return SHAHD_OK;
+}
+
+extern "C" int shahd_truncate(ShahdSession* s, const int32_t* slots, const int32_t* lengths, int32_t n) {
+  ClearError();
+  if (!s || n < 0 || (n > 0 && (!slots || !lengths))) {
+    SetError("shahd_truncate: bad arguments");
+    return SHAHD_EINVAL;
+  }
+  std::lock_guard<std::mutex> g(s->mu);
+  cudaSetDevice(s->device);
+  SHAHD_TRY(ValidateSlots(s, slots, n, "shahd_truncate"));
+  for (int i = 0; i < n; i++)
+    if (lengths[i] < 0 || lengths[i] > s->h_len[slots[i]]) {
+      SetError("shahd_truncate: slot %d holds %d positions, cannot keep %d", slots[i], s->h_len[slots[i]], lengths[i]);
+      return SHAHD_EINVAL;
+    }
+  SHAHD_CUDA_TRY(cudaStreamSynchronize(s->stream));
+  for (int i = 0; i < n; i++) s->h_len[slots[i]] = lengths[i];
+  SHAHD_TRY(UploadLengths(s));
+  SHAHD_CUDA_TRY(cudaStreamSynchronize(s->stream));
+  return SHAHD_OK;
+}
 
 extern "C" int shahd_sample_logits(const float* logits, int32_t rows, int32_t vocab, const ShahdSampling* opts,
                                    uint32_t* rng_states, int32_t* out_ids) {

@@ -166,6 +166,28 @@ class Session:
                                        nxt.ctypes.data_as(_ip)))
         return logits, nxt
 
+    def verify(self, slots, token_lists, want_logits: bool = False):
+        """Append each slot's tokens at its cached length with the LM head on every row (the target pass
+        of speculative decoding). Returns per slot the greedy id after each appended token (and the
+        logits rows when asked)."""
+        flat, offs = _pack(token_lists)
+        sl = _i32(slots)
+        ids = np.zeros(flat.size, dtype=np.int32)
+        logits = np.zeros((flat.size, self.cfg.vocab_size), dtype=np.float32) if want_logits else None
+        _lib.check(self.lib.shahd_verify(self.handle, sl.ctypes.data_as(_ip), flat.ctypes.data_as(_ip),
+                                         offs.ctypes.data_as(_ip), sl.size,
+                                         logits.ctypes.data_as(_fp) if logits is not None else None,
+                                         ids.ctypes.data_as(_ip)))
+        out_ids = [ids[offs[i]:offs[i + 1]] for i in range(sl.size)]
+        if want_logits:
+            return out_ids, [logits[offs[i]:offs[i + 1]] for i in range(sl.size)]
+        return out_ids
+
+    def truncate(self, slots, lengths) -> None:
+        """Keep only the first lengths[i] cached positions of each slot."""
+        sl, ln = _i32(slots), _i32(lengths)
+        _lib.check(self.lib.shahd_truncate(self.handle, sl.ctypes.data_as(_ip), ln.ctypes.data_as(_ip), sl.size))
+
     def generate(self, prompts, max_new: int, sampling: Sampling = GREEDY, rng_states=None) -> np.ndarray:
         """CachedGenerate for each prompt (slots 0..n-1): returns the new ids [n, max_new].
 

@@ -1,0 +1,103 @@
+"""Greedy speculative decoding on two GPU sessions: SpeculativeDecodeGreedy
+(Brain/Reasoning/SpeculativeDecode.ts:32-98) for many sequences at once.
+
+A draft session proposes up to Gamma tokens per sequence with cached greedy steps; the target session
+checks all of them in one verify pass (shahd_verify: the proposals are appended to its cache with the LM
+head on every row); each sequence keeps the longest prefix the target agrees with, plus the target's
+correction at the first disagreement or its bonus token when all were accepted. Rejected rows are then
+dropped from both caches (shahd_truncate). Within the context window the ids are those of plain greedy
+decoding with the target (SpeculativeDecode.ts:5-10); this implementation requires the whole run to fit
+the window (prompt + new tokens <= BlockSize of both models) instead of sliding it.
+
+Every id comes from a device argmax (first index of the max); the host only compares ids.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import numpy as np
+
+from .decode import Session
+
+
+@dataclass
+class SpeculativeResult:
+    ids: list            # per sequence: prompt + generated ids
+    target_calls: list   # verify passes each sequence took part in
+    draft_tokens: list   # tokens the draft proposed
+    accepted_tokens: list  # proposals the target accepted
+
+
+def speculative_decode_greedy(target: Session, draft: Session, prompts, max_new: int, gamma: int = 4,
+                              slots=None) -> SpeculativeResult:
+    """Decode each prompt with the target, using `draft` to propose `gamma` tokens per target pass."""
+    prompts = [[int(t) for t in p] for p in prompts]
+    n = len(prompts)
+    slots = list(range(n)) if slots is None else [int(x) for x in slots]
+    if any(len(p) == 0 for p in prompts):
+        raise ValueError("SpeculativeDecodeGreedy: empty prompt")
+    c_t, c_d = target.cfg.block_size, draft.cfg.block_size
+    for p in prompts:
+        if len(p) + max_new > min(c_t, c_d):
+            raise ValueError(f"speculative decoding here needs prompt + new tokens <= the context window "
+                             f"({len(p)} + {max_new} > {min(c_t, c_d)})")
+    ids = [list(p) for p in prompts]
+    calls, proposed_n, accepted_n = [0] * n, [0] * n, [0] * n
+    if max_new < 1:
+        return SpeculativeResult(ids, calls, proposed_n, accepted_n)
+    # both caches hold every id but the last one; the last id is fed by the next step or pass
+    for s in (target, draft):
+        s.prefill(slots, [p[:-1] for p in prompts])
+    dlen = [len(p) - 1 for p in prompts]  # the draft's cached length per sequence
+    while True:
+        active = [i for i in range(n) if len(ids[i]) - len(prompts[i]) < max_new]
+        if not active:
+            break
+        g = {i: min(gamma, c_t - 1, max_new - (len(ids[i]) - len(prompts[i]))) for i in active}
+        # the draft catches up on ids it has not cached yet (the target's bonus token of the last pass)
+        while True:
+            behind = [i for i in active if dlen[i] < len(ids[i]) - 1]
+            if not behind:
+                break
+            draft.step([slots[i] for i in behind], [ids[i][dlen[i]] for i in behind], want_logits=False)
+            for i in behind:
+                dlen[i] += 1
+        # 1) the draft proposes g[i] tokens greedily (cached steps, every sequence batched per step)
+        prop = {i: [] for i in active}
+        for k in range(max(g.values())):
+            rows = [i for i in active if g[i] > k]
+            feed = [ids[i][-1] if k == 0 else prop[i][-1] for i in rows]
+            _, nxt = draft.step([slots[i] for i in rows], feed, want_logits=False)
+            for i, t in zip(rows, nxt):
+                prop[i].append(int(t))
+                dlen[i] += 1
+        for i in active:
+            proposed_n[i] += g[i]
+        # 2) the target checks all proposals of every sequence in one pass
+        checks = target.verify([slots[i] for i in active], [[ids[i][-1]] + prop[i] for i in active])
+        keep_t, keep_d = [], []
+        for i, t_ids in zip(active, checks):
+            calls[i] += 1
+            corrected = False
+            acc = 0
+            for j in range(g[i]):
+                if int(t_ids[j]) == prop[i][j]:
+                    ids[i].append(prop[i][j])
+                    acc += 1
+                    accepted_n[i] += 1
+                    if len(ids[i]) - len(prompts[i]) >= max_new:
+                        break
+                else:
+                    ids[i].append(int(t_ids[j]))  # correction at the first divergence
+                    corrected = True
+                    break
+            # 3) all accepted with budget left: the target's own next argmax is free
+            if not corrected and acc == g[i] and len(ids[i]) - len(prompts[i]) < max_new:
+                ids[i].append(int(t_ids[g[i]]))
+            keep_t.append(len(ids[i]) - 1)
+            dlen[i] = min(dlen[i], len(ids[i]) - 1)
+            keep_d.append(dlen[i])
+        # 4) rows of rejected proposals leave both caches
+        target.truncate([slots[i] for i in active], keep_t)
+        draft.truncate([slots[i] for i in active], keep_d)
+    return SpeculativeResult([x[:len(p) + max_new] for x, p in zip(ids, prompts)], calls, proposed_n, accepted_n)
