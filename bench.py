@@ -40,6 +40,22 @@ def prompts_for(w, rank: int) -> np.ndarray:
     return pkg.sharding.shard_prompts(w, rank)
 
 
+def step_roofline(w, ms_per_job: float, peaks: dict, peak_kind: str) -> dict:
+    """The hot-path step roofline: algorithmic bytes of every decode step of the job (all projection
+    weights once per step, each sequence's cached K/V rows read and its new K/V row written, the embedding
+    row) over the timed job time (prefill included in the time, not in the bytes: a lower bound)."""
+    m = w.model
+    weights = 2.0 * m.matrix_params()
+    kv_pos = m.num_layers * m.kv * 2 * m.head_dim * 2  # bytes of one cached position, all layers
+    p0 = w.prompt_len - 1  # position of the first decode step's token
+    attended = sum(p0 + k + 1 for k in range(w.new_tokens))  # cached positions read per sequence
+    job = w.new_tokens * (weights + w.seqs * (kv_pos + 2 * m.embed_dim)) + w.seqs * kv_pos * attended
+    achieved = job / (ms_per_job / 1000.0) / 1e9
+    return {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+            "frac": achieved / peaks["hbm_gbs"], "algorithmic_bytes_per_job": job, "peak_source": peak_kind,
+            "scope": "all decode steps of the timed job (weights per step + KV rows read/written)"}
+
+
 def load_peaks() -> tuple[dict, str]:
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(p):
@@ -299,6 +315,7 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
         "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": int(prompts.nbytes + offs.nbytes),
                 "d2h_bytes_per_step": int(w.seqs * w.new_tokens * 4)},
         "roofline": roofline,
+        "roofline_step": step_roofline(w, ms_per_step, peaks, peak_kind),
         "cpu_baseline": cpu,
         "clocks": clk,
         "gpu_launches": int(launches),
