@@ -879,7 +879,7 @@ __global__ void __launch_bounds__(kAttnThreads) AttnDecodeGenericKernel(AttnArgs
 struct FinishArgs {
   int M;
   const int* slot;
-  const int* pos;
+  int* pos;
   int* seq_len;
   const float* am_val;  // [M, nblk] or nullptr (no head this step)
   const int* am_idx;
@@ -890,6 +890,13 @@ struct FinishArgs {
   int out_ld;
   int* gen_count;   // [M]
   const int* sampled;  // [M] ids chosen by the sampler (stochastic decoding), or nullptr for greedy
+  // decode loop only (wte != nullptr): embed each row's chosen id as the next step's input and advance its
+  // position, so that step needs no embed kernel (rows whose window is full are left to the rebuild)
+  const float* wte;
+  const float* wpe;  // nullptr for RoPE models
+  float* x;
+  bf16* xb;
+  int E, ldxb, C;
 };
 
 __global__ void FinishKernel(FinishArgs f) {
@@ -914,6 +921,20 @@ __global__ void FinishKernel(FinishArgs f) {
       ArgmaxMerge(bv, bi, ov, oi);
     }
     id = bi == 0x7fffffff ? 0 : bi;
+  }
+  if (f.wte != nullptr) {  // EmbeddingLookup (+ learned position) of the next step's token, Embedding.ts:14-26
+    const int np = f.pos[r] + 1;
+    if (np < f.C) {
+      const float* src = f.wte + (size_t)id * f.E;
+      const float* pe = f.wpe ? f.wpe + (size_t)np * f.E : nullptr;
+      for (int j = lane; j < f.E; j += 32) {
+        const float v = pe ? src[j] + pe[j] : src[j];
+        f.x[(size_t)r * f.E + j] = v;
+        f.xb[(size_t)r * f.ldxb + j] = __float2bfloat16_rn(v);
+      }
+    }
+    __syncwarp();
+    if (lane == 0) f.pos[r] = np;
   }
   if (lane != 0) return;
   if (f.next_ids) f.next_ids[r] = id;

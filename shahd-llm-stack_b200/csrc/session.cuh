@@ -40,7 +40,7 @@ struct GraphKey {
   double temperature, top_p;  // sampling knobs baked into the sampler launch (temperature 0 = greedy)
   int top_k;
   const void* logits;  // head output (verify passes run a head on prefill-style rows)
-  int head;
+  int head;            // 2 * embed_ready of the first step + head
   bool operator<(const GraphKey& o) const {
     return std::tie(kind, M, slot, tok, poff, prompt, out, out_ld, min_rows, temperature, top_p, top_k, logits, head) <
            std::tie(o.kind, o.M, o.slot, o.tok, o.poff, o.prompt, o.out, o.out_ld, o.min_rows, o.temperature, o.top_p,
@@ -247,6 +247,7 @@ struct StepPlan {
   ShahdSampling sampling;  // temperature > 0: seeded sampling from `logits` instead of the greedy argmax
   float* am_val = nullptr;  // argmax partials of a head over more rows than max_seqs (verify passes)
   int* am_idx = nullptr;
+  bool embed_ready = false;  // x, xb and positions already hold this step's input (previous finish kernel)
 };
 
 // ---- measurement hooks: kernel classes timed with CUDA events on the launching stream ---------------
@@ -405,6 +406,12 @@ const CUtensorMap* StepActivationMaps(ShahdSession* s, int M) {
   return d;
 }
 
+// Whether a step's finish kernel also embeds the next step's input (decode-loop steps), so that the
+// following step skips its embed kernel.
+bool EmbedsNext(const StepPlan& p) {
+  return p.finish && p.head && p.cur_tok != nullptr && p.out_ids != nullptr;
+}
+
 // Enqueue one batched cached step (AdvanceOneToken + HeadLogitsRow for M rows) on `st`; returns the
 // number of kernels it launched.
 int EnqueueStep(ShahdSession* s, const StepPlan& p, cudaStream_t st, int r0 = 0, int chain = 0) {
@@ -493,10 +500,12 @@ int EnqueueStep(ShahdSession* s, const StepPlan& p, cudaStream_t st, int r0 = 0,
     }, 4.0 * s->Hk * s->d * s->L, (double)p.attended, chain);
     nblk = CeilDiv(s->V, s->step_bn[4]);
   } else {
-    Timed(s, st, pk + kProfOther, 8.0 * M * s->E, [&] {
-      EmbedArgs e{p.pos_in, p.slot, p.tok, p.prompt, p.poff, s->d_seq_len, pos, s->wte, s->wpe, x, xb, s->E, s->Ep};
-      LaunchPdl(EmbedKernel, dim3(M), dim3(128), 0, st, e);
-    });
+    if (!p.embed_ready) {
+      Timed(s, st, pk + kProfOther, 8.0 * M * s->E, [&] {
+        EmbedArgs e{p.pos_in, p.slot, p.tok, p.prompt, p.poff, s->d_seq_len, pos, s->wte, s->wpe, x, xb, s->E, s->Ep};
+        LaunchPdl(EmbedKernel, dim3(M), dim3(128), 0, st, e);
+      });
+    }
     KvView kv{s->kv_pool, s->d_block_table, s->max_blocks, s->Hk, s->d, s->page_elems};
     // K and V rows read (bf16) + q read and ctx written (fp32 + bf16)
     const double attn_fixed = 10.0 * M * hd, attn_per_pos = 4.0 * s->Hk * s->d;
@@ -541,8 +550,8 @@ int EnqueueStep(ShahdSession* s, const StepPlan& p, cudaStream_t st, int r0 = 0,
     if (p.head) {
       // final norm + LM head + argmax partials (HeadLogitsRow, CachedRowMath.ts:117-137)
       nblk = HeadBlocks(s, M);
-      const LinearArgs lh = Lin(x, s->E, xb, s->Ep, R, M, s->E, s->Ep, s->w_head, s->V, eps, s->head_c1, s->head_c2,
-                                am_val, am_idx);
+      const LinearArgs lh = Lin(x, s->E, xb, s->Ep, R, M, s->E, s->Ep, s->w_head, s->V, eps, s->head_c1,
+                                s->head_c2, am_val, am_idx);
       Timed(s, st, pk + kProfLinear, LinearBytes(M, s->E, s->Ep, s->V),
             [&] { LaunchLinear(norm, lh, EpiLogits{p.logits, s->head_bias, s->V}, st); });
     }
@@ -558,7 +567,14 @@ int EnqueueStep(ShahdSession* s, const StepPlan& p, cudaStream_t st, int r0 = 0,
   }
   if (p.finish) {
     FinishArgs f{M, p.slot, pos, s->d_seq_len, p.head ? am_val : nullptr, am_idx, nblk, p.next_ids,
-                 p.cur_tok, p.out_ids, p.out_ld, gen_count, sampled};
+                 p.cur_tok, p.out_ids, p.out_ld, gen_count, sampled, nullptr, nullptr, nullptr, nullptr,
+                 s->E, s->Ep, s->C};
+    if (EmbedsNext(p)) {
+      f.wte = s->wte;
+      f.wpe = s->wpe;
+      f.x = x;
+      f.xb = xb;
+    }
     Timed(s, st, pk + kProfOther, 16.0 * M, [&] { LaunchPdl(FinishKernel, dim3(CeilDiv(M, 4)), dim3(128), 0, st, f); });
   }
   return (int)(s->launches - before);
@@ -620,9 +636,12 @@ int RunStep(ShahdSession* s, const StepPlan* plans, const int* r0, int nchain, i
   // on the device, so back-to-back steps need no host update in between
   auto enqueue = [&]() {
     int total = 0;
+    StepPlan pl[kMaxChains];
+    for (int c = 0; c < nchain; c++) pl[c] = plans[c];
     for (int j = 0; j < reps; j++) {
       s->cur_rep = j;
-      total += EnqueueChains(s, plans, r0, nchain);
+      total += EnqueueChains(s, pl, r0, nchain);
+      for (int c = 0; c < nchain; c++) pl[c].embed_ready = EmbedsNext(pl[c]);  // the finish kernel embedded the next input
     }
     s->cur_rep = 0;
     return total;
@@ -634,7 +653,7 @@ int RunStep(ShahdSession* s, const StepPlan* plans, const int* r0, int nchain, i
                g_umma_min_rows * 4 + (int)g_use_pdl * 2 + (int)s->prof,
                p.sampling.temperature > 0 ? p.sampling.temperature : 0.0,
                p.sampling.temperature > 0 ? p.sampling.top_p : 1.0, p.sampling.temperature > 0 ? p.sampling.top_k : 0,
-               p.logits, (int)p.head};
+               p.logits, (int)p.head + 2 * (int)p.embed_ready};
   auto it = s->graphs.find(key);
   if (it == s->graphs.end()) {
     enqueue();
@@ -969,6 +988,7 @@ int GenerateCore(ShahdSession* s, const int* d_prompt_packed, const std::vector<
                                               ns, k - 1, keep, s->d_window);
       s->launches++;
       SHAHD_TRY(PrefillBatched(s, s->d_window, slide, wstart, wlen));
+      for (int c = 0; c < nchain; c++) plans[c].embed_ready = false;  // the rebuild reused the activation rows
     }
     for (int c = 0; c < nchain; c++) {
       plans[c].attended = 0;
@@ -979,6 +999,7 @@ int GenerateCore(ShahdSession* s, const int* d_prompt_packed, const std::vector<
     for (int i = 0; i < n; i++) maxlen = std::max(maxlen, s->h_len[i]);
     const int reps = std::max(1, std::min({kStepsPerGraph, max_new - k, C - maxlen}));
     SHAHD_TRY(RunStep(s, plans, r0, nchain, 1, reps));
+    for (int c = 0; c < nchain; c++) plans[c].embed_ready = EmbedsNext(plans[c]);  // next input embedded
     for (int i = 0; i < n; i++) s->h_len[i] += reps;
     k += reps - 1;
   }
