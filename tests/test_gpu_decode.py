@@ -257,3 +257,13 @@ def test_persistent_step_agrees_with_per_kernel_path():
             odec.push(int(t))
         s = np.sort(odec.logits)
         assert s[-1] - s[-2] <= TOL_BF16 * (odec.logits.max() - odec.logits.min()), (i, k)
+
+
+def test_fused_attention_shape_parity():
+    # the FusedAttention config's attention shape: 8 query heads over 2 kv heads (GQA 4), head_dim 64,
+    # RoPE base 10000, causal prefill of 511 positions then cached decode steps to the end of a 512 window
+    cfg = pkg.ModelConfig(embed_dim=512, num_layers=1, num_heads=8, kv_heads=2, block_size=512, vocab_size=512,
+                          mlp_hidden=1024, position_scheme="Rope", norm_kind="RmsNorm", mlp_kind="SwiGlu")
+    w = pkg.configs.Workload("attention", cfg, weight_seed=3, seqs=2, prompt_len=512, new_tokens=0)
+    worst = _teacher_forced_shape(w, nseq=2, prompt_len=508, steps=4)
+    assert worst < TOL_BF16
