@@ -19,6 +19,7 @@
 #include "../../include/shahd_b200.h"
 #include "decode_kernels.cuh"
 #include "params.h"
+#include "prefill_attention.cuh"
 #include "sampling.cuh"
 #include "step_kernel.cuh"
 #include "umma_linear.cuh"
@@ -41,10 +42,12 @@ struct GraphKey {
   int top_k;
   const void* logits;  // head output (verify passes run a head on prefill-style rows)
   int head;            // 2 * embed_ready of the first step + head
+  int plan_i0, plan_n, plan_qblocks;  // the prefill plan entries a prefill-style step attends over
   bool operator<(const GraphKey& o) const {
-    return std::tie(kind, M, slot, tok, poff, prompt, out, out_ld, min_rows, temperature, top_p, top_k, logits, head) <
+    return std::tie(kind, M, slot, tok, poff, prompt, out, out_ld, min_rows, temperature, top_p, top_k, logits, head,
+                    plan_i0, plan_n, plan_qblocks) <
            std::tie(o.kind, o.M, o.slot, o.tok, o.poff, o.prompt, o.out, o.out_ld, o.min_rows, o.temperature, o.top_p,
-                    o.top_k, o.logits, o.head);
+                    o.top_k, o.logits, o.head, o.plan_i0, o.plan_n, o.plan_qblocks);
   }
 };
 
@@ -248,6 +251,11 @@ struct StepPlan {
   float* am_val = nullptr;  // argmax partials of a head over more rows than max_seqs (verify passes)
   int* am_idx = nullptr;
   bool embed_ready = false;  // x, xb and positions already hold this step's input (previous finish kernel)
+  // prefill-style chunks: the chunk's sequences as entries plan_i0 .. plan_i0 + plan_n - 1 of the prefill
+  // plan, for the tiled causal attention (plan_qblocks = 64-query blocks of the longest sequence)
+  const int* seq_plan = nullptr;
+  int plan_i0 = 0, plan_n = 0, plan_qblocks = 0;
+  long long kv_streamed = 0;  // cached positions the tiled kernel reads: per sequence and query block, keys 0 .. last query
 };
 
 // ---- measurement hooks: kernel classes timed with CUDA events on the launching stream ---------------
@@ -292,6 +300,16 @@ void Timed(ShahdSession* s, cudaStream_t st, int kind, double bytes, F&& launch,
   else s->prof_recs.push_back({kind, e0, e1, bytes + per_attended * attended, 0.0, chain, 0});
 }
 
+// A prefill-style step whose attention runs as query-block tiles (PrefillAttnKernel) rather than per row.
+bool PrefillTiled(const ShahdSession* s, const StepPlan& p) {
+  return p.seq_plan != nullptr && p.plan_n > 0 && s->G <= kPfMaxG && (s->d == 32 || s->d == 64 || s->d == 128);
+}
+
+// Cached positions an attention launch of plan p reads per kv head and layer.
+double AttendedPositions(const ShahdSession* s, const StepPlan& p) {
+  return (double)(PrefillTiled(s, p) ? p.kv_streamed : p.attended);
+}
+
 // Adds the event times of finished records to the per-class totals (the stream must be idle). plans
 // (graph replays) give the cached lengths of the replayed steps: rep j of a chain attends j more
 // positions per row than its first step.
@@ -301,7 +319,7 @@ int Accumulate(ShahdSession* s, const std::vector<ProfRec>& recs, const StepPlan
     SHAHD_CUDA_TRY(cudaEventElapsedTime(&t, r.e0, r.e1));
     double b = r.bytes;
     if (plans && r.per_attended > 0)
-      b += r.per_attended * ((double)plans[r.chain].attended + (double)r.rep * plans[r.chain].M);
+      b += r.per_attended * (AttendedPositions(s, plans[r.chain]) + (double)r.rep * plans[r.chain].M);
     s->prof_ms[r.kind] += t;
     s->prof_bytes[r.kind] += b;
     s->prof_n[r.kind] += 1;
@@ -523,12 +541,20 @@ int EnqueueStep(ShahdSession* s, const StepPlan& p, cudaStream_t st, int r0 = 0,
       AttnArgs aa{q, ctx, ctxb, s->HDp, kv, l, pos, p.slot, s->H, s->Hk, s->G, s->d,
                   (float)(1.0 / std::sqrt((double)s->d)), s->max_blocks, part_o, part_m, part_l, counter};
       dim3 ag(nsplit, s->Hk, M);
+      const bool tiled = PrefillTiled(s, p);
+      const PrefillAttnArgs pa{q, ctx, ctxb, s->HDp, kv, l, s->H, s->Hk, s->G,
+                               (float)(1.0 / std::sqrt((double)s->d)), p.seq_plan, s->max_seqs, p.plan_i0};
+      const dim3 pg(p.plan_qblocks, s->Hk, p.plan_n);
       Timed(s, st, pk + kProfAttention, attn_fixed, [&] {
-        if (s->d == 64) LaunchPdl(AttnDecodeKernel<64>, ag, dim3(kAttnThreads), AttnSmemBytes(64), st, aa);
+        if (tiled) {
+          if (s->d == 64) LaunchPdl(PrefillAttnKernel<64>, pg, dim3(kPfThreads), PrefillAttnSmem(64), st, pa);
+          else if (s->d == 32) LaunchPdl(PrefillAttnKernel<32>, pg, dim3(kPfThreads), PrefillAttnSmem(32), st, pa);
+          else LaunchPdl(PrefillAttnKernel<128>, pg, dim3(kPfThreads), PrefillAttnSmem(128), st, pa);
+        } else if (s->d == 64) LaunchPdl(AttnDecodeKernel<64>, ag, dim3(kAttnThreads), AttnSmemBytes(64), st, aa);
         else if (s->d == 32) LaunchPdl(AttnDecodeKernel<32>, ag, dim3(kAttnThreads), AttnSmemBytes(32), st, aa);
         else if (s->d == 128) LaunchPdl(AttnDecodeKernel<128>, ag, dim3(kAttnThreads), AttnSmemBytes(128), st, aa);
         else LaunchPdl(AttnDecodeGenericKernel, ag, dim3(kAttnThreads), 0, st, aa);
-      }, attn_per_pos, (double)p.attended, chain);
+      }, attn_per_pos, AttendedPositions(s, p), chain);
       // summed per-head Wo + residual (CachedForward.ts:81-84)
       LinearArgs lo = Lin(ctx, hd, ctxb, s->HDp, R, M, hd, s->HDp, Ly.w_o, s->E, eps, nullptr, nullptr);
       lo.ws = split_ws;
@@ -653,7 +679,7 @@ int RunStep(ShahdSession* s, const StepPlan* plans, const int* r0, int nchain, i
                g_umma_min_rows * 4 + (int)g_use_pdl * 2 + (int)s->prof,
                p.sampling.temperature > 0 ? p.sampling.temperature : 0.0,
                p.sampling.temperature > 0 ? p.sampling.top_p : 1.0, p.sampling.temperature > 0 ? p.sampling.top_k : 0,
-               p.logits, (int)p.head + 2 * (int)p.embed_ready};
+               p.logits, (int)p.head + 2 * (int)p.embed_ready, p.plan_i0, p.plan_n, p.plan_qblocks};
   auto it = s->graphs.find(key);
   if (it == s->graphs.end()) {
     enqueue();
@@ -852,6 +878,16 @@ int PrefillBatched(ShahdSession* s, const int* d_prompt, const std::vector<int>&
         s->launches++;
         StepPlan p{rows, s->d_row_pos, false, s->d_row_slot, nullptr, s->d_row_poff, d_prompt, vo != nullptr,
                    vo ? vo->logits : nullptr, nullptr, nullptr, nullptr, 0, attended};
+        int longest = 0;
+        for (int i = i0; i < i1; i++) {
+          longest = std::max(longest, lens[i]);
+          const long long b = bases ? (*bases)[i] : 0;
+          for (int qb = 0; qb < lens[i]; qb += kPfQ) p.kv_streamed += b + std::min(lens[i], qb + kPfQ);
+        }
+        p.seq_plan = s->d_seq_plan;
+        p.plan_i0 = i0;
+        p.plan_n = i1 - i0;
+        p.plan_qblocks = CeilDiv(longest, kPfQ);
         if (vo) {
           p.am_val = vo->am_val;
           p.am_idx = vo->am_idx;
@@ -1214,6 +1250,9 @@ extern "C" int shahd_session_create(const ShahdModelCfg* cfg, const void* params
   cudaFuncSetAttribute(AttnDecodeKernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, AttnSmemBytes(32));
   cudaFuncSetAttribute(AttnDecodeKernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, AttnSmemBytes(64));
   cudaFuncSetAttribute(AttnDecodeKernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, AttnSmemBytes(128));
+  cudaFuncSetAttribute(PrefillAttnKernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, PrefillAttnSmem(32));
+  cudaFuncSetAttribute(PrefillAttnKernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, PrefillAttnSmem(64));
+  cudaFuncSetAttribute(PrefillAttnKernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, PrefillAttnSmem(128));
   cudaMemset(s->attn_counter, 0, sizeof(int) * (size_t)R * s->Hk);
   cudaMemset(s->d_seq_len, 0, sizeof(int) * R);
   if (cudaDeviceSynchronize() != cudaSuccess) {
