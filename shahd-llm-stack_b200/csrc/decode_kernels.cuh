@@ -806,6 +806,229 @@ __global__ void __launch_bounds__(kAttnThreads) AttnDecodeKernel(AttnArgs aa) {
   AttnFinishSplit(aa, m, g, so, s_m, s_l);
 }
 
+// ---- decode-step attention with the cache read ahead of the predecessor --------------------------------
+// In a decode step every row appends exactly one position (its own slot): the K/V rows of positions
+// 0 .. p-1 were written by earlier steps, the block table and the row's position and slot by earlier
+// launches. With programmatic dependent launch this kernel starts once the QKV projection of the layer has
+// passed its own grid-dependency wait, i.e. after every launch before that projection has completed, so
+// all of those are read before this kernel's wait, and only q and the K/V row at p (written by the
+// projection) after it. The cached rows then arrive while the projection still runs.
+//
+// One CTA of 8 warps per (split, kv head, row); a warp task is 32 consecutive positions (lane = position
+// for the scores, lane = D/32 dims for P·V): the K row of its position as D/8 16-byte loads, and for the
+// 32 positions the lane's slice of each V row (coalesced 64..256-byte rows). Each warp keeps a running max
+// and sum per head; the warps' states merge in shared memory, the splits through AttnFinishSplit.
+constexpr int kAttnRowWarps = 8;
+constexpr int kAttnRowThreads = kAttnRowWarps * 32;
+constexpr int kAttnTask = 32;  // positions per warp task (a task never straddles a 64-position page)
+
+__host__ __device__ constexpr int AttnRowsSmem(int G, int D) {
+  // q [G][D] (reused for the merged output), warp outputs [warps][G][D], warp max/sum, merged max/sum
+  return (G * D + kAttnRowWarps * G * D + 2 * kAttnRowWarps * G + 2 * G) * 4;
+}
+
+template <int D> struct VSlice;  // the D/32 bf16 dims of one V row that a lane owns
+template <> struct VSlice<32> { using T = unsigned short; };
+template <> struct VSlice<64> { using T = unsigned int; };
+template <> struct VSlice<128> { using T = uint2; };
+
+__device__ __forceinline__ void VSliceToFloat(unsigned short v, float (&f)[1]) { f[0] = __uint_as_float((unsigned)v << 16); }
+__device__ __forceinline__ void VSliceToFloat(unsigned int v, float (&f)[2]) {
+  f[0] = __uint_as_float(v << 16);
+  f[1] = __uint_as_float(v & 0xffff0000u);
+}
+__device__ __forceinline__ void VSliceToFloat(uint2 v, float (&f)[4]) {
+  f[0] = __uint_as_float(v.x << 16);
+  f[1] = __uint_as_float(v.x & 0xffff0000u);
+  f[2] = __uint_as_float(v.y << 16);
+  f[3] = __uint_as_float(v.y & 0xffff0000u);
+}
+__device__ __forceinline__ void PrefetchL2(const void* ptr) { asm volatile("prefetch.global.L2 [%0];" ::"l"(ptr)); }
+
+// MG: a power of two >= G (per-head state lives in registers sized by it)
+template <int D, int MG>
+__global__ void __launch_bounds__(kAttnRowThreads, D <= 64 ? 2 : 1) AttnRowsKernel(AttnArgs aa) {
+  constexpr int JPL = D / 32;
+  using VT = typename VSlice<D>::T;
+  extern __shared__ __align__(16) float ar_smem[];
+  const int G = aa.G;
+  float* sq = ar_smem;                     // [G][D] q pre-scaled; later the merged output
+  float* wo = sq + G * D;                  // [warps][G][D]
+  float* wm = wo + kAttnRowWarps * G * D;  // [warps][G]
+  float* wl = wm + kAttnRowWarps * G;      // [warps][G]
+  float* mm = wl + kAttnRowWarps * G;      // [G]
+  float* ml = mm + G;                      // [G]
+  const int g = blockIdx.y, m = blockIdx.z;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  // ---- before the wait: launches older than the predecessor only ----
+  const int p = __ldcg(aa.pos + m), slot = __ldcg(aa.slot + m);
+  const int ntask = p / kAttnTask + 1;
+  const int per = CeilDiv(ntask, (int)gridDim.x);
+  const int c0 = blockIdx.x * per, c1 = min(ntask, c0 + per);
+  const size_t head_off = (size_t)((aa.layer * aa.Hk + g) * 2) * kPageTokens * D;
+  // K and V rows of task c (position c*32 + row); nullptr when the page is missing (recorded as an error)
+  auto task_base = [&](int c) -> const bf16* {
+    const int page = __ldcg(aa.kv.block_table + (size_t)slot * aa.kv.max_blocks + (c * kAttnTask) / kPageTokens);
+    if (page < 0) {
+      atomicCAS(&g_shahd_device_error, 0, kDevErrNoPage);
+      return nullptr;
+    }
+    return aa.kv.pool + (size_t)page * aa.kv.page_elems + head_off + (size_t)((c * kAttnTask) % kPageTokens) * D;
+  };
+  uint4 kr[D / 8];
+  VT vs[kAttnTask];
+#pragma unroll
+  for (int i = 0; i < D / 8; i++) kr[i] = make_uint4(0, 0, 0, 0);
+#pragma unroll
+  for (int t = 0; t < kAttnTask; t++) vs[t] = VT{};
+  // rows of task c at positions [lo, hi)
+  auto load_rows = [&](const bf16* kb, int c, int lo, int hi) {
+    const int t0 = c * kAttnTask;
+    if (t0 + lane >= lo && t0 + lane < hi) {
+      const uint4* kp = reinterpret_cast<const uint4*>(kb + (size_t)lane * D);
+#pragma unroll
+      for (int i = 0; i < D / 8; i++) kr[i] = __ldcg(kp + i);
+    }
+    const bf16* vb = kb + (size_t)kPageTokens * D;
+#pragma unroll
+    for (int t = 0; t < kAttnTask; t++)
+      if (t0 + t >= lo && t0 + t < hi) vs[t] = __ldcg(reinterpret_cast<const VT*>(vb + (size_t)t * D) + lane);
+  };
+  int c = c0 + warp;
+  const bf16* kb = c < c1 ? task_base(c) : nullptr;
+  if (kb) load_rows(kb, c, 0, p);
+  for (int cc = c + kAttnRowWarps; cc < c1; cc += kAttnRowWarps) {  // later tasks of this warp: into L2
+    const bf16* b = task_base(cc);
+    if (b && cc * kAttnTask + lane < p) {
+      for (int i = 0; i < D * 2; i += 128) PrefetchL2(reinterpret_cast<const char*>(b + (size_t)lane * D) + i);
+      for (int i = 0; i < D * 2; i += 128)
+        PrefetchL2(reinterpret_cast<const char*>(b + (size_t)(kPageTokens + lane) * D) + i);
+    }
+  }
+
+  GridDepWait();
+  GridDepLaunch();
+  // ---- after the wait: q and the row at p ----
+  const int hd = aa.H * D;
+  for (int e = threadIdx.x; e < G * D; e += blockDim.x) sq[e] = __ldcg(aa.q + (size_t)m * hd + g * G * D + e) * aa.scale;
+  if (kb) load_rows(kb, c, p, p + 1);
+  __syncthreads();
+
+  float o[MG][JPL], mrun[MG], lrun[MG];
+#pragma unroll
+  for (int i = 0; i < MG; i++) {
+    mrun[i] = -INFINITY;
+    lrun[i] = 0.f;
+#pragma unroll
+    for (int j = 0; j < JPL; j++) o[i][j] = 0.f;
+  }
+  bool first = true;
+  for (; c < c1; c += kAttnRowWarps) {
+    if (!first) {
+      kb = task_base(c);
+#pragma unroll
+      for (int t = 0; t < kAttnTask; t++) vs[t] = VT{};
+      if (kb) load_rows(kb, c, 0, p + 1);
+    }
+    first = false;
+    if (kb == nullptr) continue;  // missing page: its positions are left out (the error flag is set)
+    const bool valid = c * kAttnTask + lane <= p;
+    // scores of this lane's position for the G heads
+    float acc[MG];
+#pragma unroll
+    for (int i = 0; i < MG; i++) acc[i] = 0.f;
+#pragma unroll
+    for (int k = 0; k < D / 8; k++) {
+      const uint32_t w[4] = {kr[k].x, kr[k].y, kr[k].z, kr[k].w};
+      float kf[8];
+#pragma unroll
+      for (int u = 0; u < 4; u++) {
+        kf[2 * u] = __uint_as_float(w[u] << 16);
+        kf[2 * u + 1] = __uint_as_float(w[u] & 0xffff0000u);
+      }
+#pragma unroll
+      for (int i = 0; i < MG; i++) {
+        if (i < G) {
+          const float4 q0 = *reinterpret_cast<const float4*>(sq + i * D + 8 * k);
+          const float4 q1 = *reinterpret_cast<const float4*>(sq + i * D + 8 * k + 4);
+          acc[i] = fmaf(q0.x, kf[0], acc[i]);
+          acc[i] = fmaf(q0.y, kf[1], acc[i]);
+          acc[i] = fmaf(q0.z, kf[2], acc[i]);
+          acc[i] = fmaf(q0.w, kf[3], acc[i]);
+          acc[i] = fmaf(q1.x, kf[4], acc[i]);
+          acc[i] = fmaf(q1.y, kf[5], acc[i]);
+          acc[i] = fmaf(q1.z, kf[6], acc[i]);
+          acc[i] = fmaf(q1.w, kf[7], acc[i]);
+        }
+      }
+    }
+    // online softmax over the task (position c*32 <= p, so every task has a finite max)
+    float pv[MG];
+#pragma unroll
+    for (int i = 0; i < MG; i++) {
+      pv[i] = 0.f;
+      if (i < G) {
+        const float si = valid ? acc[i] : -INFINITY;
+        const float nm = fmaxf(mrun[i], WarpMax(si));
+        const float sc = mrun[i] == -INFINITY ? 0.f : __expf(mrun[i] - nm);
+        pv[i] = valid ? __expf(si - nm) : 0.f;
+        lrun[i] = lrun[i] * sc + pv[i];
+#pragma unroll
+        for (int j = 0; j < JPL; j++) o[i][j] *= sc;
+        mrun[i] = nm;
+      }
+    }
+    // o += sum_t p_t v_t over the task's positions (rows past p hold zeros)
+#pragma unroll
+    for (int t = 0; t < kAttnTask; t++) {
+      float vf[JPL];
+      VSliceToFloat(vs[t], vf);
+#pragma unroll
+      for (int i = 0; i < MG; i++) {
+        if (i < G) {
+          const float pt = __shfl_sync(0xffffffffu, pv[i], t);
+#pragma unroll
+          for (int j = 0; j < JPL; j++) o[i][j] = fmaf(pt, vf[j], o[i][j]);
+        }
+      }
+    }
+  }
+  // the warps' states, then their merge (weights exp(m_w - M); warps without tasks have m_w = -inf)
+#pragma unroll
+  for (int i = 0; i < MG; i++) {
+    if (i < G) {
+      const float l = WarpSum(lrun[i]);
+      if (lane == 0) {
+        wm[warp * G + i] = mrun[i];
+        wl[warp * G + i] = l;
+      }
+#pragma unroll
+      for (int j = 0; j < JPL; j++) wo[(warp * G + i) * D + lane * JPL + j] = o[i][j];
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x < G) {
+    const int i = threadIdx.x;
+    float M = -INFINITY, L = 0.f;
+    for (int w = 0; w < kAttnRowWarps; w++) M = fmaxf(M, wm[w * G + i]);
+    for (int w = 0; w < kAttnRowWarps; w++)
+      if (wm[w * G + i] != -INFINITY) L += __expf(wm[w * G + i] - M) * wl[w * G + i];
+    mm[i] = M;
+    ml[i] = L;
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < G * D; e += blockDim.x) {
+    const int i = e / D;
+    float acc = 0.f;
+    for (int w = 0; w < kAttnRowWarps; w++)
+      if (wm[w * G + i] != -INFINITY) acc += __expf(wm[w * G + i] - mm[i]) * wo[(w * G + i) * D + e % D];
+    sq[e] = acc;
+  }
+  __syncthreads();
+  AttnFinishSplit(aa, m, g, sq, mm, ml);
+}
+
 // Any even head_dim up to 128 (the reference's small test shapes use d = 4, 8, 16): scalar loops over
 // global memory, one split per (row, kv head), online softmax over the pages.
 constexpr int kMaxHeadDimGeneric = 128;

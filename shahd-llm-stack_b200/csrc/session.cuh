@@ -300,6 +300,22 @@ void Timed(ShahdSession* s, cudaStream_t st, int kind, double bytes, F&& launch,
   else s->prof_recs.push_back({kind, e0, e1, bytes + per_attended * attended, 0.0, chain, 0});
 }
 
+template <int D>
+void LaunchAttnRowsD(int G, dim3 grid, cudaStream_t st, const AttnArgs& aa) {
+  const int sm = AttnRowsSmem(G, D);
+  if (G == 1) LaunchPdl(AttnRowsKernel<D, 1>, grid, dim3(kAttnRowThreads), sm, st, aa);
+  else if (G == 2) LaunchPdl(AttnRowsKernel<D, 2>, grid, dim3(kAttnRowThreads), sm, st, aa);
+  else if (G <= 4) LaunchPdl(AttnRowsKernel<D, 4>, grid, dim3(kAttnRowThreads), sm, st, aa);
+  else LaunchPdl(AttnRowsKernel<D, 8>, grid, dim3(kAttnRowThreads), sm, st, aa);
+}
+
+// Decode-row attention for head_dim d in {32, 64, 128} and G <= kMaxGroup query heads per kv head.
+void LaunchAttnRows(int d, int G, dim3 grid, cudaStream_t st, const AttnArgs& aa) {
+  if (d == 64) LaunchAttnRowsD<64>(G, grid, st, aa);
+  else if (d == 32) LaunchAttnRowsD<32>(G, grid, st, aa);
+  else LaunchAttnRowsD<128>(G, grid, st, aa);
+}
+
 // A prefill-style step whose attention runs as query-block tiles (PrefillAttnKernel) rather than per row.
 bool PrefillTiled(const ShahdSession* s, const StepPlan& p) {
   return p.seq_plan != nullptr && p.plan_n > 0 && s->G <= kPfMaxG && (s->d == 32 || s->d == 64 || s->d == 128);
@@ -531,6 +547,12 @@ int EnqueueStep(ShahdSession* s, const StepPlan& p, cudaStream_t st, int r0 = 0,
     int nsplit = 1;
     if (r0 + M <= s->max_seqs)
       nsplit = std::max(1, std::min(s->max_blocks, CeilDiv(3 * s->num_sms / std::max(1, s->chains_hint), M * s->Hk)));
+    // decode rows (one appended position per row, distinct slots): the read-ahead kernel, split only when
+    // the rows and kv heads alone leave the SMs idle
+    const bool rows_kernel = p.pos_in == nullptr && s->G <= kMaxGroup && (s->d == 32 || s->d == 64 || s->d == 128);
+    int rsplit = 1;
+    if (r0 + M <= s->max_seqs && M * s->Hk < s->num_sms)
+      rsplit = std::max(1, std::min(s->max_blocks, CeilDiv(2 * s->num_sms / std::max(1, s->chains_hint), M * s->Hk)));
     for (int l = 0; l < s->L; l++) {
       const Layer& Ly = s->layers[l];
       // norm1 + QKV + RoPE + KV append (CachedForward.ts:66-73, :78-79)
@@ -546,7 +568,9 @@ int EnqueueStep(ShahdSession* s, const StepPlan& p, cudaStream_t st, int r0 = 0,
                                (float)(1.0 / std::sqrt((double)s->d)), p.seq_plan, s->max_seqs, p.plan_i0};
       const dim3 pg(p.plan_qblocks, s->Hk, p.plan_n);
       Timed(s, st, pk + kProfAttention, attn_fixed, [&] {
-        if (tiled) {
+        if (rows_kernel) {
+          LaunchAttnRows(s->d, s->G, dim3(rsplit, s->Hk, M), st, aa);
+        } else if (tiled) {
           if (s->d == 64) LaunchPdl(PrefillAttnKernel<64>, pg, dim3(kPfThreads), PrefillAttnSmem(64), st, pa);
           else if (s->d == 32) LaunchPdl(PrefillAttnKernel<32>, pg, dim3(kPfThreads), PrefillAttnSmem(32), st, pa);
           else LaunchPdl(PrefillAttnKernel<128>, pg, dim3(kPfThreads), PrefillAttnSmem(128), st, pa);
