@@ -814,10 +814,14 @@ __global__ void __launch_bounds__(kAttnThreads) AttnDecodeKernel(AttnArgs aa) {
 // all of those are read before this kernel's wait, and only q and the K/V row at p (written by the
 // projection) after it. The cached rows then arrive while the projection still runs.
 //
-// One CTA of 8 warps per (split, kv head, row); a warp task is 32 consecutive positions (lane = position
-// for the scores, lane = D/32 dims for P·V): the K row of its position as D/8 16-byte loads, and for the
-// 32 positions the lane's slice of each V row (coalesced 64..256-byte rows). Each warp keeps a running max
-// and sum per head; the warps' states merge in shared memory, the splits through AttnFinishSplit.
+// One CTA of 8 warps per (split, kv head, row); a warp task is 32 consecutive positions. A task's K and V
+// rows are read as coalesced 16-byte chunks: with C = D/8 chunks per row, load i (i < C) gives lane l
+// chunk l % C of row i*(32/C) + l/C, so each load instruction covers 32/C whole rows. Scores: each lane
+// dots its chunks with q, and a reduce-scatter over the C lanes of a row group leaves lane l with the full
+// score of row (l % C)*(32/C) + l/C. P.V: lane l accumulates its chunk's 8 dims over its rows (the
+// probability of row r comes from the lane that scored it); the row groups are summed once at the end.
+// Each warp keeps a running max and sum per head; the warps' states merge in shared memory, the splits
+// through AttnFinishSplit.
 constexpr int kAttnRowWarps = 8;
 constexpr int kAttnRowThreads = kAttnRowWarps * 32;
 constexpr int kAttnTask = 32;  // positions per warp task (a task never straddles a 64-position page)
@@ -827,29 +831,40 @@ __host__ __device__ constexpr int AttnRowsSmem(int G, int D) {
   return (G * D + kAttnRowWarps * G * D + 2 * kAttnRowWarps * G + 2 * G) * 4;
 }
 
-template <int D> struct VSlice;  // the D/32 bf16 dims of one V row that a lane owns
-template <> struct VSlice<32> { using T = unsigned short; };
-template <> struct VSlice<64> { using T = unsigned int; };
-template <> struct VSlice<128> { using T = uint2; };
-
-__device__ __forceinline__ void VSliceToFloat(unsigned short v, float (&f)[1]) { f[0] = __uint_as_float((unsigned)v << 16); }
-__device__ __forceinline__ void VSliceToFloat(unsigned int v, float (&f)[2]) {
-  f[0] = __uint_as_float(v << 16);
-  f[1] = __uint_as_float(v & 0xffff0000u);
-}
-__device__ __forceinline__ void VSliceToFloat(uint2 v, float (&f)[4]) {
-  f[0] = __uint_as_float(v.x << 16);
-  f[1] = __uint_as_float(v.x & 0xffff0000u);
-  f[2] = __uint_as_float(v.y << 16);
-  f[3] = __uint_as_float(v.y & 0xffff0000u);
-}
 __device__ __forceinline__ void PrefetchL2(const void* ptr) { asm volatile("prefetch.global.L2 [%0];" ::"l"(ptr)); }
+
+// Sum over the C lanes of a row group (lanes l ^ k, k < C) of C values per lane, scattered: lane l ends
+// with the total of value index l % C. C is a power of two.
+template <int C>
+__device__ __forceinline__ float ReduceScatter(float (&v)[C], int lane) {
+#pragma unroll
+  for (int o = C / 2; o >= 1; o /= 2) {
+    const bool up = (lane & o) != 0;
+#pragma unroll
+    for (int k = 0; k < o; k++) {
+      const float send = up ? v[k] : v[k + o];
+      const float keep = up ? v[k + o] : v[k];
+      v[k] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+    }
+  }
+  return v[0];
+}
+
+// Eight bf16 (a 16-byte chunk) to fp32 by moving each half into the high bits.
+__device__ __forceinline__ void Bf16ChunkToFloat(const uint4& u, float (&f)[8]) {
+  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+  for (int k = 0; k < 4; k++) {
+    f[2 * k] = __uint_as_float(w[k] << 16);
+    f[2 * k + 1] = __uint_as_float(w[k] & 0xffff0000u);
+  }
+}
 
 // MG: a power of two >= G (per-head state lives in registers sized by it)
 template <int D, int MG>
-__global__ void __launch_bounds__(kAttnRowThreads, D <= 64 ? 2 : 1) AttnRowsKernel(AttnArgs aa) {
-  constexpr int JPL = D / 32;
-  using VT = typename VSlice<D>::T;
+__global__ void __launch_bounds__(kAttnRowThreads, D <= 64 && MG <= 2 ? 2 : 1) AttnRowsKernel(AttnArgs aa) {
+  constexpr int C = D / 8;            // 16-byte chunks per row
+  constexpr int RPI = kAttnTask / C;  // rows per load instruction
   extern __shared__ __align__(16) float ar_smem[];
   const int G = aa.G;
   float* sq = ar_smem;                     // [G][D] q pre-scaled; later the merged output
@@ -860,6 +875,7 @@ __global__ void __launch_bounds__(kAttnRowThreads, D <= 64 ? 2 : 1) AttnRowsKern
   float* ml = mm + G;                      // [G]
   const int g = blockIdx.y, m = blockIdx.z;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int ck = lane % C, rg = lane / C;  // this lane's chunk and row group
 
   // ---- before the wait: launches older than the predecessor only ----
   const int p = __ldcg(aa.pos + m), slot = __ldcg(aa.slot + m);
@@ -867,7 +883,8 @@ __global__ void __launch_bounds__(kAttnRowThreads, D <= 64 ? 2 : 1) AttnRowsKern
   const int per = CeilDiv(ntask, (int)gridDim.x);
   const int c0 = blockIdx.x * per, c1 = min(ntask, c0 + per);
   const size_t head_off = (size_t)((aa.layer * aa.Hk + g) * 2) * kPageTokens * D;
-  // K and V rows of task c (position c*32 + row); nullptr when the page is missing (recorded as an error)
+  // K rows of task c (position c*32 + row; its V rows follow one K page later); nullptr when the page is
+  // missing (recorded as an error)
   auto task_base = [&](int c) -> const bf16* {
     const int page = __ldcg(aa.kv.block_table + (size_t)slot * aa.kv.max_blocks + (c * kAttnTask) / kPageTokens);
     if (page < 0) {
@@ -876,34 +893,33 @@ __global__ void __launch_bounds__(kAttnRowThreads, D <= 64 ? 2 : 1) AttnRowsKern
     }
     return aa.kv.pool + (size_t)page * aa.kv.page_elems + head_off + (size_t)((c * kAttnTask) % kPageTokens) * D;
   };
-  uint4 kr[D / 8];
-  VT vs[kAttnTask];
+  uint4 kr[C], vr[C];  // chunk ck of rows i*RPI + rg
 #pragma unroll
-  for (int i = 0; i < D / 8; i++) kr[i] = make_uint4(0, 0, 0, 0);
-#pragma unroll
-  for (int t = 0; t < kAttnTask; t++) vs[t] = VT{};
+  for (int i = 0; i < C; i++) kr[i] = vr[i] = make_uint4(0, 0, 0, 0);
   // rows of task c at positions [lo, hi)
   auto load_rows = [&](const bf16* kb, int c, int lo, int hi) {
     const int t0 = c * kAttnTask;
-    if (t0 + lane >= lo && t0 + lane < hi) {
-      const uint4* kp = reinterpret_cast<const uint4*>(kb + (size_t)lane * D);
+    const uint4* kp = reinterpret_cast<const uint4*>(kb) + ck;
+    const uint4* vp = reinterpret_cast<const uint4*>(kb + (size_t)kPageTokens * D) + ck;
 #pragma unroll
-      for (int i = 0; i < D / 8; i++) kr[i] = __ldcg(kp + i);
+    for (int i = 0; i < C; i++) {
+      const int r = i * RPI + rg;
+      if (t0 + r >= lo && t0 + r < hi) {
+        kr[i] = __ldcg(kp + (size_t)r * C);
+        vr[i] = __ldcg(vp + (size_t)r * C);
+      }
     }
-    const bf16* vb = kb + (size_t)kPageTokens * D;
-#pragma unroll
-    for (int t = 0; t < kAttnTask; t++)
-      if (t0 + t >= lo && t0 + t < hi) vs[t] = __ldcg(reinterpret_cast<const VT*>(vb + (size_t)t * D) + lane);
   };
   int c = c0 + warp;
   const bf16* kb = c < c1 ? task_base(c) : nullptr;
   if (kb) load_rows(kb, c, 0, p);
   for (int cc = c + kAttnRowWarps; cc < c1; cc += kAttnRowWarps) {  // later tasks of this warp: into L2
     const bf16* b = task_base(cc);
-    if (b && cc * kAttnTask + lane < p) {
-      for (int i = 0; i < D * 2; i += 128) PrefetchL2(reinterpret_cast<const char*>(b + (size_t)lane * D) + i);
-      for (int i = 0; i < D * 2; i += 128)
-        PrefetchL2(reinterpret_cast<const char*>(b + (size_t)(kPageTokens + lane) * D) + i);
+    if (b) {
+      for (int i = lane; i < kAttnTask * D * 2 / 128; i += 32) {  // one 128-byte line per lane and load
+        PrefetchL2(reinterpret_cast<const char*>(b) + (size_t)i * 128);
+        PrefetchL2(reinterpret_cast<const char*>(b + (size_t)kPageTokens * D) + (size_t)i * 128);
+      }
     }
   }
 
@@ -915,96 +931,86 @@ __global__ void __launch_bounds__(kAttnRowThreads, D <= 64 ? 2 : 1) AttnRowsKern
   if (kb) load_rows(kb, c, p, p + 1);
   __syncthreads();
 
-  float o[MG][JPL], mrun[MG], lrun[MG];
+  float o[MG][8], mrun[MG], lrun[MG];
 #pragma unroll
-  for (int i = 0; i < MG; i++) {
-    mrun[i] = -INFINITY;
-    lrun[i] = 0.f;
+  for (int h = 0; h < MG; h++) {
+    mrun[h] = -INFINITY;
+    lrun[h] = 0.f;
 #pragma unroll
-    for (int j = 0; j < JPL; j++) o[i][j] = 0.f;
+    for (int j = 0; j < 8; j++) o[h][j] = 0.f;
   }
-  bool first = true;
-  for (; c < c1; c += kAttnRowWarps) {
+  for (bool first = true; c < c1; c += kAttnRowWarps, first = false) {
+    const int t0 = c * kAttnTask;
     if (!first) {
       kb = task_base(c);
 #pragma unroll
-      for (int t = 0; t < kAttnTask; t++) vs[t] = VT{};
+      for (int i = 0; i < C; i++) kr[i] = vr[i] = make_uint4(0, 0, 0, 0);  // rows past p stay zero
       if (kb) load_rows(kb, c, 0, p + 1);
     }
-    first = false;
     if (kb == nullptr) continue;  // missing page: its positions are left out (the error flag is set)
-    const bool valid = c * kAttnTask + lane <= p;
-    // scores of this lane's position for the G heads
-    float acc[MG];
-#pragma unroll
-    for (int i = 0; i < MG; i++) acc[i] = 0.f;
-#pragma unroll
-    for (int k = 0; k < D / 8; k++) {
-      const uint32_t w[4] = {kr[k].x, kr[k].y, kr[k].z, kr[k].w};
-      float kf[8];
-#pragma unroll
-      for (int u = 0; u < 4; u++) {
-        kf[2 * u] = __uint_as_float(w[u] << 16);
-        kf[2 * u + 1] = __uint_as_float(w[u] & 0xffff0000u);
-      }
-#pragma unroll
-      for (int i = 0; i < MG; i++) {
-        if (i < G) {
-          const float4 q0 = *reinterpret_cast<const float4*>(sq + i * D + 8 * k);
-          const float4 q1 = *reinterpret_cast<const float4*>(sq + i * D + 8 * k + 4);
-          acc[i] = fmaf(q0.x, kf[0], acc[i]);
-          acc[i] = fmaf(q0.y, kf[1], acc[i]);
-          acc[i] = fmaf(q0.z, kf[2], acc[i]);
-          acc[i] = fmaf(q0.w, kf[3], acc[i]);
-          acc[i] = fmaf(q1.x, kf[4], acc[i]);
-          acc[i] = fmaf(q1.y, kf[5], acc[i]);
-          acc[i] = fmaf(q1.z, kf[6], acc[i]);
-          acc[i] = fmaf(q1.w, kf[7], acc[i]);
-        }
-      }
-    }
-    // online softmax over the task (position c*32 <= p, so every task has a finite max)
+    const bool valid = t0 + ck * RPI + rg <= p;  // the row this lane scores
     float pv[MG];
 #pragma unroll
-    for (int i = 0; i < MG; i++) {
-      pv[i] = 0.f;
-      if (i < G) {
-        const float si = valid ? acc[i] : -INFINITY;
-        const float nm = fmaxf(mrun[i], WarpMax(si));
-        const float sc = mrun[i] == -INFINITY ? 0.f : __expf(mrun[i] - nm);
-        pv[i] = valid ? __expf(si - nm) : 0.f;
-        lrun[i] = lrun[i] * sc + pv[i];
+    for (int h = 0; h < MG; h++) {
+      pv[h] = 0.f;
+      if (h < G) {
+        const float4 q0 = *reinterpret_cast<const float4*>(sq + h * D + ck * 8);
+        const float4 q1 = *reinterpret_cast<const float4*>(sq + h * D + ck * 8 + 4);
+        const float qf[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};  // this lane's q chunk
+        float part[C];
 #pragma unroll
-        for (int j = 0; j < JPL; j++) o[i][j] *= sc;
-        mrun[i] = nm;
+        for (int i = 0; i < C; i++) {
+          float kf[8];
+          Bf16ChunkToFloat(kr[i], kf);
+          float a = 0.f;
+#pragma unroll
+          for (int j = 0; j < 8; j++) a = fmaf(qf[j], kf[j], a);
+          part[i] = a;
+        }
+        const float full = ReduceScatter<C>(part, lane);  // every lane takes part in the shuffles
+        const float si = valid ? full : -INFINITY;
+        // online softmax (position c*32 <= p, so every task has a finite max)
+        const float nm = fmaxf(mrun[h], WarpMax(si));
+        const float sc = mrun[h] == -INFINITY ? 0.f : __expf(mrun[h] - nm);
+        pv[h] = valid ? __expf(si - nm) : 0.f;
+        lrun[h] = lrun[h] * sc + pv[h];
+#pragma unroll
+        for (int j = 0; j < 8; j++) o[h][j] *= sc;
+        mrun[h] = nm;
       }
     }
-    // o += sum_t p_t v_t over the task's positions (rows past p hold zeros)
+    // o += p_r v_r over this lane's rows r = i*RPI + rg, scored by lane rg*C + i (rows past p are zero)
 #pragma unroll
-    for (int t = 0; t < kAttnTask; t++) {
-      float vf[JPL];
-      VSliceToFloat(vs[t], vf);
+    for (int i = 0; i < C; i++) {
+      float vf[8];
+      Bf16ChunkToFloat(vr[i], vf);
 #pragma unroll
-      for (int i = 0; i < MG; i++) {
-        if (i < G) {
-          const float pt = __shfl_sync(0xffffffffu, pv[i], t);
+      for (int h = 0; h < MG; h++) {
+        if (h < G) {
+          const float pt = __shfl_sync(0xffffffffu, pv[h], rg * C + i);
 #pragma unroll
-          for (int j = 0; j < JPL; j++) o[i][j] = fmaf(pt, vf[j], o[i][j]);
+          for (int j = 0; j < 8; j++) o[h][j] = fmaf(pt, vf[j], o[h][j]);
         }
       }
     }
   }
-  // the warps' states, then their merge (weights exp(m_w - M); warps without tasks have m_w = -inf)
+  // the warps' states (row groups summed), then their merge (weights exp(m_w - M); idle warps: m_w = -inf)
 #pragma unroll
-  for (int i = 0; i < MG; i++) {
-    if (i < G) {
-      const float l = WarpSum(lrun[i]);
+  for (int h = 0; h < MG; h++) {
+    if (h < G) {
+#pragma unroll
+      for (int j = 0; j < 8; j++)
+#pragma unroll
+        for (int off = C; off < 32; off *= 2) o[h][j] += __shfl_xor_sync(0xffffffffu, o[h][j], off);
+      const float l = WarpSum(lrun[h]);
       if (lane == 0) {
-        wm[warp * G + i] = mrun[i];
-        wl[warp * G + i] = l;
+        wm[warp * G + h] = mrun[h];
+        wl[warp * G + h] = l;
       }
+      if (rg == 0) {
 #pragma unroll
-      for (int j = 0; j < JPL; j++) wo[(warp * G + i) * D + lane * JPL + j] = o[i][j];
+        for (int j = 0; j < 8; j++) wo[(warp * G + h) * D + ck * 8 + j] = o[h][j];
+      }
     }
   }
   __syncthreads();
