@@ -48,6 +48,27 @@ inline void LaunchPdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem
   cudaLaunchKernelEx(&cfg, kern, args...);
 }
 
+// LaunchPdl with the CTAs grouped into thread-block clusters of `cluster` (grid divisible by it).
+template <typename... KArgs, typename... Args>
+inline void LaunchPdlCluster(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, dim3 cluster, cudaStream_t st,
+                             Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = cluster.x;
+  attr[0].val.clusterDim.y = cluster.y;
+  attr[0].val.clusterDim.z = cluster.z;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = g_use_pdl ? 2 : 1;
+  cudaLaunchKernelEx(&cfg, kern, args...);
+}
+
 __host__ __device__ inline int CeilDiv(int a, int b) { return (a + b - 1) / b; }
 __host__ __device__ inline int RoundUp(int a, int b) { return CeilDiv(a, b) * b; }
 
@@ -100,6 +121,24 @@ __device__ __forceinline__ void GridDepLaunch() { asm volatile("griddepcontrol.l
 // Orders this thread's later async-proxy reads (TMA, bulk copies) after generic-proxy writes it may now
 // observe, such as a predecessor grid's stores seen through GridDepWait.
 __device__ __forceinline__ void FenceProxyAsyncGlobal() { asm volatile("fence.proxy.async.global;" ::: "memory"); }
+
+// Thread-block clusters: a barrier over every thread of the cluster (release/acquire: shared-memory
+// writes before it are visible to all CTAs of the cluster after it), and a 16-byte load from the shared
+// memory of CTA `rank` at the address of `p` in this CTA's window.
+__device__ __forceinline__ void ClusterSync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ float4 LoadPeerF32x4(const float* p, uint32_t rank) {
+  const uint32_t a = (uint32_t)__cvta_generic_to_shared(p);
+  uint32_t ra;
+  float4 v;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(ra) : "r"(a), "r"(rank));
+  asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(ra)
+               : "memory");
+  return v;
+}
 
 // ---- shared-memory address, mbarrier, TMA, tcgen05 (inline PTX, sm_100a) -------------------------
 

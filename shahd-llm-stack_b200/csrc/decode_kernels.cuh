@@ -366,6 +366,7 @@ struct LinearArgs {
   int* am_idx;
   float* ws;        // split-K partial tiles (tensor-core path, no norm), or nullptr: no split
   int* ws_cnt;      // [N tiles] arrival counters, zero between launches
+  int kcluster;     // the split-K CTAs of a tile form a cluster and sum their partials in shared memory
 };
 
 // ---- SIMT linear (GEMV regime, few rows): out[m, n] = sum_k xhat[m, k] * W'[n, k] -------------------

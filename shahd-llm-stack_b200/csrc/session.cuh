@@ -356,7 +356,7 @@ double LinearBytes(int M, int K, int Kp, int N) { return 2.0 * N * Kp + 2.0 * M 
 
 LinearArgs Lin(const float* a, int lda, const bf16* ab, int ldab, int rows_cap, int M, int K, int Kp, const bf16* w,
                int N, float eps, const float* c1, const float* c2, float* amv = nullptr, int* ami = nullptr) {
-  LinearArgs la;
+  LinearArgs la{};
   la.a = a; la.lda = lda; la.ab = ab; la.ldab = ldab; la.a_rows = rows_cap; la.M = M; la.K = K; la.Kp = Kp;
   la.w = w; la.N = N; la.eps = eps; la.c1 = c1; la.c2 = c2; la.am_val = amv; la.am_idx = ami;
   la.ws = nullptr; la.ws_cnt = nullptr;

@@ -553,7 +553,7 @@ __device__ __forceinline__ void StepAttnItem(const StepDesc& s, int layer, int m
 enum StepProj { kProjQkv = 0, kProjO = 1, kProjUp = 2, kProjDown = 3, kProjHead = 4 };
 
 struct StepProjInfo {
-  LinearArgs la;
+  LinearArgs la{};
   const CUtensorMap* wmap;
   const CUtensorMap* amap;
   int bn, ks, tiles;

@@ -291,7 +291,29 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
   __syncthreads();
   TcgenFenceAfter();
   const uint32_t trow = tmem + ((uint32_t)(warp * 32) << 16);  // this warp's 32 TMEM lanes
-  if (!*s_abort && ks > 1) {
+  // split-K within a cluster: each CTA leaves its partial tile in its own (now idle) stage memory; CTA
+  // kz then sums rows [kz*128/ks, (kz+1)*128/ks) over the cluster in split order and runs their epilogue
+  const bool kc = ks > 1 && la.kcluster != 0;
+  float* spart = reinterpret_cast<float*>(smem);  // [kUmmaBM][BN]
+  const bool own = !kc || r * ks / kUmmaBM == kz;
+  if (kc) {
+    if (!*s_abort) {
+#pragma unroll
+      for (int g = 0; g < kChunks; g += kGroup) {
+        uint32_t u[kGroup][16];
+#pragma unroll
+        for (int q = 0; q < kGroup; q++) TmemLoad16(trow + (uint32_t)(16 * (g + q)), u[q]);
+        TmemWaitLd();
+#pragma unroll
+        for (int q = 0; q < kGroup; q++)
+#pragma unroll
+          for (int i = 0; i < 4; i++)
+            *reinterpret_cast<uint4*>(spart + (size_t)r * BN + 16 * (g + q) + 4 * i) =
+                make_uint4(u[q][4 * i], u[q][4 * i + 1], u[q][4 * i + 2], u[q][4 * i + 3]);
+      }
+    }
+    ClusterSync();  // every CTA of the cluster reaches both barriers, aborted or not
+  } else if (!*s_abort && ks > 1) {
     // split-K: every CTA parks its partial tile in the workspace; the last CTA of the tile sums the
     // partials in split order (the result does not depend on which CTA finishes last) and runs the epilogue
     float* part = la.ws + ((size_t)(blockIdx.x * ks + kz) * kUmmaBM + r) * BN;
@@ -320,7 +342,25 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
 #pragma unroll
     for (int g = 0; g < kChunks; g += kGroup) {
       float vg[kGroup][16];
-      if (ks > 1) {
+      if (kc) {
+        if (row_ok && own) {
+#pragma unroll
+          for (int q = 0; q < kGroup; q++) {
+#pragma unroll
+            for (int j = 0; j < 16; j++) vg[q][j] = 0.f;
+            for (int z = 0; z < ks; z++) {
+#pragma unroll
+              for (int i = 0; i < 4; i++) {
+                const float4 t = LoadPeerF32x4(spart + (size_t)r * BN + 16 * (g + q) + 4 * i, (uint32_t)z);
+                vg[q][4 * i] += t.x;
+                vg[q][4 * i + 1] += t.y;
+                vg[q][4 * i + 2] += t.z;
+                vg[q][4 * i + 3] += t.w;
+              }
+            }
+          }
+        }
+      } else if (ks > 1) {
         if (row_ok) {
 #pragma unroll
           for (int q = 0; q < kGroup; q++) {
@@ -350,7 +390,7 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
 #pragma unroll
           for (int j = 0; j < 16; j++) vg[q][j] = __uint_as_float(u[q][j]);
       }
-      if (!row_ok) continue;
+      if (!row_ok || !own) continue;
 #pragma unroll
       for (int q = 0; q < kGroup; q++) {
         const int ch = g + q;
@@ -405,8 +445,9 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
         la.am_idx[(size_t)(m0 + r) * gridDim.x + blockIdx.x] = bi;
       }
     }
-    if (ks > 1 && threadIdx.x == 0) la.ws_cnt[blockIdx.x] = 0;  // ready for the next launch
+    if (ks > 1 && !kc && threadIdx.x == 0) la.ws_cnt[blockIdx.x] = 0;  // ready for the next launch
   }
+  if (kc) ClusterSync();  // the peers are done reading this CTA's partial tile
   TcgenFenceBefore();
   __syncthreads();
   __syncwarp();
@@ -427,8 +468,16 @@ void LaunchUmmaLinearBN(const LinearArgs& la, const Epi& epi, cudaStream_t st) {
   }
   const int ks = (NORM == kNormNone && la.ws != nullptr) ? UmmaKSplit(la.M, la.N, la.Kp) : 1;
   dim3 grid(CeilDiv(la.N, BN), CeilDiv(la.M, kUmmaBM), ks);
-  LaunchPdl(LinearUmmaKernel<NORM, Epi, BN>, grid, dim3(kUmmaThreads), UmmaSmem<BN>::kBytes, st, la, epi, ta, tw,
-            box);
+  static_assert(UmmaSmem<BN>::kStages * UmmaSmem<BN>::kStage >= kUmmaBM * BN * 4, "partial tile fits the stages");
+  if (ks > 1) {  // the split CTAs of a tile reduce through distributed shared memory
+    LinearArgs lc = la;
+    lc.kcluster = 1;
+    LaunchPdlCluster(LinearUmmaKernel<NORM, Epi, BN>, grid, dim3(kUmmaThreads), UmmaSmem<BN>::kBytes, dim3(1, 1, ks), st,
+                     lc, epi, ta, tw, box);
+  } else {
+    LaunchPdl(LinearUmmaKernel<NORM, Epi, BN>, grid, dim3(kUmmaThreads), UmmaSmem<BN>::kBytes, st, la, epi, ta, tw,
+              box);
+  }
 }
 
 template <int NORM, class Epi>
