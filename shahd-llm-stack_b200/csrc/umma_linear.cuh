@@ -46,7 +46,8 @@ __host__ inline int UmmaBN(int M, int N) {
 }
 
 // K splits of a decode-sized projection without a norm (the norm needs whole rows): about four k-blocks
-// of 64 per CTA, at most 8 splits and two waves of CTAs. Partial tiles meet in a workspace.
+// of 64 per CTA, at most 8 splits (one cluster) and two waves of CTAs. Partial tiles meet in the
+// cluster's shared memory; the workspace pointer only marks a projection as splittable.
 __host__ inline int UmmaKSplit(int M, int N, int Kp) {
   if (M > kUmmaBM) return 1;
   const int nk = CeilDiv(Kp, kUmmaBK), tiles = CeilDiv(N, UmmaBN(M, N));
