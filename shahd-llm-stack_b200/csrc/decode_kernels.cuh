@@ -228,7 +228,7 @@ struct EpiResid {
 // Gated MLP hidden: act[j] = Act(x·W1[:,j]) * (x·W3[:,j]) with W1/W3 interleaved per column pair
 // (MlpRow, CachedRowMath.ts:107-112; SiluValue Silu.ts:8-10; GeluValue Gelu.ts:7-14).
 struct EpiGated {
-  float* act;  // [M, F]
+  float* act;  // [M, F], or nullptr when only the bf16 copy is read (tensor-core down projection)
   bf16* actb;  // [M, ldb]
   int F, ldb;
   int gelu;
@@ -241,7 +241,7 @@ struct EpiGated {
       a = g * (1.0f / (1.0f + __expf(-g)));
     }
     const float h = a * u;
-    act[(size_t)m * F + (n >> 1)] = h;
+    if (act) act[(size_t)m * F + (n >> 1)] = h;
     actb[(size_t)m * ldb + (n >> 1)] = __float2bfloat16_rn(h);
   }
   struct Pre {};
@@ -261,7 +261,7 @@ struct EpiGated {
       }
       h[i] = a * u;
     }
-    StoreNf<8>(act + (size_t)m * F + (n >> 1), h);
+    if (act) StoreNf<8>(act + (size_t)m * F + (n >> 1), h);
     StoreNbf<8>(actb + (size_t)m * ldb + (n >> 1), h);
   }
 };
@@ -569,7 +569,7 @@ constexpr int kMaxGroup = 8;
 constexpr int kAttnRing = 3;  // page buffers in flight per CTA
 
 __device__ __forceinline__ void StoreCtx(const AttnArgs& aa, int m, int col, float v) {
-  aa.ctx[(size_t)m * aa.H * aa.d + col] = v;
+  if (aa.ctx) aa.ctx[(size_t)m * aa.H * aa.d + col] = v;
   aa.ctxb[(size_t)m * aa.ldcb + col] = __float2bfloat16_rn(v);
 }
 

@@ -21,7 +21,7 @@ constexpr int kPfMaxG = 4;    // query heads per kv head handled by this kernel
 
 struct PrefillAttnArgs {
   const float* q;      // [rows, H*d] post-RoPE
-  float* ctx;          // [rows, H*d]
+  float* ctx;          // [rows, H*d], or nullptr when only the bf16 copy is read
   bf16* ctxb;          // [rows, ldcb]
   int ldcb;
   KvView kv;
@@ -188,7 +188,7 @@ __global__ void __launch_bounds__(kPfThreads) PrefillAttnKernel(PrefillAttnArgs 
       for (int j = 0; j < DPT; j++) {
         const int col = (g * G + h) * D + tx * DPT + j;
         const float v = o[h][i][j] * inv;
-        a.ctx[row * hd + col] = v;
+        if (a.ctx) a.ctx[row * hd + col] = v;
         a.ctxb[row * a.ldcb + col] = __float2bfloat16_rn(v);
       }
     }

@@ -541,8 +541,13 @@ int EnqueueStep(ShahdSession* s, const StepPlan& p, cudaStream_t st, int r0 = 0,
       });
     }
     KvView kv{s->kv_pool, s->d_block_table, s->max_blocks, s->Hk, s->d, s->page_elems};
-    // K and V rows read (bf16) + q read and ctx written (fp32 + bf16)
-    const double attn_fixed = 10.0 * M * hd, attn_per_pos = 4.0 * s->Hk * s->d;
+    // the fp32 context and MLP activation rows feed only the CUDA-core projections (few rows); the
+    // tensor-core projections read the bf16 copies, so the fp32 rows are not written for them
+    const bool tc_rows = M >= kUmmaMinRows;
+    float* ctx_f32 = tc_rows ? nullptr : ctx;
+    float* act_f32 = tc_rows ? nullptr : act;
+    // K and V rows read (bf16) + q read and ctx written (bf16, and fp32 for the CUDA-core projection)
+    const double attn_fixed = (tc_rows ? 6.0 : 10.0) * M * hd, attn_per_pos = 4.0 * s->Hk * s->d;
     // splits per (row, kv head): enough CTAs to fill the GPU; one split (no partials) beyond max_seqs rows
     int nsplit = 1;
     if (r0 + M <= s->max_seqs)
@@ -560,11 +565,11 @@ int EnqueueStep(ShahdSession* s, const StepPlan& p, cudaStream_t st, int r0 = 0,
       const EpiQKV eq{q, kv, l, pos, p.slot, s->rope_cos, s->rope_sin, s->H, s->Hk, s->d};
       Timed(s, st, pk + kProfLinear, LinearBytes(M, s->E, s->Ep, s->Nqkv), [&] { LaunchLinear(norm, la, eq, st); });
       // attention over the cache (CachedForward.ts:76-80)
-      AttnArgs aa{q, ctx, ctxb, s->HDp, kv, l, pos, p.slot, s->H, s->Hk, s->G, s->d,
+      AttnArgs aa{q, ctx_f32, ctxb, s->HDp, kv, l, pos, p.slot, s->H, s->Hk, s->G, s->d,
                   (float)(1.0 / std::sqrt((double)s->d)), s->max_blocks, part_o, part_m, part_l, counter};
       dim3 ag(nsplit, s->Hk, M);
       const bool tiled = PrefillTiled(s, p);
-      const PrefillAttnArgs pa{q, ctx, ctxb, s->HDp, kv, l, s->H, s->Hk, s->G,
+      const PrefillAttnArgs pa{q, ctx_f32, ctxb, s->HDp, kv, l, s->H, s->Hk, s->G,
                                (float)(1.0 / std::sqrt((double)s->d)), p.seq_plan, s->max_seqs, p.plan_i0};
       const dim3 pg(p.plan_qblocks, s->Hk, p.plan_n);
       Timed(s, st, pk + kProfAttention, attn_fixed, [&] {
@@ -589,7 +594,7 @@ int EnqueueStep(ShahdSession* s, const StepPlan& p, cudaStream_t st, int r0 = 0,
       const LinearArgs lu = Lin(x, s->E, xb, s->Ep, R, M, s->E, s->Ep, Ly.w_up, s->Nup, eps, Ly.up_c1, Ly.up_c2);
       Timed(s, st, pk + kProfLinear, LinearBytes(M, s->E, s->Ep, s->Nup), [&] {
         if (s->cfg.mlp_kind == 0) LaunchLinear(norm, lu, EpiReluFc{act, actb, s->F, s->Fp, Ly.b_fc}, st);
-        else LaunchLinear(norm, lu, EpiGated{act, actb, s->F, s->Fp, s->cfg.mlp_kind == 2}, st);
+        else LaunchLinear(norm, lu, EpiGated{act_f32, actb, s->F, s->Fp, s->cfg.mlp_kind == 2}, st);
       });
       LinearArgs ld = Lin(act, s->F, actb, s->Fp, R, M, s->F, s->Fp, Ly.w_down, s->E, eps, nullptr, nullptr);
       ld.ws = split_ws;
