@@ -65,7 +65,10 @@ __host__ inline int UmmaGridN(int N) { return CeilDiv(N, 16); }  // upper bound 
 inline bool UmmaLinearSupported(const LinearArgs& la) { return la.Kp % 8 == 0 && la.N >= 1 && la.ab != nullptr; }
 
 // Pipeline depth by tile width: narrow tiles keep a whole decode-sized K in flight.
-__host__ __device__ constexpr int UmmaStages(int BN) { return BN <= 32 ? 8 : (BN <= 64 ? 6 : 4); }
+// Stage ring depth. BN = 128 tiles (batched prefill rows, a few k-blocks each) keep two stages, so three
+// CTAs share an SM and one CTA's epilogue overlaps the others' main loops (4096-sequence prefill-heavy
+// job 149 -> 134 ms against four stages).
+__host__ __device__ constexpr int UmmaStages(int BN) { return BN <= 32 ? 8 : (BN <= 64 ? 6 : 2); }
 
 // Rows of the activation tile fetched per stage: the 8-row multiple covering M (at most 128). The MMA
 // always reads 128 rows; the rows past the box hold stale shared memory and only feed accumulator rows
