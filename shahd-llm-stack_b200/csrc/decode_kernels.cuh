@@ -823,8 +823,7 @@ __global__ void __launch_bounds__(kAttnThreads) AttnDecodeKernel(AttnArgs aa) {
 // probability of row r comes from the lane that scored it); the row groups are summed once at the end.
 // Each warp keeps a running max and sum per head; the warps' states merge in shared memory, the splits
 // through AttnFinishSplit.
-constexpr int kAttnRowWarps = 8;
-constexpr int kAttnRowThreads = kAttnRowWarps * 32;
+constexpr int kAttnRowWarps = 8;  // the most warps a CTA has (shared memory is sized for them)
 constexpr int kAttnTask = 32;  // positions per warp task (a task never straddles a 64-position page)
 
 __host__ __device__ constexpr int AttnRowsSmem(int G, int D) {
@@ -861,18 +860,19 @@ __device__ __forceinline__ void Bf16ChunkToFloat(const uint4& u, float (&f)[8]) 
   }
 }
 
-// MG: a power of two >= G (per-head state lives in registers sized by it)
-template <int D, int MG>
-__global__ void __launch_bounds__(kAttnRowThreads, D <= 64 && MG <= 2 ? 2 : 1) AttnRowsKernel(AttnArgs aa) {
+// MG: a power of two >= G (per-head state lives in registers sized by it); NW warps per CTA: 8 while
+// the grid fits two CTAs per SM, 4 for many rows, so that more rows are resident at once.
+template <int D, int MG, int NW>
+__global__ void __launch_bounds__(NW * 32, (D <= 64 && MG <= 2 ? 2 : 1) * (8 / NW)) AttnRowsKernel(AttnArgs aa) {
   constexpr int C = D / 8;            // 16-byte chunks per row
   constexpr int RPI = kAttnTask / C;  // rows per load instruction
   extern __shared__ __align__(16) float ar_smem[];
   const int G = aa.G;
   float* sq = ar_smem;                     // [G][D] q pre-scaled; later the merged output
   float* wo = sq + G * D;                  // [warps][G][D]
-  float* wm = wo + kAttnRowWarps * G * D;  // [warps][G]
-  float* wl = wm + kAttnRowWarps * G;      // [warps][G]
-  float* mm = wl + kAttnRowWarps * G;      // [G]
+  float* wm = wo + NW * G * D;  // [warps][G]
+  float* wl = wm + NW * G;      // [warps][G]
+  float* mm = wl + NW * G;      // [G]
   float* ml = mm + G;                      // [G]
   const int g = blockIdx.y, m = blockIdx.z;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -914,7 +914,7 @@ __global__ void __launch_bounds__(kAttnRowThreads, D <= 64 && MG <= 2 ? 2 : 1) A
   int c = c0 + warp;
   const bf16* kb = c < c1 ? task_base(c) : nullptr;
   if (kb) load_rows(kb, c, 0, p);
-  for (int cc = c + kAttnRowWarps; cc < c1; cc += kAttnRowWarps) {  // later tasks of this warp: into L2
+  for (int cc = c + NW; cc < c1; cc += NW) {  // later tasks of this warp: into L2
     const bf16* b = task_base(cc);
     if (b) {
       for (int i = lane; i < kAttnTask * D * 2 / 128; i += 32) {  // one 128-byte line per lane and load
@@ -940,7 +940,7 @@ __global__ void __launch_bounds__(kAttnRowThreads, D <= 64 && MG <= 2 ? 2 : 1) A
 #pragma unroll
     for (int j = 0; j < 8; j++) o[h][j] = 0.f;
   }
-  for (bool first = true; c < c1; c += kAttnRowWarps, first = false) {
+  for (bool first = true; c < c1; c += NW, first = false) {
     const int t0 = c * kAttnTask;
     if (!first) {
       kb = task_base(c);
@@ -1018,8 +1018,8 @@ __global__ void __launch_bounds__(kAttnRowThreads, D <= 64 && MG <= 2 ? 2 : 1) A
   if (threadIdx.x < G) {
     const int i = threadIdx.x;
     float M = -INFINITY, L = 0.f;
-    for (int w = 0; w < kAttnRowWarps; w++) M = fmaxf(M, wm[w * G + i]);
-    for (int w = 0; w < kAttnRowWarps; w++)
+    for (int w = 0; w < NW; w++) M = fmaxf(M, wm[w * G + i]);
+    for (int w = 0; w < NW; w++)
       if (wm[w * G + i] != -INFINITY) L += __expf(wm[w * G + i] - M) * wl[w * G + i];
     mm[i] = M;
     ml[i] = L;
@@ -1028,7 +1028,7 @@ __global__ void __launch_bounds__(kAttnRowThreads, D <= 64 && MG <= 2 ? 2 : 1) A
   for (int e = threadIdx.x; e < G * D; e += blockDim.x) {
     const int i = e / D;
     float acc = 0.f;
-    for (int w = 0; w < kAttnRowWarps; w++)
+    for (int w = 0; w < NW; w++)
       if (wm[w * G + i] != -INFINITY) acc += __expf(wm[w * G + i] - mm[i]) * wo[(w * G + i) * D + e % D];
     sq[e] = acc;
   }

@@ -300,20 +300,22 @@ void Timed(ShahdSession* s, cudaStream_t st, int kind, double bytes, F&& launch,
   else s->prof_recs.push_back({kind, e0, e1, bytes + per_attended * attended, 0.0, chain, 0});
 }
 
-template <int D>
-void LaunchAttnRowsD(int G, dim3 grid, cudaStream_t st, const AttnArgs& aa) {
+template <int D, int NW>
+void LaunchAttnRowsDW(int G, dim3 grid, cudaStream_t st, const AttnArgs& aa) {
   const int sm = AttnRowsSmem(G, D);
-  if (G == 1) LaunchPdl(AttnRowsKernel<D, 1>, grid, dim3(kAttnRowThreads), sm, st, aa);
-  else if (G == 2) LaunchPdl(AttnRowsKernel<D, 2>, grid, dim3(kAttnRowThreads), sm, st, aa);
-  else if (G <= 4) LaunchPdl(AttnRowsKernel<D, 4>, grid, dim3(kAttnRowThreads), sm, st, aa);
-  else LaunchPdl(AttnRowsKernel<D, 8>, grid, dim3(kAttnRowThreads), sm, st, aa);
+  if (G == 1) LaunchPdl(AttnRowsKernel<D, 1, NW>, grid, dim3(NW * 32), sm, st, aa);
+  else if (G == 2) LaunchPdl(AttnRowsKernel<D, 2, NW>, grid, dim3(NW * 32), sm, st, aa);
+  else if (G <= 4) LaunchPdl(AttnRowsKernel<D, 4, NW>, grid, dim3(NW * 32), sm, st, aa);
+  else LaunchPdl(AttnRowsKernel<D, 8, NW>, grid, dim3(NW * 32), sm, st, aa);
 }
 
-// Decode-row attention for head_dim d in {32, 64, 128} and G <= kMaxGroup query heads per kv head.
-void LaunchAttnRows(int d, int G, dim3 grid, cudaStream_t st, const AttnArgs& aa) {
-  if (d == 64) LaunchAttnRowsD<64>(G, grid, st, aa);
-  else if (d == 32) LaunchAttnRowsD<32>(G, grid, st, aa);
-  else LaunchAttnRowsD<128>(G, grid, st, aa);
+// Decode-row attention for head_dim d in {32, 64, 128} and G <= kMaxGroup query heads per kv head:
+// 8-warp CTAs while the grid fits two per SM, 4-warp CTAs beyond.
+void LaunchAttnRows(int d, int G, dim3 grid, int num_sms, cudaStream_t st, const AttnArgs& aa) {
+  const bool wide = (long long)grid.x * grid.y * grid.z <= 2LL * num_sms;
+  if (d == 64) (wide ? LaunchAttnRowsDW<64, 8> : LaunchAttnRowsDW<64, 4>)(G, grid, st, aa);
+  else if (d == 32) (wide ? LaunchAttnRowsDW<32, 8> : LaunchAttnRowsDW<32, 4>)(G, grid, st, aa);
+  else (wide ? LaunchAttnRowsDW<128, 8> : LaunchAttnRowsDW<128, 4>)(G, grid, st, aa);
 }
 
 // A prefill-style step whose attention runs as query-block tiles (PrefillAttnKernel) rather than per row.
@@ -574,7 +576,7 @@ int EnqueueStep(ShahdSession* s, const StepPlan& p, cudaStream_t st, int r0 = 0,
       const dim3 pg(p.plan_qblocks, s->Hk, p.plan_n);
       Timed(s, st, pk + kProfAttention, attn_fixed, [&] {
         if (rows_kernel) {
-          LaunchAttnRows(s->d, s->G, dim3(rsplit, s->Hk, M), st, aa);
+          LaunchAttnRows(s->d, s->G, dim3(rsplit, s->Hk, M), s->num_sms, st, aa);
         } else if (tiled) {
           if (s->d == 64) LaunchPdl(PrefillAttnKernel<64>, pg, dim3(kPfThreads), PrefillAttnSmem(64), st, pa);
           else if (s->d == 32) LaunchPdl(PrefillAttnKernel<32>, pg, dim3(kPfThreads), PrefillAttnSmem(32), st, pa);
