@@ -1,12 +1,14 @@
 // Tensor-core (tcgen05 / TMEM / TMA) kernels for sm_100a.
 //
 // LinearUmmaKernel: the batched-rows regime of every decode/prefill projection. 128-row x BN-column
-// output tile per CTA; the weight tile [BN x 64] arrives by TMA (128-byte swizzle); the activation
-// tile [128 x 64] is produced by the CTA's own threads from fp32 rows with the layer norm applied
-// (NormRow, CachedRowMath.ts:25-56) and converted to bf16 into the same swizzled K-major layout; one
-// thread issues tcgen05.mma (M=128, N=BN, K=16) into a TMEM accumulator; the four warps read their
-// 32-lane quadrant back with tcgen05.ld and run the fused epilogue (RoPE + KV append, residual add,
-// SwiGLU/GeGLU, LM head + argmax).
+// output tile per CTA; the weight tile [BN x 64] (issued before the grid-dependency wait) and the bf16
+// activation rows [up to 128 x 64] arrive by TMA (128-byte swizzle, K-major); the layer norm
+// (NormRow, CachedRowMath.ts:25-56) is folded into the weights, its per-row statistics are taken from
+// the staged activation tiles and applied in the epilogue; one thread issues tcgen05.mma (M=128, N=BN,
+// K=16) into a TMEM accumulator; the four warps read their 32-lane quadrant back with tcgen05.ld and
+// run the fused epilogue (RoPE + KV append, residual add, SwiGLU/GeGLU, LM head + argmax). A long
+// decode reduction is split over a cluster of CTAs that sum their partial tiles through distributed
+// shared memory.
 //
 // GemmNtBf16Kernel: out[M,N] (+)= A[M,K] · B[N,K]ᵀ with both operands bf16 in global memory, both
 // fed by TMA, warp-specialized (producer warp, MMA warp, 4 epilogue warps) — the MatMulNT operator.
