@@ -1015,6 +1015,19 @@ __global__ void __launch_bounds__(NW * 32, (D <= 64 && MG <= 2 ? 2 : 1) * (8 / N
     }
   }
   __syncthreads();
+  if (gridDim.x == 1) {  // one split: every thread merges the warps for its outputs and stores them
+    for (int e = threadIdx.x; e < G * D; e += blockDim.x) {
+      const int i = e / D;
+      float M = -INFINITY, L = 0.f, acc = 0.f;
+      for (int w = 0; w < NW; w++) M = fmaxf(M, wm[w * G + i]);
+      for (int w = 0; w < NW; w++)
+        if (wm[w * G + i] != -INFINITY) L += __expf(wm[w * G + i] - M) * wl[w * G + i];
+      for (int w = 0; w < NW; w++)
+        if (wm[w * G + i] != -INFINITY) acc += __expf(wm[w * G + i] - M) * wo[(w * G + i) * D + e % D];
+      StoreCtx(aa, m, (g * G + i) * D + e % D, acc / L);
+    }
+    return;
+  }
   if (threadIdx.x < G) {
     const int i = threadIdx.x;
     float M = -INFINITY, L = 0.f;
