@@ -6,13 +6,13 @@ greedy decode of 384 new ids each (prefill of the 127-id context included). Sequ
 GPU (each rank runs its own 64, seeded by global sequence index: weak scaling); nothing crosses
 NVLink on the hot path — NCCL only takes the max of the timings and gathers per-rank output checksums.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload NAME]
 
 `value` is generated tokens/s of the whole job with prompts already resident in HBM, timed with CUDA
 events on the launching stream (max over ranks); `e2e` is the same metric through the host-buffer C ABI
 (shahd_generate: prompts copied in, ids copied out, inside the timed region). `--impl reference` times
-the reference's own CPU algorithm (the oracle restatement of its TS decode, all host threads) on a
-bounded sample of the same workload.
+the reference's own CPU algorithm (the oracle restatement of its TS decode, all host threads) on the same
+sequences; that arm imports nothing of the GPU package.
 """
 from __future__ import annotations
 
@@ -30,14 +30,65 @@ import numpy as np
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
-pkg = importlib.import_module("shahd-llm-stack_b200")
 
 METRIC = "KV-cached decode tokens/s at MicroChat shape, 1-8 B200; % of HBM roofline"
 L2_FLUSH_BYTES = 512 << 20  # > 126 MB L2
+PROMPT_SEED_BASE = 1000  # sequence g's prompt: floor(NextFloat() * vocab) from SeededRng(1000 + g)
+
+# The decode workloads as plain data, so the reference arm runs without the GPU package. They equal
+# shahd-llm-stack_b200/configs.py (tests/test_bench_contract.py checks it). `ref_sample`: sequences and
+# new tokens of one reference-arm step (None: the whole job).
+WORKLOADS = {
+    "foundry": dict(name="foundry-shape E128 L4 H4 GeGlu F512 ctx256 V4096", embed_dim=128, num_layers=4, num_heads=4,
+                    kv_heads=4, block_size=256, vocab_size=4096, mlp_hidden=512, position_scheme="Learned",
+                    norm_kind="LayerNorm", mlp_kind="GeGlu", weight_seed=0, seqs=1, prompt_len=64, new_tokens=192,
+                    ref_sample=None),
+    "microchat": dict(name="MicroChat-shape E256 L6 H4 SwiGlu F1024 ctx512 V4096", embed_dim=256, num_layers=6,
+                      num_heads=4, kv_heads=4, block_size=512, vocab_size=4096, mlp_hidden=1024, position_scheme="Rope",
+                      norm_kind="RmsNorm", mlp_kind="SwiGlu", weight_seed=1, seqs=64, prompt_len=128, new_tokens=384,
+                      ref_sample=None),
+    "phase2": dict(name="Phase2Modern-style E1024 L16 H16/4 SwiGlu F2816 ctx2048 V32768", embed_dim=1024,
+                   num_layers=16, num_heads=16, kv_heads=4, block_size=2048, vocab_size=32768, mlp_hidden=2816,
+                   position_scheme="Rope", norm_kind="RmsNorm", mlp_kind="SwiGlu", weight_seed=4, seqs=4096,
+                   prompt_len=512, new_tokens=512, ref_sample=(1, 8)),
+}
+_SHAPE_KEYS = ("embed_dim", "num_layers", "num_heads", "kv_heads", "block_size", "vocab_size", "mlp_hidden",
+               "position_scheme", "norm_kind", "mlp_kind")
+
+
+def cpu_model() -> str:
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+def ref_prompts(wd: dict, rank: int, n: int) -> np.ndarray:
+    """The prompts of sequences rank*seqs .. rank*seqs+n-1, drawn with the oracle's SeededRng."""
+    from oracle import oracle as O
+
+    g0 = rank * wd["seqs"]
+    return np.stack([O.uniform_ids(wd["prompt_len"], wd["vocab_size"], PROMPT_SEED_BASE + g0 + i) for i in range(n)])
+
+
+def ref_model(wd: dict):
+    """The oracle model on the reference's seeded init (bit-exact with the product's f32 master weights)."""
+    from oracle import oracle as O
+
+    shape = O.Shape(**{k: wd[k] for k in _SHAPE_KEYS}, precision="F32")
+    return O.Model(shape, O.init_params(shape, wd["weight_seed"]))
+
+
+def package():
+    return importlib.import_module("shahd-llm-stack_b200")
 
 
 def prompts_for(w, rank: int) -> np.ndarray:
-    return pkg.sharding.shard_prompts(w, rank)
+    return package().sharding.shard_prompts(w, rank)
 
 
 def step_roofline(w, ms_per_job: float, peaks: dict, peak_kind: str) -> dict:
@@ -113,44 +164,89 @@ class ClockSampler:
         return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons), "samples": len(sm)}
 
 
-def cpu_baseline(w, params: np.ndarray, threads: int, seqs: int, new_tokens: int) -> dict:
-    """The reference's CPU decode (oracle restatement of CachedGenerate, f64) on a bounded sample."""
-    from oracle import oracle as O
-
-    cfg = w.model
-    shape = O.Shape(embed_dim=cfg.embed_dim, num_layers=cfg.num_layers, num_heads=cfg.num_heads,
-                    block_size=cfg.block_size, vocab_size=cfg.vocab_size, mlp_hidden=cfg.mlp_hidden, kv_heads=cfg.kv,
-                    position_scheme=cfg.position_scheme, norm_kind=cfg.norm_kind, mlp_kind=cfg.mlp_kind,
-                    weight_tying=cfg.weight_tying, precision="F32")
-    model = O.Model(shape, params.astype(np.float64))
-    prompts = prompts_for(w, 0)[:seqs]
+def cpu_baseline(wd: dict, model, threads: int, seqs: int, new_tokens: int, rank: int = 0) -> dict:
+    """The reference's CPU decode (oracle restatement of CachedGenerate, f64 row math on f32 weights):
+    `seqs` of the workload's sequences, one per thread."""
+    prompts = ref_prompts(wd, rank, seqs)
     t0 = time.perf_counter()
     model.cached_generate_batch(prompts, new_tokens, threads=threads)
     dt = time.perf_counter() - t0
     return {"value": seqs * new_tokens / dt, "unit": "tokens/s", "cores": threads, "kind": "port",
-            "sample": f"{seqs} sequences x (prefill {w.prompt_len - 1} + {new_tokens} greedy tokens), f64, "
+            "cpu": cpu_model(),
+            "sample": f"{seqs} sequences x (prefill {wd['prompt_len'] - 1} + {new_tokens} greedy tokens), f64, "
                       f"{threads} threads (one sequence per thread), {dt:.1f} s"}
 
 
+def goffi_projection_bound(wd: dict, threads: int, steps: int = 32) -> dict | None:
+    """The reference's own C kernels (GoKernels/ffi/matmul_avx.c, compiled unmodified into oracle/_ref) behind
+    the pthread FanOutRows twin (matmul.go:132-163), timed on every projection of a batched decode step of
+    the workload's sequences (QKV, O, MLP up/down, LM head; f32). Decode in the reference never calls this
+    seam (its row math is inline TS), so this is an upper bound for a GoFfi-backed decode: attention, norms
+    and sampling are left out."""
+    import ctypes
+
+    from oracle import oracle as O
+
+    R = O.ref_lib()
+    if R is None:
+        return None
+    E, H, Hk, F, V, L = (wd["embed_dim"], wd["num_heads"], wd["kv_heads"], wd["mlp_hidden"], wd["vocab_size"],
+                         wd["num_layers"])
+    d = E // H
+    M = wd["seqs"]
+    up = 2 * F if wd["mlp_kind"] != "Relu" else F
+    shapes = [(E, (H + 2 * Hk) * d), (H * d, E), (E, up), (F, E)] * L + [(E, V)]
+    rng = np.random.default_rng(0)
+    bufs = []
+    for k, n in shapes:
+        a = rng.standard_normal((M, k), dtype=np.float32)
+        bt = rng.standard_normal((n, k), dtype=np.float32)
+        bufs.append((a, bt, np.empty((M, n), np.float32), k, n))
+    fp = ctypes.POINTER(ctypes.c_float)
+
+    def step():
+        for a, bt, out, k, n in bufs:
+            R.RefMatMulNTF32(a.ctypes.data_as(fp), bt.ctypes.data_as(fp), out.ctypes.data_as(fp), M, k, n, 0, threads)
+
+    step()
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        step()
+    dt = time.perf_counter() - t0
+    return {"value": M * steps / dt, "unit": "tokens/s", "cores": threads, "kind": "reference", "cpu": cpu_model(),
+            "avx2_fma": bool(R.RefCpuHasAvx2Fma()),
+            "sample": f"{steps} decode steps of {M} rows: every projection (QKV, O, MLP up/down, LM head) through the "
+                      f"reference's own AVX2 f32 kernels behind the FanOutRows twin, {threads} threads; attention, "
+                      "norms and sampling excluded (an upper bound for a GoFfi-backed decode)"}
+
+
 def run_reference(args, rank: int, world: int) -> None:
+    """The reference's CPU decode on the host cores (rank 0 only), on the workload's own sequences."""
     if rank != 0:
         return
-    w = pkg.configs.WORKLOADS[args.workload]
-    params = pkg.init_params(w.model, w.weight_seed)
+    wd = WORKLOADS[args.workload]
     threads = os.cpu_count() or 1
-    seqs, new = min(threads, w.seqs), w.new_tokens
-    for _ in range(args.warmup):
-        cpu_baseline(w, params, threads, seqs, new)
-    vals = [cpu_baseline(w, params, threads, seqs, new) for _ in range(args.steps)]
-    value = statistics.mean(v["value"] for v in vals)
-    ms = seqs * new / value * 1000.0
+    seqs, new = (wd["seqs"], wd["new_tokens"]) if wd["ref_sample"] is None else wd["ref_sample"]
+    from oracle import oracle as O
+
+    if wd["ref_sample"] is not None:
+        O.set_threads(threads)  # one long prefill: split its matmuls instead of the sequences
+    model = ref_model(wd)
+    warm = (min(2, seqs), min(4, new))
+    for _ in range(args.warmup):  # untimed warm-up on a small sample
+        cpu_baseline(wd, model, threads, *warm)
+    vals = [cpu_baseline(wd, model, threads, seqs, new) for _ in range(args.steps)]
+    ms = statistics.mean(seqs * new / v["value"] * 1000.0 for v in vals)
+    value = seqs * new / (ms / 1000.0)
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "f64", "data": "synthetic",
-        "config": {"workload": w.name, "seqs": seqs, "prompt_len": w.prompt_len, "new_tokens": new,
-                   "sample_of": f"{w.seqs} sequences x {w.new_tokens} new tokens per GPU"},
-        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "port",
+        "config": {"workload": wd["name"], "seqs_per_gpu": seqs, "prompt_len": wd["prompt_len"], "new_tokens": new,
+                   "global_batch": seqs, "seq_len": wd["prompt_len"] + new,
+                   "sample_of": f"{wd['seqs']} sequences x {wd['new_tokens']} new tokens per GPU",
+                   "warmup_sample": f"{warm[0]} sequences x {warm[1]} new tokens"},
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "port", "cpu": cpu_model(),
                          "sample": vals[0]["sample"]},
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
@@ -169,7 +265,11 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300))
     torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
+    pkg = package()
     w = pkg.configs.WORKLOADS[args.workload]
+    if args.new_tokens is not None:
+        import dataclasses
+        w = dataclasses.replace(w, new_tokens=args.new_tokens)
     cfg = w.model
     params = pkg.init_params(cfg, w.weight_seed)
     lib = pkg.load()
@@ -261,13 +361,14 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
         dist.all_reduce(te, op=dist.ReduceOp.MAX)
     e2e_value = tokens_per_step_all / (float(te.item()) / len(e2e_ms) / 1000.0)
 
-    # live per-kernel-class timing (CUDA events on the launching stream) over one extra profiled job
+    # live per-kernel-class timing (CUDA events on the launching stream) over one extra job. The decode
+    # steps of a greedy job run in ONE launch of the persistent decode loop, so the events around it perturb
+    # nothing; prefill launches are bracketed one by one and reported apart.
     sess.profile(True)
     flush.zero_()
     step()
     torch.cuda.synchronize(dev)
-    prof = {k: sess.profile_read(k) for k in ("attention", "linear", "other", "prefill_attention", "prefill_linear",
-                                                 "prefill_other")}
+    prof = {k: sess.profile_read(k) for k in sess.PROFILE_KINDS}
     sess.profile(False)
 
     if dist is not None:
@@ -277,32 +378,46 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
         return
 
     peaks, peak_kind = load_peaks()
-    dom = max(("attention", "linear"), key=lambda k: prof[k]["ms"])
-    p = prof[dom]
-    achieved = p["bytes"] / (p["ms"] / 1000.0) / 1e9 if p["ms"] > 0 else 0.0
-    traffic = None
+    traffic_ratio = {}
     tpath = os.path.join(ROOT, "profiles", "traffic_ratio.json")
     if os.path.exists(tpath):
-        ratio = json.load(open(tpath)).get(dom)
-        if ratio:
-            traffic = ratio * p["bytes"] / max(p["launches"], 1)
+        with open(tpath) as f:
+            traffic_ratio = json.load(f)
+    if prof["decode_loop"]["launches"] > 0:
+        dom, kernel = "decode_loop", "DecodeLoopKernel"
+    else:  # per-kernel decode steps (a model the loop does not take): the projection class dominates
+        dom = max(("attention", "linear"), key=lambda k: prof[k]["ms"])
+        kernel = {"attention": "decode attention kernels", "linear": "projection kernels"}[dom]
+    p = prof[dom]
+    nl = max(p["launches"], 1)
+    achieved = p["bytes"] / (p["ms"] / 1000.0) / 1e9 if p["ms"] > 0 else 0.0
+    traffic = traffic_ratio[dom] * p["bytes"] / nl if traffic_ratio.get(dom) else None
     roofline = {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
-                "frac": achieved / peaks["hbm_gbs"], "traffic": traffic, "kernel": dom, "peak_source": peak_kind,
-                "avg_launch_us": p["ms"] * 1000.0 / max(p["launches"], 1), "launches_profiled": p["launches"],
-                "algorithmic_bytes_per_launch": p["bytes"] / max(p["launches"], 1),
-                "share_of_step": p["ms"] / max(sum(prof[k]["ms"] for k in ("attention", "linear", "other")), 1e-9),
-                "scope": "decode-step launches (prefill launches are reported apart)",
-                # both HBM-bound kernel classes, measured the same way (event nodes around each kernel)
-                "classes": {k: {"avg_launch_us": prof[k]["ms"] * 1000.0 / max(prof[k]["launches"], 1),
-                                "achieved_gbs": prof[k]["bytes"] / (prof[k]["ms"] / 1000.0) / 1e9 if prof[k]["ms"] else 0.0,
-                                "frac": (prof[k]["bytes"] / (prof[k]["ms"] / 1000.0) / 1e9 / peaks["hbm_gbs"]
-                                         if prof[k]["ms"] else 0.0),
-                                "ms_per_job": prof[k]["ms"]}
-                            for k in ("attention", "linear")}}
-    cpu = None
-    if world == 1:
+                "frac": achieved / peaks["hbm_gbs"], "traffic": traffic, "kernel": kernel, "peak_source": peak_kind,
+                "launches_per_job": p["launches"], "avg_launch_ms": p["ms"] / nl,
+                "algorithmic_bytes_per_launch": p["bytes"] / nl,
+                "share_of_step": p["ms"] / ms_per_step,
+                "timing": "CUDA events on the session stream around each launch (one launch per run of decode steps)",
+                "bytes": "per decode step: every weight matrix once (bf16) + each row's cached K/V rows read and its new "
+                         "K/V row written (bf16); prefill not included"}
+    classes = {k: {"ms_per_job": v["ms"], "launches": v["launches"], "algorithmic_bytes": v["bytes"]}
+               for k, v in prof.items() if v["launches"] > 0}
+    expected = None
+    gpath = os.path.join(ROOT, "tests", "golden", "microchat_job.json")
+    if w.name == pkg.configs.MICROCHAT.name and w.new_tokens == pkg.configs.MICROCHAT.new_tokens and os.path.exists(gpath):
+        with open(gpath) as f:
+            expected = json.load(f)["checksum"]
+    output_check = {"expected_checksum_per_rank": expected,
+                    "match": None if expected is None else checksums[0] == expected,
+                    "how": "tests/golden/microchat_job.json: the ids of rank 0's 64 sequences, every id checked against "
+                           "the oracle teacher-forced on its own prefix"}
+    cpu = goffi = None
+    if world == 1:  # the reference's CPU path on this host, rank 0 at N=1 only
         threads = os.cpu_count() or 1
-        cpu = cpu_baseline(w, params, threads, min(threads, w.seqs), w.new_tokens)
+        wd = WORKLOADS[args.workload]
+        seqs, new = (w.seqs, w.new_tokens) if wd["ref_sample"] is None else wd["ref_sample"]
+        cpu = cpu_baseline(wd, ref_model(wd), threads, seqs, new)
+        goffi = goffi_projection_bound(wd, threads)
     line = {
         "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
@@ -316,10 +431,12 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
                 "d2h_bytes_per_step": int(w.seqs * w.new_tokens * 4)},
         "roofline": roofline,
         "roofline_step": step_roofline(w, ms_per_step, peaks, peak_kind),
+        "output_check": output_check,
         "cpu_baseline": cpu,
+        "cpu_baseline_goffi_kernels": goffi,
         "clocks": clk,
         "gpu_launches": int(launches),
-        "kernel_classes_ms_per_job": {k: v["ms"] for k, v in prof.items()},
+        "kernel_classes_per_job": classes,
     }
     print(json.dumps(line), flush=True)
 
@@ -330,7 +447,7 @@ def main() -> None:
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", default="microchat", choices=sorted(pkg.configs.WORKLOADS))
+    ap.add_argument("--workload", default="microchat", choices=sorted(WORKLOADS))
     ap.add_argument("--no-extras", action="store_true",
                     help="time the steps only (no e2e, profile or CPU legs): the profiling command line")
     ap.add_argument("--chains", type=int, default=0, help="concurrent decode chains (0 = library default)")
@@ -343,10 +460,6 @@ def main() -> None:
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     if args.warmup < 3:
         args.warmup = 3
-    if args.new_tokens is not None:
-        import dataclasses
-        w = pkg.configs.WORKLOADS[args.workload]
-        pkg.configs.WORKLOADS[args.workload] = dataclasses.replace(w, new_tokens=args.new_tokens)
     if args.impl == "reference":
         run_reference(args, rank, world)
     else:

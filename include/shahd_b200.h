@@ -72,11 +72,11 @@ void ShahdSetProgrammaticLaunch(int enable);
  * joined in one CUDA graph); 0 = automatic (one chain). Process-wide tuning hook;
  * no counterpart in the reference. Results do not depend on it. */
 void ShahdSetDecodeChains(int chains);
-/* Opt-in (default 0): batched decode steps of 17-128 rows as one persistent cooperative launch (one CTA
- * per SM, phases separated by grid-wide barriers) instead of one launch per kernel. Used only where the
- * model fits it (head_dim 32 or 64, 1, 2 or 4 query heads per kv head) and the GPU holds one such CTA
- * per SM. At MicroChat size it is slower than the per-kernel path, whose launches overlap. Process-wide;
- * no counterpart in the reference. Results agree with the per-kernel path within the parity tolerance. */
+/* Greedy shahd_generate / shahd_generate_device run every decode step until the next window rebuild (or the
+ * end) in ONE persistent launch when the model fits it (default 1): thread-block clusters of 16 CTAs each own up
+ * to 16 sequences for all steps (tcgen05 tiles, TMA weight streaming, cluster barriers, no host round trip and
+ * no launch per step). 0 runs one CUDA-graph-replayed launch chain per step instead. Results agree within the
+ * parity tolerance. Process-wide; no counterpart in the reference. */
 void ShahdSetPersistentStep(int enable);
 /* First error code a kernel recorded for a bounded device-side wait that gave up (0 = none). */
 int ShahdDeviceErrorFlag(void);
@@ -196,6 +196,13 @@ int shahd_verify(ShahdSession* s, const int32_t* slots, const int32_t* tokens, c
  * of rejected draft tokens after a verify pass. Pages stay assigned to the slot. */
 int shahd_truncate(ShahdSession* s, const int32_t* slots, const int32_t* lengths, int32_t n);
 
+/* Greedy CachedGenerate like shahd_generate that also records every step's logits (CachedDecoder.Logits after
+ * each push, CachedForward.ts:113-150): logits [n, max_new, vocab] fp32 on the host; row i, step k holds the
+ * logits the id out_ids[i, k] was chosen from. Needs the persistent decode loop (greedy, a model it supports);
+ * otherwise returns SHAHD_EINVAL. A parity and diagnostics entry point: the logits cross PCIe every call. */
+int shahd_generate_logits(ShahdSession* s, const int32_t* prompts, const int32_t* offsets, int32_t n, int32_t max_new,
+                          int32_t* out_ids, float* logits);
+
 /* Wait for the session's outstanding device work; returns the first recorded device error, if any. */
 int shahd_sync(ShahdSession* s);
 
@@ -209,9 +216,10 @@ int64_t shahd_kernel_launches(ShahdSession* s);
  * kernels from overlapping), and each step is waited for so its times can be read. Enabling (or
  * disabling) clears the totals. */
 int shahd_profile(ShahdSession* s, int32_t enable);
-/* Totals over the records of one class of decode-step launches: 0 = attention, 1 = projections
- * (GEMV/GEMM incl. the LM head), 2 = embed/sampler/finish; 3-5 = the same classes of prefill launches. total_ms sums the launches' event times; bytes sums their algorithmic
- * bytes (weights once + activations + KV rows read). */
+/* Totals over the records of one class of launches: 0 = attention, 1 = projections (GEMV/GEMM incl. the LM
+ * head), 2 = embed/sampler/finish of per-kernel decode steps; 3-5 = the same classes of prefill launches;
+ * 6 = the persistent decode loop (one launch per run of steps). total_ms sums the launches' event times; bytes
+ * sums their algorithmic bytes (weights once per step + KV rows read and written). */
 int shahd_profile_read(ShahdSession* s, int32_t kind, double* total_ms, int64_t* launches, double* bytes);
 
 /* SampleFromLogits (Sampler.ts:16-27) for `rows` independent logits rows on the current device: the

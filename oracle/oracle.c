@@ -515,17 +515,61 @@ int oracle_cached_step(const OracleModel* m, OracleCache* c, int token, int posi
 
 #define ST(x) (f32 ? StoreF32(x) : (x))
 
+/* Intra-op threads of the tensor matmul (1 = serial). Rows are split across threads and handled in
+ * blocks of 4 that share each streamed row of B; every output element still accumulates over pp in
+ * ascending order, so results do not depend on the thread count. */
+static int g_oracle_threads = 1;
+void oracle_set_threads(int n) { g_oracle_threads = n < 1 ? 1 : n; }
+
+typedef struct TMatJob {
+  const double *a, *b;
+  double* out;
+  int i0, i1, K, N, f32;
+} TMatJob;
+
 /* MatMul inline path, Ops/MatMul.ts:60-73: Out += AVal * B with the zero skip; each += stores. */
-static void TMatMul(const double* a, const double* b, double* out, int M, int K, int N, int f32) {
-  memset(out, 0, sizeof(double) * (size_t)M * N);
-  for (int i = 0; i < M; i++)
+static void TMatMulRows(const double* a, const double* b, double* out, int i0, int i1, int K, int N, int f32) {
+  memset(out + (size_t)i0 * N, 0, sizeof(double) * (size_t)(i1 - i0) * N);
+  for (int ib = i0; ib < i1; ib += 4) {
+    const int ie = ib + 4 < i1 ? ib + 4 : i1;
     for (int pp = 0; pp < K; pp++) {
-      double av = a[(size_t)i * K + pp];
-      if (av == 0) continue;
       const double* br = b + (size_t)pp * N;
-      double* o = out + (size_t)i * N;
-      for (int j = 0; j < N; j++) o[j] = ST(o[j] + av * br[j]);
+      for (int i = ib; i < ie; i++) {
+        double av = a[(size_t)i * K + pp];
+        if (av == 0) continue;
+        double* o = out + (size_t)i * N;
+        if (f32)
+          for (int j = 0; j < N; j++) o[j] = StoreF32(o[j] + av * br[j]);
+        else
+          for (int j = 0; j < N; j++) o[j] = o[j] + av * br[j];
+      }
     }
+  }
+}
+
+static void* TMatWorker(void* arg) {
+  TMatJob* j = (TMatJob*)arg;
+  TMatMulRows(j->a, j->b, j->out, j->i0, j->i1, j->K, j->N, j->f32);
+  return NULL;
+}
+
+static void TMatMul(const double* a, const double* b, double* out, int M, int K, int N, int f32) {
+  int nt = g_oracle_threads;
+  if (nt > M / 4) nt = M / 4;
+  if (nt <= 1 || (double)M * K * N < 4e6) {
+    TMatMulRows(a, b, out, 0, M, K, N, f32);
+    return;
+  }
+  pthread_t th[64];
+  TMatJob jobs[64];
+  if (nt > 64) nt = 64;
+  const int per = ((M + nt - 1) / nt + 3) / 4 * 4;
+  int n = 0;
+  for (int i0 = 0; i0 < M; i0 += per, n++) {
+    jobs[n] = (TMatJob){a, b, out, i0, i0 + per < M ? i0 + per : M, K, N, f32};
+    pthread_create(&th[n], NULL, TMatWorker, &jobs[n]);
+  }
+  for (int t = 0; t < n; t++) pthread_join(th[t], NULL);
 }
 
 /* MatMulNT InlineForward, Ops/MatMulNT.ts:27-43: p-ascending dot from zero, one store. */
@@ -969,6 +1013,97 @@ int oracle_cached_generate_batch(const OracleModel* m, const int32_t* prompts, i
   for (int t = 0; t < threads; t++) {
     jobs[t] = (BatchJob){m, prompts, nseq, plen, max_new, threads, t, 0, o, rng, out};
     pthread_create(&th[t], NULL, BatchWorker, &jobs[t]);
+  }
+  int rc = 0;
+  for (int t = 0; t < threads; t++) {
+    pthread_join(th[t], NULL);
+    if (jobs[t].rc) rc = jobs[t].rc;
+  }
+  free(th);
+  free(jobs);
+  return rc;
+}
+
+/* ---- teacher-forced check of externally produced greedy trajectories ----------------------------
+ * For sequence s a CachedDecoder (CachedForward.ts:113-150) is built from prompts[s]; at step k the
+ * oracle's logits, given prompt ++ ids[s][0..k), judge ids[s][k]: it passes when it is the oracle's
+ * ArgmaxOf (Distribution.ts:19-30), or when the oracle's top-2 margin is within tol x (max - min), a near
+ * tie where a rounding difference may pick either id. ids[s][k] is then pushed, so every step is judged
+ * on the checked implementation's own prefix. Outputs per sequence: failing steps, the first failing
+ * step (-1: none), near ties met with a different id, and the largest gap (max logit - logit of the
+ * chosen id) relative to the logit range. */
+typedef struct CheckJob {
+  const OracleModel* m;
+  const int32_t* prompts;
+  const int32_t* ids;
+  int nseq, plen, nnew, threads, tid, rc;
+  double tol;
+  int32_t *fails, *first_fail, *near_ties;
+  double* max_gap;
+} CheckJob;
+
+static void* CheckWorker(void* arg) {
+  CheckJob* j = (CheckJob*)arg;
+  const int V = j->m->V;
+  for (int s = j->tid; s < j->nseq; s += j->threads) {
+    const int32_t* ids = j->ids + (size_t)s * j->nnew;
+    int fails = 0, first = -1, ties = 0;
+    double worst = 0.0;
+    OracleDecoder* d = oracle_decoder_create(j->m, j->prompts + (size_t)s * j->plen, j->plen);
+    if (!d) {
+      j->rc = -1;
+      continue;
+    }
+    for (int k = 0; k < j->nnew; k++) {
+      const double* lg = d->logits;
+      const int tok = ids[k];
+      if (tok < 0 || tok >= V) {
+        fails++;
+        if (first < 0) first = k;
+        break;
+      }
+      double mx = -INFINITY, mn = INFINITY, second = -INFINITY;
+      int am = oracle_argmax(lg, V);
+      for (int v = 0; v < V; v++) {
+        if (lg[v] > mx) mx = lg[v];
+        if (lg[v] < mn) mn = lg[v];
+        if (v != am && lg[v] > second) second = lg[v];
+      }
+      const double range = mx - mn > 0 ? mx - mn : 1e-300;
+      const double gap = (mx - lg[tok]) / range;
+      if (gap > worst) worst = gap;
+      if (tok != am) {
+        if (mx - second <= j->tol * range && gap <= j->tol) {
+          ties++;
+        } else {
+          fails++;
+          if (first < 0) first = k;
+        }
+      }
+      if (k + 1 < j->nnew && oracle_decoder_push(d, tok) != 0) {
+        j->rc = -1;
+        break;
+      }
+    }
+    oracle_decoder_destroy(d);
+    j->fails[s] = fails;
+    j->first_fail[s] = first;
+    j->near_ties[s] = ties;
+    j->max_gap[s] = worst;
+  }
+  return NULL;
+}
+
+int oracle_check_trajectories(const OracleModel* m, const int32_t* prompts, int nseq, int plen, const int32_t* ids,
+                              int nnew, double tol, int threads, int32_t* fails, int32_t* first_fail,
+                              int32_t* near_ties, double* max_gap) {
+  if (threads < 1) threads = 1;
+  if (threads > nseq) threads = nseq;
+  pthread_t* th = (pthread_t*)malloc(sizeof(pthread_t) * (size_t)threads);
+  CheckJob* jobs = (CheckJob*)malloc(sizeof(CheckJob) * (size_t)threads);
+  for (int t = 0; t < threads; t++) {
+    jobs[t] = (CheckJob){m, prompts, ids, nseq, plen, nnew, threads, t, 0, tol, fails, first_fail, near_ties, max_gap};
+    pthread_create(&th[t], NULL, CheckWorker, &jobs[t]);
   }
   int rc = 0;
   for (int t = 0; t < threads; t++) {

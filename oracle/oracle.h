@@ -63,6 +63,9 @@ int64_t oracle_param_count(const OracleCfg* cfg);
  * Values are rounded to f32 when cfg->precision_f32 (Float32Array storage). */
 int oracle_init_params(const OracleCfg* cfg, uint32_t seed, double* params);
 
+/* Intra-op threads of the batched (prefill / full-forward) matmuls; results do not depend on it. */
+void oracle_set_threads(int n);
+
 /* ---- matmul semantics of the seam ---- */
 void oracle_matmul(const double* a, const double* b, double* out, int m, int k, int n);       /* TsBackend.MatMul */
 void oracle_matmul_nt(const double* a, const double* bt, double* out, int m, int k, int n, int acc);
@@ -115,6 +118,12 @@ int oracle_decoder_push(OracleDecoder* d, int token);
 const double* oracle_decoder_logits(const OracleDecoder* d);
 int oracle_decoder_cache_length(const OracleDecoder* d);
 void oracle_decoder_destroy(OracleDecoder* d);
+
+/* Teacher-forced judgement of greedy trajectories ids [nseq, nnew] produced elsewhere from prompts
+ * [nseq, plen] (one CachedDecoder per sequence over a pthread pool; see oracle.c for the rule). */
+int oracle_check_trajectories(const OracleModel* m, const int32_t* prompts, int nseq, int plen, const int32_t* ids,
+                              int nnew, double tol, int threads, int32_t* fails, int32_t* first_fail,
+                              int32_t* near_ties, double* max_gap);
 
 const char* oracle_last_error(void);
 

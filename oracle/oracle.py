@@ -66,8 +66,15 @@ class Shape:
 
 
 def build() -> None:
-    """Compile liboracle.so (and oracle/_ref when the reference tree is present)."""
+    """Compile liboracle.so (and oracle/_ref when REF_ROOT names a reference checkout)."""
     subprocess.run(["make", "-s", "-C", HERE], check=True)
+
+
+def _stale() -> bool:
+    if not os.path.exists(LIB_PATH):
+        return True
+    t = os.path.getmtime(LIB_PATH)
+    return any(os.path.getmtime(os.path.join(HERE, f)) > t for f in ("oracle.c", "oracle.h"))
 
 
 _LIB = None
@@ -76,7 +83,7 @@ _LIB = None
 def lib() -> ctypes.CDLL:
     global _LIB
     if _LIB is None:
-        if not os.path.exists(LIB_PATH):
+        if _stale():
             build()
         L = ctypes.CDLL(LIB_PATH)
         L.oracle_mix_seed.restype = ctypes.c_uint32
@@ -122,6 +129,9 @@ def lib() -> ctypes.CDLL:
         L.oracle_decoder_logits.argtypes = [ctypes.c_void_p]
         L.oracle_decoder_cache_length.argtypes = [ctypes.c_void_p]
         L.oracle_decoder_destroy.argtypes = [ctypes.c_void_p]
+        L.oracle_set_threads.argtypes = [_i32]
+        L.oracle_check_trajectories.argtypes = [ctypes.c_void_p, _ip, _i32, _i32, _ip, _i32, ctypes.c_double, _i32,
+                                                _ip, _ip, _ip, _dp]
         L.oracle_last_error.restype = ctypes.c_char_p
         _LIB = L
     return _LIB
@@ -184,6 +194,11 @@ def create_streams(seed: int) -> list[int]:
     out = np.zeros(4, dtype=np.uint32)
     lib().oracle_create_streams(seed & 0xFFFFFFFF, _u(out))
     return [int(v) for v in out]
+
+
+def set_threads(n: int) -> None:
+    """Threads of the oracle's batched matmuls (prefill and full forward); results do not depend on it."""
+    lib().oracle_set_threads(int(n))
 
 
 def uniform_ids(count: int, vocab: int, seed: int) -> np.ndarray:
@@ -291,6 +306,24 @@ class Model:
         o = sampling(temperature, top_k, top_p)
         _check(lib().oracle_generate(self.handle, _i(prompt), prompt.size, max_new, ctypes.byref(o), _u(st), _i(out)))
         return out, int(st[0])
+
+    def check_trajectories(self, prompts: np.ndarray, ids: np.ndarray, tol: float, threads: int = 0) -> dict:
+        """Teacher-forced judgement of greedy ids [nseq, nnew] produced elsewhere from prompts [nseq, plen]:
+        each id must be the oracle's argmax on the same prefix unless the oracle's top-2 margin is within
+        tol x logit range. Returns per-sequence failing steps, first failing step (-1 none), near ties
+        met with a different id and the largest (max - chosen) logit gap relative to the range."""
+        prompts = np.ascontiguousarray(prompts, dtype=np.int32)
+        ids = np.ascontiguousarray(ids, dtype=np.int32)
+        nseq, plen = prompts.shape
+        nnew = ids.shape[1]
+        fails = np.zeros(nseq, np.int32)
+        first = np.full(nseq, -1, np.int32)
+        ties = np.zeros(nseq, np.int32)
+        gap = np.zeros(nseq, np.float64)
+        threads = threads or (os.cpu_count() or 1)
+        _check(lib().oracle_check_trajectories(self.handle, _i(prompts), nseq, plen, _i(ids), nnew, float(tol), threads,
+                                               _i(fails), _i(first), _i(ties), _d(gap)))
+        return {"fails": fails, "first_fail": first, "near_ties": ties, "max_gap": gap}
 
     def cached_generate_batch(self, prompts: np.ndarray, max_new: int, rng_states: np.ndarray | None = None,
                               threads: int = 1, temperature=0.0, top_k=0, top_p=1.0) -> np.ndarray:

@@ -75,6 +75,7 @@ SIGNATURES = {
     "shahd_step": (ctypes.c_int, [_vp, _ip, _ip, _i32, _fp, _ip]),
     "shahd_generate": (ctypes.c_int, [_vp, _ip, _ip, _i32, _i32, ctypes.POINTER(ShahdSampling), _up, _ip]),
     "shahd_generate_device": (ctypes.c_int, [_vp, _vp, _ip, _i32, _i32, ctypes.POINTER(ShahdSampling), _vp, _vp, _vp]),
+    "shahd_generate_logits": (ctypes.c_int, [_vp, _ip, _ip, _i32, _i32, _ip, _fp]),
     "shahd_sync": (ctypes.c_int, [_vp]),
     "shahd_verify": (ctypes.c_int, [_vp, _ip, _ip, _ip, _i32, _fp, _ip]),
     "shahd_truncate": (ctypes.c_int, [_vp, _ip, _ip, _i32]),

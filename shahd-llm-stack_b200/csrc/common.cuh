@@ -33,6 +33,17 @@ using bf16 = __nv_bfloat16;
 // before GridDepWait(). Process-wide switch, on by default.
 extern bool g_use_pdl;
 
+// First launch failure on this thread since the last TakeLaunchError() (a kernel that did not launch, or
+// could not be prepared, e.g. a tensor map that failed to encode). Launch helpers record into it instead of
+// returning silently, and every entry point that enqueues kernels checks it before reporting success.
+void NoteLaunchError(cudaError_t e, const char* what);
+cudaError_t TakeLaunchError(std::string* what);
+
+// Sets a kernel's dynamic shared memory limit (and, optionally, non-portable cluster sizes) once per
+// (device, kernel): function attributes belong to the device's context, and sessions on several devices
+// may run in one process. Thread-safe. Returns false (and records the failure) when the runtime refuses.
+bool EnsureKernelAttrs(const void* fn, int smem_bytes, bool nonportable_cluster = false);
+
 template <typename... KArgs, typename... Args>
 inline void LaunchPdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, Args... args) {
   cudaLaunchConfig_t cfg = {};
@@ -45,7 +56,8 @@ inline void LaunchPdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = g_use_pdl ? 1 : 0;
-  cudaLaunchKernelEx(&cfg, kern, args...);
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, args...);
+  if (e != cudaSuccess) NoteLaunchError(e, "kernel launch");
 }
 
 // LaunchPdl with the CTAs grouped into thread-block clusters of `cluster` (grid divisible by it).
@@ -66,7 +78,8 @@ inline void LaunchPdlCluster(void (*kern)(KArgs...), dim3 grid, dim3 block, size
   attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = g_use_pdl ? 2 : 1;
-  cudaLaunchKernelEx(&cfg, kern, args...);
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, args...);
+  if (e != cudaSuccess) NoteLaunchError(e, "cluster kernel launch");
 }
 
 __host__ __device__ inline int CeilDiv(int a, int b) { return (a + b - 1) / b; }

@@ -3,10 +3,13 @@
 #include <cstdarg>
 #include <cstring>
 #include <mutex>
+#include <set>
 #include <string>
+#include <tuple>
 
 #include "../../include/shahd_b200.h"
 #include "common.cuh"
+#include "gemm_tf32.cuh"
 #include "umma_linear.cuh"
 
 namespace shahd {
@@ -14,10 +17,50 @@ namespace shahd {
 int g_umma_min_rows = 17;
 bool g_use_pdl = true;
 int g_decode_chains = 0;  // 0 = automatic
-int g_persistent_step = 0;  // decode steps as one cooperative launch (opt-in: slower at MicroChat size)
+int g_persistent_step = 1;  // greedy generate runs its decode steps in the persistent cluster loop
 
 // ---- thread-local last error --------------------------------------------------------------------
 static thread_local std::string t_error;
+
+static thread_local cudaError_t t_launch_err = cudaSuccess;
+static thread_local std::string t_launch_what;
+
+void NoteLaunchError(cudaError_t e, const char* what) {
+  if (t_launch_err == cudaSuccess) {
+    t_launch_err = e;
+    t_launch_what = what;
+  }
+}
+
+cudaError_t TakeLaunchError(std::string* what) {
+  const cudaError_t e = t_launch_err;
+  if (what) *what = t_launch_what;
+  t_launch_err = cudaSuccess;
+  t_launch_what.clear();
+  return e;
+}
+
+bool EnsureKernelAttrs(const void* fn, int smem_bytes, bool nonportable_cluster) {
+  static std::mutex mu;
+  static std::set<std::tuple<int, const void*, int, bool>> done;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) {
+    NoteLaunchError(cudaErrorInvalidDevice, "cudaGetDevice before setting kernel attributes");
+    return false;
+  }
+  const auto key = std::make_tuple(dev, fn, smem_bytes, nonportable_cluster);
+  std::lock_guard<std::mutex> g(mu);
+  if (done.count(key)) return true;
+  cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes);
+  if (e == cudaSuccess && nonportable_cluster) e = cudaFuncSetAttribute(fn, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    NoteLaunchError(e, "cudaFuncSetAttribute");
+    return false;
+  }
+  done.insert(key);
+  return true;
+}
 
 void SetError(const char* fmt, ...) {
   char buf[1024];
@@ -100,12 +143,19 @@ static Workspace& WorkspaceFor(int dev) {
   return ws[dev & 63];
 }
 
+// Whether the calling thread's current device is an sm_100 GPU this build runs on.
 static int DeviceOk() {
-  int n = 0;
-  if (cudaGetDeviceCount(&n) != cudaSuccess || n < 1) return 0;
-  cudaDeviceProp p;
-  if (cudaGetDeviceProperties(&p, 0) != cudaSuccess) return 0;
-  return p.major == 10 ? 1 : 0;
+  int n = 0, dev = 0, major = 0;
+  if (cudaGetDeviceCount(&n) != cudaSuccess || n < 1) {
+    cudaGetLastError();
+    return 0;
+  }
+  if (cudaGetDevice(&dev) != cudaSuccess ||
+      cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess) {
+    cudaGetLastError();
+    return 0;
+  }
+  return major == 10 ? 1 : 0;
 }
 
 static bool CheckDims(const char* op, long long m, long long k, long long n) {
@@ -120,6 +170,10 @@ static bool CheckDims(const char* op, long long m, long long k, long long n) {
 }
 
 enum Layout { kNN, kNT, kTN };
+
+static int NumSMs(int dev);
+
+static size_t Align64(size_t n) { return (n + 63) / 64 * 64; }  // 256-byte boundaries between workspace regions
 
 template <typename T>
 static void RunSeam(const char* op, Layout lay, const T* a, const T* b, T* out, int m, int k, int n, int acc) {
@@ -139,7 +193,11 @@ static void RunSeam(const char* op, Layout lay, const T* a, const T* b, T* out, 
   std::lock_guard<std::mutex> g(w.mu);
   const size_t na = (size_t)m * k, nb = lay == kTN ? (size_t)m * n : (size_t)k * n;
   const size_t no = lay == kTN ? (size_t)k * n : (size_t)m * n;
-  const size_t need = (na + nb + no) * sizeof(T) + 256;
+  // f32 NT / NN with enough rows: split-TF32 tensor-core GEMM (A, A lo, B as [n,k], B lo, C, NN: B as given)
+  const bool tc = sizeof(T) == 4 && lay != kTN && Tf32Eligible(m, k, n);
+  const size_t need = tc ? (2 * Align64(na) + 2 * Align64((size_t)n * k) + Align64(no) + (lay == kNN ? Align64(nb) : 0)) *
+                               sizeof(T)
+                         : (na + nb + no) * sizeof(T) + 256;
   if (w.cap < need) {
     if (w.buf) cudaFree(w.buf);
     w.buf = nullptr;
@@ -151,6 +209,29 @@ static void RunSeam(const char* op, Layout lay, const T* a, const T* b, T* out, 
     w.cap = need;
   }
   if (!w.stream) cudaStreamCreateWithFlags(&w.stream, cudaStreamNonBlocking);
+  cudaGetLastError();
+  if (tc) {
+    float* da = static_cast<float*>(w.buf);
+    float* da_lo = da + Align64(na);
+    float* dbt = da_lo + Align64(na);
+    float* db_lo = dbt + Align64((size_t)n * k);
+    float* dc = db_lo + Align64((size_t)n * k);
+    cudaMemcpyAsync(da, a, na * 4, cudaMemcpyHostToDevice, w.stream);
+    if (lay == kNT) {
+      cudaMemcpyAsync(dbt, b, nb * 4, cudaMemcpyHostToDevice, w.stream);
+    } else {  // MatMulF32: b is [k, n]; the GEMM wants it K-major [n, k]
+      float* dbn = dc + Align64(no);
+      cudaMemcpyAsync(dbn, b, nb * 4, cudaMemcpyHostToDevice, w.stream);
+      TransposeF32Kernel<<<dim3(CeilDiv(n, 32), CeilDiv(k, 32)), dim3(32, 8), 0, w.stream>>>(dbn, dbt, k, n);
+    }
+    if (acc) cudaMemcpyAsync(dc, out, no * 4, cudaMemcpyHostToDevice, w.stream);
+    cudaError_t e = GemmNtTf32x3(da, da_lo, dbt, db_lo, dc, m, k, n, acc, NumSMs(dev), w.stream);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(out, dc, no * 4, cudaMemcpyDeviceToHost, w.stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(w.stream);
+    if (e == cudaSuccess) e = cudaGetLastError();
+    if (e != cudaSuccess) SetError("%s: device error: %s", op, cudaGetErrorString(e));
+    return;
+  }
   T* da = static_cast<T*>(w.buf);
   T* db = da + na;
   T* dc = db + nb;
@@ -338,10 +419,10 @@ int GemmNtBf16(const void* a, const void* bt, float* out, int m, int k, int n, i
     SetError("ShahdMatMulNTBF16Device: cuTensorMapEncodeTiled failed");
     return SHAHD_ECUDA;
   }
-  static bool configured = false;
-  if (!configured) {
-    cudaFuncSetAttribute(GemmNtBf16Kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemmSmem);
-    configured = true;
+  if (!EnsureKernelAttrs((const void*)GemmNtBf16Kernel, kGemmSmem)) {
+    TakeLaunchError(nullptr);
+    SetError("ShahdMatMulNTBF16Device: the GEMM kernel's shared-memory limit could not be set");
+    return SHAHD_ECUDA;
   }
   int dev = 0;
   cudaGetDevice(&dev);

@@ -9,6 +9,8 @@
 #include <algorithm>
 #include <cmath>
 #include <cstdarg>
+#include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <map>
 #include <mutex>
@@ -21,7 +23,7 @@
 #include "params.h"
 #include "prefill_attention.cuh"
 #include "sampling.cuh"
-#include "step_kernel.cuh"
+#include "decode_loop.cuh"
 #include "umma_linear.cuh"
 
 namespace shahd {
@@ -84,6 +86,7 @@ struct ShahdSession {
   cudaEvent_t join_in = nullptr, join_out = nullptr;
   std::mutex mu;
   std::vector<void*> allocs;
+  std::map<void*, size_t> alloc_bytes;
 
   std::vector<shahd::Layer> layers;
   shahd::bf16* w_head;
@@ -106,14 +109,15 @@ struct ShahdSession {
   int am_stride;
   float *part_o, *part_m, *part_l;
   int* attn_counter;
-  // persistent decode step: weight tensor maps and per-layer constants in device memory, activation
-  // tensor maps per row count, the grid-barrier counter and abort flag
-  int step_state = -1;  // -1 not set up yet, 0 unavailable on this device/model, 1 ready
-  int step_bn[5] = {};  // tile widths: qkv, o, up, down, head
-  shahd::StepLayer* d_step_layers = nullptr;
-  CUtensorMap* d_step_wmaps = nullptr;
-  std::map<int, CUtensorMap*> step_amaps;
-  unsigned* d_step_sync = nullptr;  // [barrier counter, abort flag]
+  // persistent cluster decode loop: weight tensor maps (box 64 x 128) and per-layer constants in device memory
+  int loop_state = -1;  // -1 not set up yet, 0 unavailable for this model/device, 1 ready
+  shahd::LoopLayer* d_loop_layers = nullptr;
+  CUtensorMap* d_loop_wmaps = nullptr;
+  int loop_max_clusters = 0;  // clusters of kLoopCS CTAs resident at once with the loop's shared memory
+  float* d_loop_logits = nullptr;  // recorded logits of shahd_generate_logits [rows, steps, V]
+  size_t loop_logits_cap = 0;
+  unsigned long long* d_loop_trace = nullptr;  // per-phase timestamps when SHAHD_LOOP_TRACE names a file
+  size_t loop_trace_cap = 0;
   // verify passes (speculative decoding): per-row logits, argmax partials and ids, grown on demand
   float* d_vlogits = nullptr;
   float* d_vam_val = nullptr;
@@ -176,6 +180,7 @@ int DevAlloc(ShahdSession* s, T** p, size_t count) {
     return e == cudaErrorMemoryAllocation ? SHAHD_ENOMEM : SHAHD_ECUDA;
   }
   s->allocs.push_back(v);
+  s->alloc_bytes[v] = count * sizeof(T);
   *p = static_cast<T*>(v);
   return SHAHD_OK;
 }
@@ -191,11 +196,7 @@ int DevAlloc(ShahdSession* s, T** p, size_t count) {
 template <int MT, int NORM, class Epi>
 void LaunchSimt(const LinearArgs& la, const Epi& epi, cudaStream_t st) {
   const size_t smem = (size_t)MT * la.Kp * sizeof(float);
-  static bool configured = false;  // per template instance; the attribute is per function
-  if (!configured) {
-    cudaFuncSetAttribute(LinearSimtKernel<MT, NORM, Epi>, cudaFuncAttributeMaxDynamicSharedMemorySize, 224 * 1024);
-    configured = true;
-  }
+  if (!EnsureKernelAttrs((const void*)LinearSimtKernel<MT, NORM, Epi>, 224 * 1024)) return;
   dim3 grid(CeilDiv(la.N, kSimtCols), CeilDiv(la.M, MT));
   LaunchPdl(LinearSimtKernel<MT, NORM, Epi>, grid, dim3(kSimtWarps * 32), smem, st, la, epi);
 }
@@ -260,8 +261,8 @@ struct StepPlan {
 
 // ---- measurement hooks: kernel classes timed with CUDA events on the launching stream ---------------
 // Classes 0-2 are decode-step launches; prefill launches (steps without the finish kernel) land in 3-5.
-// Class 6: the persistent decode step (all of a step's projections and attention in one launch).
-enum ProfKind { kProfAttention = 0, kProfLinear = 1, kProfOther = 2, kProfPrefill = 3, kProfFused = 6, kProfKinds = 7 };
+// Class 6: the persistent cluster decode loop (every decode step of a run in one launch).
+enum ProfKind { kProfAttention = 0, kProfLinear = 1, kProfOther = 2, kProfPrefill = 3, kProfLoop = 6, kProfKinds = 7 };
 
 // An event recorded on `st`: inside a stream capture it becomes an event-record node of the graph (each
 // replay records it again), otherwise a plain record from the recycled pool.
@@ -365,83 +366,6 @@ LinearArgs Lin(const float* a, int lda, const bf16* ab, int ldab, int rows_cap, 
   return la;
 }
 
-// ---- persistent decode step (one cooperative launch per step) ------------------------------------
-
-using StepKernelFn = void (*)(StepDesc);
-
-StepKernelFn StepKernelFor(int norm, int d) {
-  if (norm == kNormRms) return d == 64 ? DecodeStepKernel<kNormRms, 64> : DecodeStepKernel<kNormRms, 32>;
-  return d == 64 ? DecodeStepKernel<kNormLayer, 64> : DecodeStepKernel<kNormLayer, 32>;
-}
-
-// One-time set-up: weight tensor maps and per-layer constants in device memory, the sync words, and the
-// check that one CTA with the step's shared memory fits on every SM (a cooperative launch needs all of
-// them resident at once). Returns whether the persistent step can run for this session.
-bool StepSetup(ShahdSession* s) {
-  if (s->step_state >= 0) return s->step_state == 1;
-  s->step_state = 0;
-  if (!(s->d == 64 || s->d == 32) || !(s->G == 1 || s->G == 2 || s->G == 4)) return false;
-  const int norm = s->cfg.norm_kind == 1 ? kNormRms : kNormLayer;
-  const StepKernelFn fn = StepKernelFor(norm, s->d);
-  if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, kStepSmemDyn) != cudaSuccess) {
-    cudaGetLastError();
-    return false;
-  }
-  int per_sm = 0;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, kStepThreads, kStepSmemDyn) != cudaSuccess ||
-      per_sm < 1) {
-    cudaGetLastError();
-    return false;
-  }
-  int coop = 0;
-  cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, s->device);
-  if (!coop) return false;
-  // the persistent kernel's tile widths: 16 for the layer projections, 32 for the LM head
-  s->step_bn[0] = s->step_bn[1] = s->step_bn[2] = s->step_bn[3] = 16;
-  s->step_bn[4] = 32;
-  std::vector<CUtensorMap> wm(4 * s->L + 1);
-  for (int l = 0; l < s->L; l++) {
-    const Layer& Ly = s->layers[l];
-    if (!MakeTmaBf16(Ly.w_qkv, s->Nqkv, s->Ep, s->Ep, s->step_bn[0], &wm[4 * l]) ||
-        !MakeTmaBf16(Ly.w_o, s->E, s->HDp, s->HDp, s->step_bn[1], &wm[4 * l + 1]) ||
-        !MakeTmaBf16(Ly.w_up, s->Nup, s->Ep, s->Ep, s->step_bn[2], &wm[4 * l + 2]) ||
-        !MakeTmaBf16(Ly.w_down, s->E, s->Fp, s->Fp, s->step_bn[3], &wm[4 * l + 3]))
-      return false;
-  }
-  if (!MakeTmaBf16(s->w_head, s->V, s->Ep, s->Ep, s->step_bn[4], &wm[4 * s->L])) return false;
-  std::vector<StepLayer> ly(s->L);
-  for (int l = 0; l < s->L; l++) {
-    const Layer& Ly = s->layers[l];
-    ly[l] = StepLayer{Ly.qkv_c1, Ly.qkv_c2, Ly.up_c1, Ly.up_c2, Ly.b_fc, Ly.b_proj};
-  }
-  if (DevAlloc(s, &s->d_step_wmaps, wm.size()) != SHAHD_OK || DevAlloc(s, &s->d_step_layers, ly.size()) != SHAHD_OK ||
-      DevAlloc(s, &s->d_step_sync, 2) != SHAHD_OK)
-    return false;
-  if (cudaMemcpy(s->d_step_wmaps, wm.data(), sizeof(CUtensorMap) * wm.size(), cudaMemcpyHostToDevice) != cudaSuccess ||
-      cudaMemcpy(s->d_step_layers, ly.data(), sizeof(StepLayer) * ly.size(), cudaMemcpyHostToDevice) != cudaSuccess ||
-      cudaMemset(s->d_step_sync, 0, 2 * sizeof(unsigned)) != cudaSuccess)
-    return false;
-  s->step_state = 1;
-  return true;
-}
-
-// Activation tensor maps (xb, ctxb, actb) with tiles of the rows a step of M rows uses.
-const CUtensorMap* StepActivationMaps(ShahdSession* s, int M) {
-  const int box = UmmaBoxRows(M);
-  auto it = s->step_amaps.find(box);
-  if (it != s->step_amaps.end()) return it->second;
-  CUtensorMap am[3];
-  if (!MakeTmaBf16(s->xb, s->rows_cap, s->Ep, s->Ep, box, &am[0]) ||
-      !MakeTmaBf16(s->ctxb, s->rows_cap, s->HDp, s->HDp, box, &am[1]) ||
-      !MakeTmaBf16(s->actb, s->rows_cap, s->Fp, s->Fp, box, &am[2]))
-    return nullptr;
-  CUtensorMap* d = nullptr;
-  if (DevAlloc(s, &d, 3) != SHAHD_OK) return nullptr;
-  if (cudaMemcpy(d, am, sizeof(am), cudaMemcpyHostToDevice) != cudaSuccess) return nullptr;
-  s->step_amaps[box] = d;
-  return d;
-}
-
 // Whether a step's finish kernel also embeds the next step's input (decode-loop steps), so that the
 // following step skips its embed kernel.
 bool EmbedsNext(const StepPlan& p) {
@@ -484,58 +408,8 @@ int EnqueueStep(ShahdSession* s, const StepPlan& p, cudaStream_t st, int r0 = 0,
   int* counter = s->attn_counter + rd * s->Hk;
   float* split_ws = s->split_ws + (size_t)chain * s->split_ws_floats;
   int* split_cnt = s->split_cnt + (size_t)chain * s->split_cnt_len;
-  // decode rows of the batched regime: the whole step (embed .. LM head) as one persistent launch
-  const bool fused = g_persistent_step && r0 == 0 && chain == 0 && s->chains_hint <= 1 && p.head && p.finish &&
-                     p.pos_in == nullptr && p.poff == nullptr && p.tok != nullptr && M >= kUmmaMinRows &&
-                     M <= kUmmaBM && StepSetup(s);
   int nblk = 0;
-  if (fused) {
-    const CUtensorMap* amaps = StepActivationMaps(s, M);
-    if (amaps == nullptr) {
-      SetError("internal: tensor maps of the persistent step could not be made");
-      return -1;
-    }
-    StepDesc d;
-    d.M = M; d.E = s->E; d.Ep = s->Ep; d.H = s->H; d.Hk = s->Hk; d.d = s->d; d.G = s->G; d.F = s->F; d.Fp = s->Fp;
-    d.V = s->V; d.L = s->L; d.HDp = s->HDp; d.Nqkv = s->Nqkv; d.Nup = s->Nup;
-    d.norm = norm; d.mlp_kind = s->cfg.mlp_kind;
-    d.bn_qkv = s->step_bn[0]; d.bn_o = s->step_bn[1]; d.bn_up = s->step_bn[2]; d.bn_down = s->step_bn[3];
-    d.bn_head = s->step_bn[4];
-    d.ks_o = UmmaKSplit(M, s->E, s->HDp);
-    d.ks_down = UmmaKSplit(M, s->E, s->Fp);
-    d.a_box_rows = UmmaBoxRows(M);
-    d.eps = eps;
-    d.scale = (float)(1.0 / std::sqrt((double)s->d));
-    d.x = x; d.q = q; d.ctx = ctx; d.act = act; d.logits = p.logits;
-    d.xb = xb; d.ctxb = ctxb; d.actb = actb;
-    d.pos = pos; d.slot = p.slot; d.tok = p.tok; d.seq_len = s->d_seq_len;
-    d.wte = s->wte; d.wpe = s->wpe; d.rope_cos = s->rope_cos; d.rope_sin = s->rope_sin;
-    d.head_bias = s->head_bias; d.head_c1 = s->head_c1; d.head_c2 = s->head_c2;
-    d.am_val = am_val; d.am_idx = am_idx;
-    d.kv = KvView{s->kv_pool, s->d_block_table, s->max_blocks, s->Hk, s->d, s->page_elems};
-    d.layers = s->d_step_layers; d.wmaps = s->d_step_wmaps; d.amaps = amaps;
-    d.ws = split_ws; d.ws_cnt = split_cnt;
-    d.bar = s->d_step_sync; d.abort_flag = reinterpret_cast<int*>(s->d_step_sync + 1);
-    double bytes = 8.0 * M * s->E + LinearBytes(M, s->E, s->Ep, s->V) + 10.0 * M * hd * s->L;
-    bytes += s->L * (LinearBytes(M, s->E, s->Ep, s->Nqkv) + LinearBytes(M, hd, s->HDp, s->E) +
-                     LinearBytes(M, s->E, s->Ep, s->Nup) + LinearBytes(M, s->F, s->Fp, s->E));
-    cudaMemsetAsync(s->d_step_sync, 0, 2 * sizeof(unsigned), st);
-    const StepKernelFn fn = StepKernelFor(norm, s->d);
-    Timed(s, st, kProfFused, bytes, [&] {
-      cudaLaunchConfig_t lc = {};
-      lc.gridDim = dim3(s->num_sms);
-      lc.blockDim = dim3(kStepThreads);
-      lc.dynamicSmemBytes = kStepSmemDyn;
-      lc.stream = st;
-      cudaLaunchAttribute at[1];
-      at[0].id = cudaLaunchAttributeCooperative;
-      at[0].val.cooperative = 1;
-      lc.attrs = at;
-      lc.numAttrs = 1;
-      cudaLaunchKernelEx(&lc, fn, d);
-    }, 4.0 * s->Hk * s->d * s->L, (double)p.attended, chain);
-    nblk = CeilDiv(s->V, s->step_bn[4]);
-  } else {
+  {
     if (!p.embed_ready) {
       Timed(s, st, pk + kProfOther, 8.0 * M * s->E, [&] {
         EmbedArgs e{p.pos_in, p.slot, p.tok, p.prompt, p.poff, s->d_seq_len, pos, s->wte, s->wpe, x, xb, s->E, s->Ep};
@@ -644,8 +518,17 @@ int DecodeChains(int n) {
   return std::max(1, std::min(std::min(c, kMaxChains), n));
 }
 
+// Reports a kernel that failed to launch (or could not be prepared) since the last check, then any sticky
+// runtime error.
 int CheckLaunch(const char* what) {
-  cudaError_t e = cudaGetLastError();
+  std::string where;
+  cudaError_t e = TakeLaunchError(&where);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    SetError("%s: %s failed: %s", what, where.c_str(), cudaGetErrorString(e));
+    return SHAHD_ECUDA;
+  }
+  e = cudaGetLastError();
   if (e != cudaSuccess) {
     SetError("%s: kernel launch failed: %s", what, cudaGetErrorString(e));
     return SHAHD_ECUDA;
@@ -727,9 +610,16 @@ int RunStep(ShahdSession* s, const StepPlan* plans, const int* r0, int nchain, i
     const int n = enqueue();
     s->capturing = false;
     s->launches = saved;
+    std::string where;
+    const cudaError_t le = TakeLaunchError(&where);
     it->second.recs.swap(s->prof_recs);
     s->prof_recs.clear();
     cudaError_t e = cudaStreamEndCapture(s->stream, &g);
+    if (le != cudaSuccess) {
+      if (g) cudaGraphDestroy(g);
+      SetError("step capture: %s failed: %s", where.c_str(), cudaGetErrorString(le));
+      return SHAHD_ECUDA;
+    }
     if (e != cudaSuccess) {
       SetError("step capture failed: %s", cudaGetErrorString(e));
       return SHAHD_ECUDA;
@@ -983,10 +873,226 @@ int GrowOut(ShahdSession* s, size_t count) {
   return SHAHD_OK;
 }
 
+// ---- persistent cluster decode loop: eligibility, shared-memory plan, launch ------------------------
+
+using LoopKernelFn = void (*)(const LoopDesc);
+constexpr size_t kLoopSmemBudget = 227 * 1024;  // dynamic shared memory of one CTA at most
+
+LoopKernelFn LoopKernelFor(int d, int G) {
+  const int mg = G <= 1 ? 1 : (G <= 2 ? 2 : 4);
+  if (d == 64) return mg == 1 ? DecodeLoopKernel<64, 1> : (mg == 2 ? DecodeLoopKernel<64, 2> : DecodeLoopKernel<64, 4>);
+  return mg == 1 ? DecodeLoopKernel<32, 1> : (mg == 2 ? DecodeLoopKernel<32, 2> : DecodeLoopKernel<32, 4>);
+}
+
+// Shared-memory plan of a launch whose clusters hold `rows` rows; returns the bytes (0: does not fit).
+size_t LoopPlan(const ShahdSession* s, int rows, LoopDesc* D) {
+  const int max_items = CeilDiv(rows * s->Hk, kLoopCS);
+  const int nq = CeilDiv(CeilDiv(s->Nqkv, 128), kLoopCS), nu = CeilDiv(CeilDiv(s->Nup, 128), kLoopCS);
+  const int gd = s->G * s->d;
+  size_t off = 0;
+  auto take = [&](size_t bytes, size_t align) {
+    off = (off + align - 1) / align * align;
+    const size_t at = off;
+    off += bytes;
+    return (int)at;
+  };
+  // everything after the ring; the ring depth is chosen last
+  size_t tail = 0;
+  {
+    off = 0;
+    D->off_xb = take((size_t)(s->Ep / 64) * kLoopOpBlock, 1024);
+    D->off_ctxb = take((size_t)CeilDiv(gd, 64) * kLoopOpBlock, 1024);
+    D->off_actb = take((size_t)nu * LoopActKb(s->cfg.mlp_kind) * kLoopOpBlock, 1024);
+    D->off_xf = take((size_t)kLoopRows * s->E * 4, 16);
+    D->off_qkv = take((size_t)nq * kLoopRows * 128 * 4, 16);
+    D->off_opart = take((size_t)max_items * s->E * 4, 16);
+    D->off_dpart = take((size_t)s->E * kLoopRows * 4, 16);
+    D->off_xs = take((size_t)kLoopRows * (s->E / kLoopCS) * 4, 16);
+    D->off_att = take((size_t)std::max(kLoopWarps, max_items) * (2 * s->G + gd) * 4, 16);
+    D->off_sq = take((size_t)max_items * gd * 4, 16);
+    D->off_misc = take(sizeof(LoopMisc), 16);
+    tail = off;
+  }
+  const size_t budget = kLoopSmemBudget - 1024;  // the kernel aligns its base to 1024 bytes
+  if (tail + 4 * (size_t)kLoopStageBytes > budget) return 0;
+  const int stages = (int)std::min<size_t>(kLoopMaxStages, (budget - tail) / kLoopStageBytes);
+  const int ring = stages * kLoopStageBytes;
+  D->off_xb += ring; D->off_ctxb += ring; D->off_actb += ring; D->off_xf += ring; D->off_qkv += ring;
+  D->off_opart += ring; D->off_dpart += ring; D->off_xs += ring; D->off_att += ring; D->off_sq += ring;
+  D->off_misc += ring;
+  D->stages = stages;
+  D->max_items = max_items;
+  return ring + tail + 1024;
+}
+
+// The decode loop runs greedy decode steps of models whose shapes fit its fixed work split: head_dim 32 or
+// 64, at most four query heads per kv head, kv heads dividing the cluster, E a multiple of 64 up to 512,
+// at most four QKV / MLP-up tiles of 128 features per CTA. One-time set-up per session: tensor maps of
+// every weight (box 64 x 128), the per-layer constants, kernel attributes and the resident-cluster count.
+bool LoopSetup(ShahdSession* s) {
+  if (s->loop_state >= 0) return s->loop_state == 1;
+  s->loop_state = 0;
+  if (!(s->d == 32 || s->d == 64) || s->G > 4 || kLoopCS % s->Hk != 0) return false;
+  if (s->E % 64 != 0 || s->E > 512 || s->Ep != s->E) return false;
+  if (CeilDiv(CeilDiv(s->Nqkv, 128), kLoopCS) > kLoopMaxTiles || CeilDiv(CeilDiv(s->Nup, 128), kLoopCS) > kLoopMaxTiles ||
+      CeilDiv(s->E, 128) > kLoopMaxTiles)
+    return false;
+  LoopDesc D{};
+  if (LoopPlan(s, kLoopRows, &D) == 0) return false;
+  // every plan (any rows per cluster: fewer rows leave room for a deeper weight ring) fits the budget
+  const size_t smem = kLoopSmemBudget;
+  const LoopKernelFn fn = LoopKernelFor(s->d, s->G);
+  if (!EnsureKernelAttrs((const void*)fn, (int)smem, true)) {
+    TakeLaunchError(nullptr);  // not an error of the caller's run: the per-kernel path takes over
+    return false;
+  }
+  cudaLaunchConfig_t lc = {};
+  lc.gridDim = dim3(kLoopCS * 8);
+  lc.blockDim = dim3(kLoopThreads);
+  lc.dynamicSmemBytes = smem;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeClusterDimension;
+  at[0].val.clusterDim.x = kLoopCS;
+  at[0].val.clusterDim.y = 1;
+  at[0].val.clusterDim.z = 1;
+  lc.attrs = at;
+  lc.numAttrs = 1;
+  int nclusters = 0;
+  if (cudaOccupancyMaxActiveClusters(&nclusters, (void*)fn, &lc) != cudaSuccess || nclusters < 1) {
+    cudaGetLastError();
+    return false;
+  }
+  std::vector<CUtensorMap> wm(4 * s->L + 1);
+  for (int l = 0; l < s->L; l++) {
+    const Layer& Ly = s->layers[l];
+    if (!MakeTmaBf16(Ly.w_qkv, s->Nqkv, s->Ep, s->Ep, 128, &wm[4 * l]) ||
+        !MakeTmaBf16(Ly.w_o, s->E, s->HDp, s->HDp, 128, &wm[4 * l + 1]) ||
+        !MakeTmaBf16(Ly.w_up, s->Nup, s->Ep, s->Ep, 128, &wm[4 * l + 2]) ||
+        !MakeTmaBf16(Ly.w_down, s->E, s->Fp, s->Fp, 128, &wm[4 * l + 3]))
+      return false;
+  }
+  if (!MakeTmaBf16(s->w_head, s->V, s->Ep, s->Ep, 128, &wm[4 * s->L])) return false;
+  std::vector<LoopLayer> ly(s->L);
+  for (int l = 0; l < s->L; l++) {
+    const Layer& Ly = s->layers[l];
+    ly[l] = LoopLayer{Ly.qkv_c1, Ly.qkv_c2, Ly.up_c1, Ly.up_c2, Ly.b_fc, Ly.b_proj};
+  }
+  if (DevAlloc(s, &s->d_loop_wmaps, wm.size()) != SHAHD_OK || DevAlloc(s, &s->d_loop_layers, ly.size()) != SHAHD_OK)
+    return false;
+  if (cudaMemcpy(s->d_loop_wmaps, wm.data(), sizeof(CUtensorMap) * wm.size(), cudaMemcpyHostToDevice) != cudaSuccess ||
+      cudaMemcpy(s->d_loop_layers, ly.data(), sizeof(LoopLayer) * ly.size(), cudaMemcpyHostToDevice) != cudaSuccess)
+    return false;
+  s->loop_max_clusters = nclusters;
+  s->loop_state = 1;
+  return true;
+}
+
+// Rows per cluster for n rows: spread them over the clusters that are resident at once (more clusters only
+// queue behind the first wave), at most kLoopRows each.
+int LoopRows(const ShahdSession* s, int n) {
+  const int clusters = std::max(1, std::min(s->loop_max_clusters, n));
+  return std::min(kLoopRows, CeilDiv(n, clusters));
+}
+
+// Algorithmic bytes of `steps` decode steps of n rows whose cached lengths before the first step are `len`:
+// every weight matrix once per step, each row's cached K/V rows read and its new K/V row written.
+double LoopBytes(const ShahdSession* s, const std::vector<int>& len, int n, int steps) {
+  const double w = 2.0 * ((double)s->L * ((double)s->Nqkv * s->E + (double)s->E * s->H * s->d + (double)s->Nup * s->E +
+                                          (double)s->E * s->F) + (double)s->V * s->E);
+  const double per_pos = (double)s->L * s->Hk * 2 * s->d * 2;
+  double kv = 0;
+  for (int i = 0; i < n; i++)
+    for (int k = 0; k < steps; k++) kv += per_pos * (len[i] + k + 1) + per_pos;
+  return w * steps + kv;
+}
+
+// Launches the decode loop for `steps` greedy steps of rows 0..n-1 (slots d_slot, inputs d_tok); the ids of
+// step k land in out[:, gen0 + k]. logits (nullable, device [n, steps, V]) records every step's logits.
+int LaunchLoop(ShahdSession* s, int n, int steps, int* d_out, int out_ld, int gen0, float* logits) {
+  const int rows = LoopRows(s, n);
+  LoopDesc D{};
+  const size_t smem = LoopPlan(s, rows, &D);
+  D.M = n; D.E = s->E; D.Ep = s->Ep; D.H = s->H; D.Hk = s->Hk; D.d = s->d; D.G = s->G; D.F = s->F; D.Fp = s->Fp;
+  D.V = s->V; D.L = s->L; D.HDp = s->HDp; D.Nqkv = s->Nqkv; D.Nup = s->Nup;
+  D.norm = s->cfg.norm_kind == 1 ? kNormRms : kNormLayer;
+  D.mlp_kind = s->cfg.mlp_kind;
+  D.rows = rows;
+  D.steps = steps;
+  D.gen0 = gen0;
+  D.out_ld = out_ld;
+  D.eps = (float)s->cfg.layer_norm_eps;
+  D.scale = (float)(1.0 / std::sqrt((double)s->d));
+  D.slot = s->d_slot; D.tok = s->d_tok; D.seq_len = s->d_seq_len; D.out_ids = d_out; D.gen_count = s->d_gen_count;
+  D.logits = logits;
+  D.wte = s->wte; D.wpe = s->wpe; D.rope_cos = s->rope_cos; D.rope_sin = s->rope_sin;
+  D.head_bias = s->head_bias; D.head_c1 = s->head_c1; D.head_c2 = s->head_c2;
+  D.kv = KvView{s->kv_pool, s->d_block_table, s->max_blocks, s->Hk, s->d, s->page_elems};
+  D.layers = s->d_loop_layers;
+  D.wmaps = s->d_loop_wmaps;
+  D.trace = nullptr;
+  D.trace_steps = 0;
+  if (std::getenv("SHAHD_LOOP_TRACE") != nullptr) {
+    D.trace_steps = std::min(steps, 8);
+    const size_t nt = (size_t)D.trace_steps * (s->L + 1) * kLoopMarks;
+    if (s->loop_trace_cap < nt) {
+      SHAHD_TRY(DevAlloc(s, &s->d_loop_trace, nt));
+      s->loop_trace_cap = nt;
+    }
+    SHAHD_CUDA_TRY(cudaMemsetAsync(s->d_loop_trace, 0, nt * 8, s->stream));
+    D.trace = s->d_loop_trace;
+  }
+  const LoopKernelFn fn = LoopKernelFor(s->d, s->G);
+  const int clusters = CeilDiv(n, rows);
+  cudaError_t err = cudaSuccess;
+  std::vector<int> len(n);
+  for (int i = 0; i < n; i++) len[i] = s->h_len[i];
+  Timed(s, s->stream, kProfLoop, LoopBytes(s, len, n, steps), [&] {
+    cudaLaunchConfig_t lc = {};
+    lc.gridDim = dim3(clusters * kLoopCS);
+    lc.blockDim = dim3(kLoopThreads);
+    lc.dynamicSmemBytes = smem;
+    lc.stream = s->stream;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeClusterDimension;
+    at[0].val.clusterDim.x = kLoopCS;
+    at[0].val.clusterDim.y = 1;
+    at[0].val.clusterDim.z = 1;
+    lc.attrs = at;
+    lc.numAttrs = 1;
+    err = cudaLaunchKernelEx(&lc, fn, D);
+  });
+  if (err != cudaSuccess) {
+    SetError("decode loop launch failed: %s", cudaGetErrorString(err));
+    return SHAHD_ECUDA;
+  }
+  if (D.trace) {  // diagnostics: per-phase timestamps of the first steps, appended to SHAHD_LOOP_TRACE
+    const size_t nt = (size_t)D.trace_steps * (s->L + 1) * kLoopMarks;
+    std::vector<unsigned long long> h(nt);
+    SHAHD_CUDA_TRY(cudaMemcpyAsync(h.data(), D.trace, nt * 8, cudaMemcpyDeviceToHost, s->stream));
+    SHAHD_CUDA_TRY(cudaStreamSynchronize(s->stream));
+    if (FILE* f = std::fopen(std::getenv("SHAHD_LOOP_TRACE"), "a")) {
+      std::fprintf(f, "# rows %d rows_per_cluster %d clusters %d stages %d steps %d layers %d\n", n, rows,
+                   CeilDiv(n, rows), D.stages, steps, s->L);
+      for (size_t i = 0; i < nt; i += kLoopMarks) {
+        std::fprintf(f, "%zu %zu", i / kLoopMarks / (s->L + 1), (i / kLoopMarks) % (s->L + 1));
+        for (int k = 0; k < kLoopMarks; k++) std::fprintf(f, " %llu", h[i + k]);
+        std::fprintf(f, "\n");
+      }
+      std::fclose(f);
+    }
+  }
+  return SHAHD_OK;
+}
+
+// Whether a generate call runs its decode steps in the persistent loop.
+bool UseLoop(ShahdSession* s, int n, const ShahdSampling* o) {
+  return g_persistent_step && !(o && o->temperature > 0) && n >= 1 && n <= s->max_seqs && LoopSetup(s);
+}
+
 // Core of shahd_generate / shahd_generate_device on the session stream. d_prompt_packed holds the packed
 // prompts on the device; offs their host offsets. Output ids land in d_out [n, max_new].
 int GenerateCore(ShahdSession* s, const int* d_prompt_packed, const std::vector<int>& offs, int n, int max_new,
-                 const ShahdSampling* o, int* d_out) {
+                 const ShahdSampling* o, int* d_out, float* d_logits = nullptr) {
   const bool sample = o && o->temperature > 0;
   const int C = s->C;
   // CachedDecoder constructor: Context = prompt.slice(-BlockSize); prefill all but its last id.
@@ -1020,8 +1126,14 @@ int GenerateCore(ShahdSession* s, const int* d_prompt_packed, const std::vector<
   SHAHD_TRY(PrefillBatched(s, d_prompt_packed, slots, pstart, plen));
   GatherLastTokens<<<CeilDiv(n, 128), 128, 0, s->stream>>>(d_prompt_packed, s->d_ends, n, s->d_tok);
   s->launches++;
-  // the decode loop: step k consumes the last context id (k = 0) or the id sampled at k-1. Rows are split
-  // into concurrent chains (independent sequences) so several latency-bound kernel chains share the GPU.
+  // the decode loop: step k consumes the last context id (k = 0) or the id sampled at k-1. Greedy runs of
+  // supported shapes go through the persistent cluster loop; otherwise rows are split into chains of
+  // per-kernel steps (independent sequences on their own streams).
+  const bool loop = UseLoop(s, n, o);
+  if (d_logits && !loop) {
+    SetError("logits recording needs a greedy run of a model the decode loop supports");
+    return SHAHD_EINVAL;
+  }
   const int nchain = DecodeChains(n);
   StepPlan plans[kMaxChains];
   int r0[kMaxChains];
@@ -1061,9 +1173,16 @@ int GenerateCore(ShahdSession* s, const int* d_prompt_packed, const std::vector<
       plans[c].attended = 0;
       for (int i = r0[c]; i < r0[c] + plans[c].M; i++) plans[c].attended += s->h_len[i] + 1;
     }
-    // consecutive steps that need no window rebuild go into one graph
     int maxlen = 0;
     for (int i = 0; i < n; i++) maxlen = std::max(maxlen, s->h_len[i]);
+    if (loop) {  // every step until the next window rebuild (or the end) in one persistent launch
+      const int steps = std::max(1, std::min(max_new - k, C - maxlen));
+      SHAHD_TRY(LaunchLoop(s, n, steps, d_out, max_new, k, d_logits));
+      for (int i = 0; i < n; i++) s->h_len[i] += steps;
+      k += steps - 1;
+      continue;
+    }
+    // consecutive steps that need no window rebuild go into one graph
     const int reps = std::max(1, std::min({kStepsPerGraph, max_new - k, C - maxlen}));
     SHAHD_TRY(RunStep(s, plans, r0, nchain, 1, reps));
     for (int c = 0; c < nchain; c++) plans[c].embed_ready = EmbedsNext(plans[c]);  // next input embedded
@@ -1278,12 +1397,18 @@ extern "C" int shahd_session_create(const ShahdModelCfg* cfg, const void* params
   cudaMemset(s->xb, 0, sizeof(bf16) * RC * s->Ep);
   cudaMemset(s->ctxb, 0, sizeof(bf16) * RC * s->HDp);
   cudaMemset(s->actb, 0, sizeof(bf16) * RC * s->Fp);
-  cudaFuncSetAttribute(AttnDecodeKernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, AttnSmemBytes(32));
-  cudaFuncSetAttribute(AttnDecodeKernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, AttnSmemBytes(64));
-  cudaFuncSetAttribute(AttnDecodeKernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, AttnSmemBytes(128));
-  cudaFuncSetAttribute(PrefillAttnKernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, PrefillAttnSmem(32));
-  cudaFuncSetAttribute(PrefillAttnKernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, PrefillAttnSmem(64));
-  cudaFuncSetAttribute(PrefillAttnKernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, PrefillAttnSmem(128));
+  // per-device kernel attributes (a process may hold sessions on several devices)
+  TakeLaunchError(nullptr);
+  if (!EnsureKernelAttrs((const void*)AttnDecodeKernel<32>, AttnSmemBytes(32)) ||
+      !EnsureKernelAttrs((const void*)AttnDecodeKernel<64>, AttnSmemBytes(64)) ||
+      !EnsureKernelAttrs((const void*)AttnDecodeKernel<128>, AttnSmemBytes(128)) ||
+      !EnsureKernelAttrs((const void*)PrefillAttnKernel<32>, PrefillAttnSmem(32)) ||
+      !EnsureKernelAttrs((const void*)PrefillAttnKernel<64>, PrefillAttnSmem(64)) ||
+      !EnsureKernelAttrs((const void*)PrefillAttnKernel<128>, PrefillAttnSmem(128))) {
+    TakeLaunchError(nullptr);
+    SetError("shahd_session_create: kernel attributes could not be set on device %d", s->device);
+    return fail(SHAHD_ECUDA);
+  }
   cudaMemset(s->attn_counter, 0, sizeof(int) * (size_t)R * s->Hk);
   cudaMemset(s->d_seq_len, 0, sizeof(int) * R);
   if (cudaDeviceSynchronize() != cudaSuccess) {
@@ -1302,7 +1427,11 @@ extern "C" int shahd_session_destroy(ShahdSession* s) {
     if (kv.second.exec) cudaGraphExecDestroy(kv.second.exec);
   for (cudaEvent_t e : s->ev_pool) cudaEventDestroy(e);
   for (cudaEvent_t e : s->graph_events) cudaEventDestroy(e);
-  for (void* p : s->allocs) cudaFree(p);
+  for (void* p : s->allocs) {
+    auto it = s->alloc_bytes.find(p);
+    ForgetTmaRange(p, static_cast<char*>(p) + (it != s->alloc_bytes.end() ? it->second : 1));  // maps into it go stale
+    cudaFree(p);
+  }
   if (s->h_block_table) cudaFreeHost(s->h_block_table);
   if (s->h_pinned_rows) cudaFreeHost(s->h_pinned_rows);
   for (int c = 0; c < kMaxChains - 1; c++) {
@@ -1534,6 +1663,47 @@ extern "C" int shahd_generate_device(ShahdSession* s, const int32_t* d_prompts, 
   }
   JoinOut(s, caller);
   return rc;
+}
+
+extern "C" int shahd_generate_logits(ShahdSession* s, const int32_t* prompts, const int32_t* offsets, int32_t n,
+                                     int32_t max_new, int32_t* out_ids, float* logits) {
+  ClearError();
+  if (!s || !prompts || !offsets || (max_new > 0 && (!out_ids || !logits))) {
+    SetError("shahd_generate_logits: null argument");
+    return SHAHD_EINVAL;
+  }
+  std::lock_guard<std::mutex> g(s->mu);
+  cudaSetDevice(s->device);
+  SHAHD_TRY(ValidateGenerate(s, offsets, n, max_new));
+  const size_t total = offsets[n];
+  SHAHD_TRY(ValidateIds(s, prompts, total, "CachedGenerate"));
+  if (max_new == 0) return SHAHD_OK;
+  if (!UseLoop(s, n, nullptr)) {
+    SetError("shahd_generate_logits: needs the persistent decode loop (enabled, and a model it supports)");
+    return SHAHD_EINVAL;
+  }
+  std::vector<int> offs(offsets, offsets + n + 1);
+  SHAHD_CUDA_TRY(cudaStreamSynchronize(s->stream));
+  SHAHD_TRY(GrowPrompt(s, total));
+  SHAHD_TRY(GrowOut(s, (size_t)n * max_new));
+  const size_t nl = (size_t)n * max_new * s->V;
+  if (nl > s->loop_logits_cap) {
+    if (s->d_loop_logits) {
+      cudaFree(s->d_loop_logits);
+      s->allocs.erase(std::find(s->allocs.begin(), s->allocs.end(), (void*)s->d_loop_logits));
+      s->alloc_bytes.erase((void*)s->d_loop_logits);
+      s->d_loop_logits = nullptr;
+      s->loop_logits_cap = 0;
+    }
+    SHAHD_TRY(DevAlloc(s, &s->d_loop_logits, nl));
+    s->loop_logits_cap = nl;
+  }
+  SHAHD_CUDA_TRY(cudaMemcpyAsync(s->d_prompt, prompts, sizeof(int) * total, cudaMemcpyHostToDevice, s->stream));
+  SHAHD_TRY(GenerateCore(s, s->d_prompt, offs, n, max_new, nullptr, s->d_out, s->d_loop_logits));
+  SHAHD_CUDA_TRY(cudaMemcpyAsync(out_ids, s->d_out, sizeof(int) * (size_t)n * max_new, cudaMemcpyDeviceToHost, s->stream));
+  SHAHD_CUDA_TRY(cudaMemcpyAsync(logits, s->d_loop_logits, sizeof(float) * nl, cudaMemcpyDeviceToHost, s->stream));
+  SHAHD_CUDA_TRY(cudaStreamSynchronize(s->stream));
+  return SHAHD_OK;
 }
 
 extern "C" int shahd_sync(ShahdSession* s) {

@@ -21,7 +21,9 @@ static std::mutex g_noalloc_setup_mu;
 static float* g_noalloc_ptr[64];  // device address of g_noalloc_scratch, looked up once per device
 
 // Looks the array's device address up for the current device (the first call on each device does this;
-// it also makes the runtime load the library's device module on that device if nothing has yet).
+// it also makes the runtime load the library's device module on that device if nothing has yet). The
+// address belongs to the device's primary context, the one the CUDA runtime uses: callers that make some
+// other context current on the device are not supported.
 static float* NoAllocScratch(int dev) {
   std::lock_guard<std::mutex> g(g_noalloc_setup_mu);
   if (g_noalloc_ptr[dev & 63]) return g_noalloc_ptr[dev & 63];
@@ -41,6 +43,7 @@ static size_t RoundUpFloats(size_t n) { return (n + kNoAllocAlignFloats - 1) / k
 extern "C" int ShahdMatMulNTF32NoAlloc(const float* a, const float* bt, float* out, int m, int k, int n, int acc) {
   const char* op = "ShahdMatMulNTF32NoAlloc";
   ClearError();
+  cudaGetLastError();  // a stale error of an earlier runtime call on this thread is not this call's failure
   if (!CheckDims(op, m, k, n)) return SHAHD_EINVAL;
   if (!a || !bt || !out) {
     SetError("%s: null buffer", op);
@@ -71,16 +74,32 @@ extern "C" int ShahdMatMulNTF32NoAlloc(const float* a, const float* bt, float* o
   // serialize behind one another. Nothing in the scratch has to start at zero: A and B are uploaded on
   // every call, C is uploaded when acc != 0 and otherwise fully written by the kernel.
   const cudaStream_t st = cudaStreamPerThread;
-  cudaMemcpyAsync(da, a, (size_t)m * k * sizeof(float), cudaMemcpyHostToDevice, st);
-  cudaMemcpyAsync(db, bt, (size_t)n * k * sizeof(float), cudaMemcpyHostToDevice, st);
-  if (acc) cudaMemcpyAsync(dc, out, no * sizeof(float), cudaMemcpyHostToDevice, st);
-  dim3 grid(CeilDiv(n, kGT), CeilDiv(m, kGT));
-  GemmSimtKernel<float><<<grid, 256, 0, st>>>(da, k, 1, db, 1, k, dc, m, n, k, acc);
-  cudaMemcpyAsync(out, dc, no * sizeof(float), cudaMemcpyDeviceToHost, st);
-  cudaError_t e = cudaStreamSynchronize(st);
-  if (e == cudaSuccess) e = cudaGetLastError();
+  const char* step = "copying A to the device";
+  cudaError_t e = cudaMemcpyAsync(da, a, (size_t)m * k * sizeof(float), cudaMemcpyHostToDevice, st);
+  if (e == cudaSuccess) {
+    step = "copying B to the device";
+    e = cudaMemcpyAsync(db, bt, (size_t)n * k * sizeof(float), cudaMemcpyHostToDevice, st);
+  }
+  if (e == cudaSuccess && acc) {
+    step = "copying C to the device";
+    e = cudaMemcpyAsync(dc, out, no * sizeof(float), cudaMemcpyHostToDevice, st);
+  }
+  if (e == cudaSuccess) {
+    step = "launching the GEMM";
+    dim3 grid(CeilDiv(n, kGT), CeilDiv(m, kGT));
+    GemmSimtKernel<float><<<grid, 256, 0, st>>>(da, k, 1, db, 1, k, dc, m, n, k, acc);
+    e = cudaGetLastError();
+  }
+  if (e == cudaSuccess) {
+    step = "copying C back";
+    e = cudaMemcpyAsync(out, dc, no * sizeof(float), cudaMemcpyDeviceToHost, st);
+  }
+  if (e == cudaSuccess) {
+    step = "waiting for the device";
+    e = cudaStreamSynchronize(st);
+  }
   if (e != cudaSuccess) {
-    SetError("%s: device error: %s", op, cudaGetErrorString(e));
+    SetError("%s: %s failed: %s", op, step, cudaGetErrorString(e));
     return SHAHD_ECUDA;
   }
   return SHAHD_OK;

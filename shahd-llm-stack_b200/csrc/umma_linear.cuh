@@ -106,26 +106,34 @@ inline EncodeTiledFn GetEncodeTiled() {
   return fn;
 }
 
-// Cached per (pointer, shape, box): weights are fixed for a session's lifetime.
-inline bool MakeTmaBf16(const void* base, int rows, int cols, int ld, int box_rows, CUtensorMap* out) {
-  struct Key {
-    const void* p;
-    int r, c, ld, b;
-    bool operator<(const Key& o) const {
-      if (p != o.p) return p < o.p;
-      if (r != o.r) return r < o.r;
-      if (c != o.c) return c < o.c;
-      if (ld != o.ld) return ld < o.ld;
-      return b < o.b;
-    }
-  };
+// Cached per (pointer, shape, box): weights are fixed for a session's lifetime, and a session forgets its own
+// entries when it frees its memory (ForgetTmaRange), so the cache holds only live buffers.
+struct TmaKey {
+  const void* p;
+  int r, c, ld, b;
+  bool operator<(const TmaKey& o) const {
+    if (p != o.p) return p < o.p;
+    if (r != o.r) return r < o.r;
+    if (c != o.c) return c < o.c;
+    if (ld != o.ld) return ld < o.ld;
+    return b < o.b;
+  }
+};
+inline std::mutex& TmaCacheMutex() {
   static std::mutex mu;
-  static std::map<Key, CUtensorMap> cache;
-  Key k{base, rows, cols, ld, box_rows};
+  return mu;
+}
+inline std::map<TmaKey, CUtensorMap>& TmaCache() {
+  static std::map<TmaKey, CUtensorMap> cache;
+  return cache;
+}
+
+inline bool MakeTmaBf16(const void* base, int rows, int cols, int ld, int box_rows, CUtensorMap* out) {
+  const TmaKey k{base, rows, cols, ld, box_rows};
   {
-    std::lock_guard<std::mutex> g(mu);
-    auto it = cache.find(k);
-    if (it != cache.end()) {
+    std::lock_guard<std::mutex> g(TmaCacheMutex());
+    auto it = TmaCache().find(k);
+    if (it != TmaCache().end()) {
       *out = it->second;
       return true;
     }
@@ -141,14 +149,21 @@ inline bool MakeTmaBf16(const void* base, int rows, int cols, int ld, int box_ro
                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return false;
-  std::lock_guard<std::mutex> g(mu);
-  cache[k] = m;
+  std::lock_guard<std::mutex> g(TmaCacheMutex());
+  TmaCache()[k] = m;
   *out = m;
   return true;
 }
 
-// Forget cached descriptors that point into [lo, hi) (a session freeing its weights).
-inline void ForgetTmaRange(const void* lo, const void* hi) { (void)lo; (void)hi; }
+// Forgets the cached descriptors whose base address lies in [lo, hi) (memory that is being freed).
+inline void ForgetTmaRange(const void* lo, const void* hi) {
+  std::lock_guard<std::mutex> g(TmaCacheMutex());
+  auto& c = TmaCache();
+  for (auto it = c.begin(); it != c.end();) {
+    if (it->first.p >= lo && it->first.p < hi) it = c.erase(it);
+    else ++it;
+  }
+}
 
 // ---- device: fused linear over a 128-row tile ---------------------------------------------------------
 
@@ -464,14 +479,11 @@ template <int NORM, class Epi, int BN>
 void LaunchUmmaLinearBN(const LinearArgs& la, const Epi& epi, cudaStream_t st) {
   CUtensorMap tw, ta;
   const int box = UmmaBoxRows(la.M);
-  if (!MakeTmaBf16(la.w, la.N, la.Kp, la.Kp, BN, &tw) || !MakeTmaBf16(la.ab, la.a_rows, la.Kp, la.ldab, box, &ta))
-    return;  // the missing launch surfaces through the caller's result checks
-  static bool configured = false;
-  if (!configured) {
-    cudaFuncSetAttribute(LinearUmmaKernel<NORM, Epi, BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         UmmaSmem<BN>::kBytes);
-    configured = true;
+  if (!MakeTmaBf16(la.w, la.N, la.Kp, la.Kp, BN, &tw) || !MakeTmaBf16(la.ab, la.a_rows, la.Kp, la.ldab, box, &ta)) {
+    NoteLaunchError(cudaErrorInvalidValue, "cuTensorMapEncodeTiled for a projection");  // reported by the caller
+    return;
   }
+  if (!EnsureKernelAttrs((const void*)LinearUmmaKernel<NORM, Epi, BN>, UmmaSmem<BN>::kBytes)) return;
   const int ks = (NORM == kNormNone && la.ws != nullptr) ? UmmaKSplit(la.M, la.N, la.Kp) : 1;
   dim3 grid(CeilDiv(la.N, BN), CeilDiv(la.M, kUmmaBM), ks);
   static_assert(UmmaSmem<BN>::kStages * UmmaSmem<BN>::kStage >= kUmmaBM * BN * 4, "partial tile fits the stages");

@@ -204,6 +204,17 @@ class Session:
             rng_states[...] = st  # SeededRng.SetState: the streams advanced by one draw per sampled token
         return out
 
+    def generate_logits(self, prompts, max_new: int) -> tuple[np.ndarray, np.ndarray]:
+        """Greedy CachedGenerate that also returns every step's logits [n, max_new, vocab] (the logits each
+        new id was chosen from; CachedDecoder.Logits after each push). Needs the persistent decode loop."""
+        flat, offs = _pack(prompts)
+        n = offs.size - 1
+        out = np.zeros((n, max(max_new, 0)), dtype=np.int32)
+        logits = np.zeros((n, max(max_new, 0), self.cfg.vocab_size), dtype=np.float32)
+        _lib.check(self.lib.shahd_generate_logits(self.handle, flat.ctypes.data_as(_ip), offs.ctypes.data_as(_ip), n,
+                                                  max_new, out.ctypes.data_as(_ip), logits.ctypes.data_as(_fp)))
+        return out, logits
+
     def generate_device(self, d_prompts: int, host_offsets: np.ndarray, max_new: int, d_out: int,
                         sampling: Sampling = GREEDY, d_rng: int = 0, stream: int = 0) -> None:
         """Asynchronous CachedGenerate over device buffers (ids already resident in HBM)."""
@@ -226,7 +237,7 @@ class Session:
         _lib.check(self.lib.shahd_profile(self.handle, int(enable)))
 
     PROFILE_KINDS = {"attention": 0, "linear": 1, "other": 2,
-                     "prefill_attention": 3, "prefill_linear": 4, "prefill_other": 5}
+                     "prefill_attention": 3, "prefill_linear": 4, "prefill_other": 5, "decode_loop": 6}
 
     def profile_read(self, kind: str) -> dict:
         ms = ctypes.c_double()

@@ -109,3 +109,53 @@ def test_bf16_tensor_core_matmul_nt(m, k, n):
     err = float((acc.double() - (ref + seed.double())).abs().max()) / rng
     assert err < 1e-4, err
     assert pkg._lib.load().ShahdDeviceErrorFlag() == 0
+
+
+# ---- f32 seam on the tensor cores (split-TF32, three tcgen05 kind::tf32 passes) ---------------------
+# The operator-sweep shapes of the MatMulNT config: fp32 A[M,K], B[N,K] ~ N(0,1); M >= 64 takes the
+# tensor cores, M = 1 the CUDA-core kernel. The bar is north_star's 1e-4 of the output range for TF32/fp32
+# and FfiGuard's 1e-4 scaled error (Tests/FfiGuard.Test.ts:146-200). Reference: an f64 product of the
+# same f32 inputs (numpy's f64 matmul for the large shapes: the oracle's f64 dot product, only faster).
+
+SWEEP_NK = [(768, 256), (1024, 256), (256, 1024), (4096, 256), (4096, 1024)]
+
+
+@pytest.mark.parametrize("m", [1, 64, 1024])
+@pytest.mark.parametrize("n,k", SWEEP_NK)
+def test_f32_matmul_nt_sweep_shapes(gpu, m, n, k):
+    rng = np.random.default_rng(2)
+    a = rng.standard_normal((m, k), dtype=np.float32)
+    bt = rng.standard_normal((n, k), dtype=np.float32)
+    want = a.astype(np.float64) @ bt.astype(np.float64).T
+    out = np.full(m * n, 7, np.float32)
+    gpu.MatMulNtInto(a.ravel(), bt.ravel(), out, m, k, n)
+    rng_w = float(want.max() - want.min())
+    assert float(np.abs(out.reshape(m, n) - want).max()) / rng_w < 1e-4
+    assert scaled(out, want.ravel()) < 1e-4
+    seed = rng.standard_normal(m * n).astype(np.float32)
+    acc = seed.copy()
+    gpu.MatMulNtAcc(a.ravel(), bt.ravel(), acc, m, k, n)
+    assert scaled(acc, want.ravel() + seed) < 1e-4
+
+
+def test_f32_matmul_nt_largest_sweep_shape(gpu):
+    m, n, k = 8192, 4096, 1024
+    rng = np.random.default_rng(2)
+    a = rng.standard_normal((m, k), dtype=np.float32)
+    bt = rng.standard_normal((n, k), dtype=np.float32)
+    out = np.empty(m * n, np.float32)
+    gpu.MatMulNtInto(a.ravel(), bt.ravel(), out, m, k, n)
+    want = a.astype(np.float64) @ bt.astype(np.float64).T
+    assert float(np.abs(out.reshape(m, n) - want).max()) / float(want.max() - want.min()) < 1e-4
+
+
+@pytest.mark.parametrize("m,k,n", [(64, 256, 768), (300, 100, 130), (1024, 1024, 256)])
+def test_f32_matmul_nn_on_tensor_cores(gpu, m, k, n):
+    rng = np.random.default_rng(4)
+    a = rng.standard_normal((m, k), dtype=np.float32)
+    b = rng.standard_normal((k, n), dtype=np.float32)
+    out = np.full(m * n, 7, np.float32)
+    gpu.MatMulInto(a.ravel(), b.ravel(), out, m, k, n)
+    want = (a.astype(np.float64) @ b.astype(np.float64)).ravel()
+    assert scaled(out, want) < 1e-4
+    assert pkg._lib.load().ShahdDeviceErrorFlag() == 0

@@ -79,17 +79,42 @@ def test_known_answer_and_limit():
     assert _noalloc(lib, a, bt, out[:4], 0, 3, 2, 0) == pkg._lib.SHAHD_EINVAL
 
 
+def _cudart():
+    """The CUDA runtime library of the toolkit (cudaMemGetInfo), without importing torch."""
+    import ctypes.util
+    import glob
+    import os
+
+    cands = [ctypes.util.find_library("cudart")]
+    home = os.environ.get("CUDA_HOME", "/usr/local/cuda")
+    cands += sorted(glob.glob(os.path.join(home, "lib64", "libcudart.so*")))
+    for c in cands:
+        if c:
+            try:
+                return ctypes.CDLL(c)
+            except OSError:
+                continue
+    pytest.fail("no CUDA runtime library found for cudaMemGetInfo")
+
+
+def _free_bytes(rt) -> int:
+    free, total = ctypes.c_size_t(), ctypes.c_size_t()
+    assert rt.cudaDeviceSynchronize() == 0
+    assert rt.cudaMemGetInfo(ctypes.byref(free), ctypes.byref(total)) == 0
+    return free.value
+
+
 def test_free_device_memory_unchanged():
-    torch = pytest.importorskip("torch")
+    # the entry point's whole promise: no cudaMalloc/cudaFree, however large the calls get (up to the limit)
+    rt = _cudart()
     lib = pkg.load()
     rng = np.random.default_rng(5)
     a, bt, seed = _case(rng, 64, 64, 64)
     out = seed.copy()
     assert _noalloc(lib, a, bt, out, 64, 64, 64, 0) == pkg._lib.SHAHD_OK  # set-up done by now
-    torch.cuda.synchronize()
-    free0 = torch.cuda.mem_get_info()[0]
+    free0 = _free_bytes(rt)
     for m, k, n in ((1024, 1024, 1024), (5, 900, 777), (64, 64, 64)):
         a, bt, seed = _case(rng, m, k, n)
         out = seed.copy()
         assert _noalloc(lib, a, bt, out, m, k, n, 1) == pkg._lib.SHAHD_OK, lib.ShahdLastError()
-    assert torch.cuda.mem_get_info()[0] == free0
+        assert _free_bytes(rt) == free0, (m, k, n)
