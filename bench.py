@@ -361,9 +361,10 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
         dist.all_reduce(te, op=dist.ReduceOp.MAX)
     e2e_value = tokens_per_step_all / (float(te.item()) / len(e2e_ms) / 1000.0)
 
-    # live per-kernel-class timing (CUDA events on the launching stream) over one extra job. The decode
-    # steps of a greedy job run in ONE launch of the persistent decode loop, so the events around it perturb
-    # nothing; prefill launches are bracketed one by one and reported apart.
+    # per-kernel-class shares over one extra job with CUDA events on the session stream around every launch.
+    # Event nodes inside a replayed graph add time and break the programmatic overlap, so the bracketed run
+    # gives only each class's SHARE of the job; a class's time is that share of the unbracketed ms_per_step
+    # (the decode loop, when it runs, is one launch per run of steps and is timed directly).
     sess.profile(True)
     flush.zero_()
     step()
@@ -383,24 +384,30 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
     if os.path.exists(tpath):
         with open(tpath) as f:
             traffic_ratio = json.load(f)
+    bracketed_ms = sum(v["ms"] for v in prof.values())
+    scale = ms_per_step / bracketed_ms if bracketed_ms > 0 else 0.0
     if prof["decode_loop"]["launches"] > 0:
-        dom, kernel = "decode_loop", "DecodeLoopKernel"
-    else:  # per-kernel decode steps (a model the loop does not take): the projection class dominates
+        dom, kernel, scale = "decode_loop", "DecodeLoopKernel", 1.0
+    else:  # per-kernel decode steps: the larger of the projection and decode-attention classes
         dom = max(("attention", "linear"), key=lambda k: prof[k]["ms"])
-        kernel = {"attention": "decode attention kernels", "linear": "projection kernels"}[dom]
+        kernel = {"attention": "decode attention kernels", "linear": "decode projection kernels"}[dom]
     p = prof[dom]
     nl = max(p["launches"], 1)
-    achieved = p["bytes"] / (p["ms"] / 1000.0) / 1e9 if p["ms"] > 0 else 0.0
+    class_ms = p["ms"] * scale
+    achieved = p["bytes"] / (class_ms / 1000.0) / 1e9 if class_ms > 0 else 0.0
     traffic = traffic_ratio[dom] * p["bytes"] / nl if traffic_ratio.get(dom) else None
     roofline = {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
                 "frac": achieved / peaks["hbm_gbs"], "traffic": traffic, "kernel": kernel, "peak_source": peak_kind,
-                "launches_per_job": p["launches"], "avg_launch_ms": p["ms"] / nl,
+                "launches_per_job": p["launches"], "avg_launch_ms": class_ms / nl,
                 "algorithmic_bytes_per_launch": p["bytes"] / nl,
-                "share_of_step": p["ms"] / ms_per_step,
-                "timing": "CUDA events on the session stream around each launch (one launch per run of decode steps)",
+                "share_of_step": class_ms / ms_per_step,
+                "timing": ("one CUDA-event-timed launch per run of decode steps" if dom == "decode_loop" else
+                           "the class's share of a job with CUDA events around every launch, times the unbracketed "
+                           "ms_per_step"),
                 "bytes": "per decode step: every weight matrix once (bf16) + each row's cached K/V rows read and its new "
                          "K/V row written (bf16); prefill not included"}
-    classes = {k: {"ms_per_job": v["ms"], "launches": v["launches"], "algorithmic_bytes": v["bytes"]}
+    classes = {k: {"share": v["ms"] / bracketed_ms if bracketed_ms > 0 else None, "ms_per_job": v["ms"] * scale,
+                   "bracketed_ms_per_job": v["ms"], "launches": v["launches"], "algorithmic_bytes": v["bytes"]}
                for k, v in prof.items() if v["launches"] > 0}
     expected = None
     gpath = os.path.join(ROOT, "tests", "golden", "microchat_job.json")
@@ -441,13 +448,84 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
     print(json.dumps(line), flush=True)
 
 
+SWEEP_M = (1, 64, 1024, 8192)
+SWEEP_NK = ((768, 256), (1024, 256), (256, 1024), (4096, 256), (4096, 1024))
+
+
+def run_matmul_sweep(args, rank: int) -> None:
+    """The MatMulNT operator sweep (C = A·Bᵀ, A[M,K], B[N,K] ~ N(0,1), seed 2) on the two tensor-core GEMMs of
+    the library with operands resident in HBM: bf16 (ShahdMatMulNTBF16Device) and fp32 through split-TF32
+    (ShahdMatMulNTF32Device, three kind::tf32 passes). Each call timed alone with CUDA events after an L2 flush;
+    median of --steps calls after --warmup untimed ones. One JSON line, the per-shape figures in `shapes`."""
+    import torch
+
+    if rank != 0:
+        return
+    pkg = package()
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    peaks, peak_kind = load_peaks()
+    flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    g = torch.Generator(device="cpu").manual_seed(2)
+    shapes = []
+    launches = 0
+    for n, k in SWEEP_NK:
+        bt32 = torch.randn(n, k, generator=g).to(dev)
+        bt16 = bt32.to(torch.bfloat16)
+        for m in SWEEP_M:
+            a32 = torch.randn(m, k, generator=g).to(dev)
+            a16 = a32.to(torch.bfloat16)
+            out = torch.empty(m, n, device=dev)
+            res = {"M": m, "N": n, "K": k}
+            for name, call in (
+                ("bf16", lambda: pkg.backend.matmul_nt_bf16_device(a16.data_ptr(), bt16.data_ptr(), out.data_ptr(), m, k, n,
+                                                                   stream=stream.cuda_stream)),
+                ("tf32x3", lambda: pkg.backend.matmul_nt_f32_device(a32.data_ptr(), bt32.data_ptr(), out.data_ptr(), m, k,
+                                                                    n, stream=stream.cuda_stream))):
+                for _ in range(args.warmup):
+                    call()
+                # every timed call sits behind its own L2 flush on the stream, enqueued without waiting, so the
+                # events measure the device and not the host's enqueue latency
+                evs = []
+                for _ in range(args.steps):
+                    flush.zero_()
+                    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                    e0.record(stream)
+                    call()
+                    e1.record(stream)
+                    evs.append((e0, e1))
+                torch.cuda.synchronize(dev)
+                times = [a.elapsed_time(b) for a, b in evs]
+                launches += args.steps * (1 if name == "bf16" else 3)
+                ms = statistics.median(times)
+                tflops = 2.0 * m * n * k / (ms / 1000.0) / 1e12
+                res[name] = {"ms": ms, "tflops": tflops}
+            res["bf16"]["frac_of_bf16_peak"] = res["bf16"]["tflops"] / peaks["bf16_tflops"]
+            # three kind::tf32 passes, each at half the bf16 tensor rate
+            res["tf32x3"]["frac_of_tf32_pipe"] = 3 * res["tf32x3"]["tflops"] / (peaks["bf16_tflops"] / 2)
+            shapes.append(res)
+    big = [r for r in shapes if r["M"] >= 1024]
+    value = statistics.mean(r["bf16"]["tflops"] for r in big)
+    line = {"metric": "MatMulNT operator sweep TFLOP/s (bf16 tcgen05, M >= 1024 mean)", "value": value,
+            "unit": "TFLOP/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": statistics.mean(r["bf16"]["ms"] for r in big), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": "MatMulNT sweep M in {1,64,1024,8192} x (N,K) in 5 shapes, N(0,1) seed 2",
+                       "l2": "flushed (512 MiB write) before every timed call"},
+            "roofline": {"bound": "tensor", "achieved": value, "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
+                         "frac": value / peaks["bf16_tflops"], "traffic": None, "peak_source": peak_kind},
+            "gpu_launches": launches, "shapes": shapes}
+    print(json.dumps(line), flush=True)
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", default="microchat", choices=sorted(WORKLOADS))
+    ap.add_argument("--workload", default="microchat", choices=sorted(WORKLOADS) + ["matmul_sweep"])
     ap.add_argument("--no-extras", action="store_true",
                     help="time the steps only (no e2e, profile or CPU legs): the profiling command line")
     ap.add_argument("--chains", type=int, default=0, help="concurrent decode chains (0 = library default)")
@@ -460,7 +538,13 @@ def main() -> None:
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     if args.warmup < 3:
         args.warmup = 3
-    if args.impl == "reference":
+    if args.workload == "matmul_sweep":
+        if args.impl == "reference":
+            print(json.dumps({"impl": "reference", "unavailable": "the MatMulNT sweep has no reference arm here; the "
+                              "decode workloads carry it"}), flush=True)
+        else:
+            run_matmul_sweep(args, rank)
+    elif args.impl == "reference":
         run_reference(args, rank, world)
     else:
         run_ours(args, rank, world, local_rank)

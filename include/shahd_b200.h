@@ -41,7 +41,10 @@ void MatMulF64(const double* a, const double* b, double* out, int m, int k, int 
 void MatMulNTF64(const double* a, const double* bt, double* out, int m, int k, int n, int acc);
 /* db[K,N] (+)= aᵀ @ dout, a [M,K], dout [M,N].                   replaces MatMulTNF64, matmul.go:252-289 */
 void MatMulTNF64(const double* a, const double* dout, double* db, int m, int k, int n, int acc);
-/* f32 twins (fp32 FMA accumulation on the GPU).                  replace matmul.go:329-395 */
+/* f32 twins.                                                     replace matmul.go:329-395
+ * MatMulF32 / MatMulNTF32 with M >= 64 run on the tensor cores: operands split into two TF32 parts, three
+ * tcgen05 kind::tf32 passes into fp32 accumulators (within 1e-4 of the output range); smaller M, and every
+ * call while SetScalarKernels(1) is in force, run exact fp32 FMA chains on CUDA cores. MatMulTNF32 is fp32 FMA. */
 void MatMulF32(const float* a, const float* b, float* out, int m, int k, int n);
 void MatMulNTF32(const float* a, const float* bt, float* out, int m, int k, int n, int acc);
 void MatMulTNF32(const float* a, const float* dout, float* db, int m, int k, int n, int acc);
@@ -50,9 +53,9 @@ void SetKernelThreads(int n);
 /* 1 when the fast kernels can run. For this library that means a usable sm_100 device, so the
  * reference selector's probe (BackendSelector.ts:74-93, matmul.go:106-109) keeps working unchanged. */
 int ShahdCpuSupportsAvx2Fma(void);
-/* Test hook with the meaning of matmul.go:111-118: force != 0 makes every decode projection run the
- * CUDA-core (SIMT) kernels whatever the row count, so the tensor-core tiles can be parity-checked
- * against them; 0 restores the row-count rule. Process-wide. */
+/* Test hook with the meaning of matmul.go:111-118: force != 0 makes every decode projection and the f32
+ * seam run the CUDA-core (SIMT) kernels whatever the row count (exact fp32 FMA chains), so the tensor-core
+ * tiles can be parity-checked against them; 0 restores the row-count rule. Process-wide. */
 void SetScalarKernels(int force);
 
 /* ---- additions of this library ---------------------------------------------------------------- */
@@ -72,11 +75,12 @@ void ShahdSetProgrammaticLaunch(int enable);
  * joined in one CUDA graph); 0 = automatic (one chain). Process-wide tuning hook;
  * no counterpart in the reference. Results do not depend on it. */
 void ShahdSetDecodeChains(int chains);
-/* Greedy shahd_generate / shahd_generate_device run every decode step until the next window rebuild (or the
- * end) in ONE persistent launch when the model fits it (default 1): thread-block clusters of 16 CTAs each own up
- * to 16 sequences for all steps (tcgen05 tiles, TMA weight streaming, cluster barriers, no host round trip and
- * no launch per step). 0 runs one CUDA-graph-replayed launch chain per step instead. Results agree within the
- * parity tolerance. Process-wide; no counterpart in the reference. */
+/* 1: greedy shahd_generate / shahd_generate_device (and shahd_generate_logits, which needs it) run every
+ * decode step until the next window rebuild (or the end) in ONE persistent launch when the model fits it:
+ * thread-block clusters of 16 CTAs each own up to 16 sequences for all steps (tcgen05 tiles, TMA weight
+ * streaming, cluster barriers, no host round trip and no launch per step). 0 (the default, faster at the
+ * shapes measured) runs one CUDA-graph-replayed launch chain per step. Results agree within the parity
+ * tolerance. Process-wide; no counterpart in the reference. */
 void ShahdSetPersistentStep(int enable);
 /* First error code a kernel recorded for a bounded device-side wait that gave up (0 = none). */
 int ShahdDeviceErrorFlag(void);
@@ -85,6 +89,13 @@ int ShahdDeviceErrorFlag(void);
  * pointers 16-byte aligned. stream may be 0. Returns a status code.  (MatMulNtInto/MatMulNtAcc of
  * ComputeBackend.ts:29-36 for device-resident operands.) */
 int ShahdMatMulNTBF16Device(const void* a, const void* bt, float* out, int m, int k, int n, int acc, void* stream);
+/* Device-pointer MatMulNT with fp32 operands on the tensor cores: out[M,N] (+)= a[M,K] @ btᵀ, a, bt, out fp32
+ * row-major on the device; the operands are split into two TF32 parts (in a per-device workspace) and
+ * multiplied in three tcgen05 kind::tf32 passes with fp32 accumulation (within 1e-4 of the output range).
+ * K must be a multiple of 4 and out 16-byte aligned. Asynchronous on `stream` (0 = the legacy stream); the
+ * workspace is reused by the next call on the device, so calls on one device must not overlap. Returns a
+ * status code.  (MatMulNtInto/MatMulNtAcc of ComputeBackend.ts:29-36 for device-resident f32 operands.) */
+int ShahdMatMulNTF32Device(const float* a, const float* bt, float* out, int m, int k, int n, int acc, void* stream);
 /* MatMulNTF32 that never allocates or frees device memory; no counterpart in the reference.
  * out[M,N] (+)= a[M,K] @ btᵀ with the same kernel and the same results as MatMulNTF32, but the
  * operands are staged in one fixed 16 MiB array per device that is part of the library's device image
@@ -228,6 +239,21 @@ int shahd_profile_read(ShahdSession* s, int32_t kind, double* total_ms, int64_t*
  * written back advanced by one draw each. out_ids [rows]. Synchronous. */
 int shahd_sample_logits(const float* logits, int32_t rows, int32_t vocab, const ShahdSampling* opts,
                         uint32_t* rng_states, int32_t* out_ids);
+
+/* One verification round of stochastic speculative sampling (SpeculativeSample, Brain/Reasoning/
+ * SpeculativeSampling.ts:82-112) for n sequences on the current device, on caller logits (host, f32):
+ * target_logits [n, gamma + 1, vocab] (row k: the target's prediction for proposal k; row g[i]: the bonus
+ * position), draft_logits [n, gamma, vocab] (row k: the draft distribution proposal k was drawn from),
+ * proposals [n, gamma], g [n] proposals this round (0..gamma), budget [n] new ids still allowed (>= 1).
+ * Proposal k is accepted with probability min(1, p/q) (one SeededRng draw each); the first rejection is
+ * replaced by a draw from the normalized max(0, p - q) (from p when that has no mass); all accepted with
+ * budget left draws a bonus id from p. p and q: ProbsFromLogits with opts (temperature > 0 required).
+ * out_ids [n, gamma + 1] receives the appended ids, out_count [n] their number, accepted [n] the accepted
+ * proposals; rng_states [n] are read and written back advanced. Synchronous. */
+int shahd_speculative_round(const float* target_logits, const float* draft_logits, const int32_t* proposals,
+                            const int32_t* g, const int32_t* budget, int32_t n, int32_t gamma, int32_t vocab,
+                            const ShahdSampling* opts, uint32_t* rng_states, int32_t* out_ids, int32_t* out_count,
+                            int32_t* accepted);
 
 const char* shahd_last_error(void);
 

@@ -1114,3 +1114,114 @@ int oracle_check_trajectories(const OracleModel* m, const int32_t* prompts, int 
   free(jobs);
   return rc;
 }
+
+/* ---- stochastic speculative sampling (Brain/Reasoning/SpeculativeSampling.ts) ------------------- */
+
+/* ResidualSample, SpeculativeSampling.ts:23-36: a draw from the normalized max(0, P - Q), or from P when
+ * that residual has no mass. */
+static int ResidualSample(const double* P, const double* Q, int V, uint32_t* rng, double* tmp) {
+  double sum = 0;
+  for (int j = 0; j < V; j++) {
+    const double r = P[j] - Q[j];
+    tmp[j] = r > 0 ? r : 0;
+    if (r > 0) sum += r;
+  }
+  if (sum <= 0) return oracle_sample_from_distribution(P, V, rng);
+  for (int j = 0; j < V; j++) tmp[j] /= sum;
+  return oracle_sample_from_distribution(tmp, V, rng);
+}
+
+/* One verification round (SpeculativeSampling.ts:82-112) on given logits: target rows [g + 1][V] (row i is
+ * the target's prediction for proposal i, row g the bonus position), draft rows [g][V] (row i is the
+ * distribution proposal i was drawn from). Appends the round's ids to out (at most budget of them) and
+ * returns their count; *accepted receives the accepted proposals. One Rng draw per examined proposal, one
+ * more for the residual or bonus sample, in the reference's order. */
+int oracle_speculative_round(const double* target, const double* draft, const int32_t* proposals, int g, int V,
+                             int budget, const OracleSampling* o, uint32_t* rng, int32_t* out, int* accepted) {
+  double* P = (double*)malloc(sizeof(double) * (size_t)V);
+  double* Q = (double*)malloc(sizeof(double) * (size_t)V);
+  double* T = (double*)malloc(sizeof(double) * (size_t)V);
+  int n = 0, acc = 0, corrected = 0;
+  for (int i = 0; i < g; i++) {
+    oracle_probs_from_logits(target + (size_t)i * V, V, o, P);
+    oracle_probs_from_logits(draft + (size_t)i * V, V, o, Q);
+    const int tok = proposals[i];
+    const double ratio = Q[tok] > 0 ? P[tok] / Q[tok] : (P[tok] > 0 ? 1 : 0);
+    if (oracle_rng_next_float(rng) < (ratio < 1 ? ratio : 1)) {
+      out[n++] = tok;
+      acc++;
+      if (n >= budget) break;
+    } else {
+      out[n++] = ResidualSample(P, Q, V, rng, T);
+      corrected = 1;
+      break;
+    }
+  }
+  if (!corrected && n < budget) {
+    oracle_probs_from_logits(target + (size_t)g * V, V, o, P);
+    out[n++] = oracle_sample_from_distribution(P, V, rng);
+  }
+  free(P);
+  free(Q);
+  free(T);
+  *accepted = acc;
+  return n;
+}
+
+/* SpeculativeSample, SpeculativeSampling.ts:38-115: the draft proposes from ForwardLastLogits of its window,
+ * the target scores [ids, proposals].slice(-BlockSize) in one Forward. out_ids receives prompt + max_new ids;
+ * stats (nullable) [target calls, draft tokens, accepted tokens]. */
+int oracle_speculative_sample(const OracleModel* target, const OracleModel* draft, const int32_t* prompt, int n,
+                              int max_new, const OracleSampling* o, uint32_t* rng, int gamma, int32_t* out_ids,
+                              int32_t* stats) {
+  if (n <= 0) return Fail("SpeculativeSample: empty prompt");
+  const int V = target->V, C = target->C, DC = draft->C;
+  int32_t* ids = (int32_t*)malloc(sizeof(int32_t) * (size_t)(n + max_new + gamma + 2));
+  memcpy(ids, prompt, sizeof(int32_t) * (size_t)n);
+  int len = n, calls = 0, dtok = 0, acc_total = 0, rc = 0;
+  double* dl = (double*)malloc(sizeof(double) * (size_t)gamma * V);
+  double* tl = (double*)malloc(sizeof(double) * (size_t)C * V);
+  double* row = (double*)malloc(sizeof(double) * (size_t)V);
+  double* q = (double*)malloc(sizeof(double) * (size_t)V);
+  int32_t* prop = (int32_t*)malloc(sizeof(int32_t) * (size_t)(gamma + 1));
+  int32_t* work = (int32_t*)malloc(sizeof(int32_t) * (size_t)(n + max_new + gamma + 2));
+  while (len - n < max_new && rc == 0) {
+    int G = gamma;
+    if (C - 1 < G) G = C - 1;
+    if (max_new - (len - n) < G) G = max_new - (len - n);
+    if (G <= 0) break;
+    memcpy(work, ids, sizeof(int32_t) * (size_t)len);
+    int wl = len;
+    for (int i = 0; i < G && rc == 0; i++) {
+      const int t = wl < DC ? wl : DC;
+      rc = oracle_forward_last_logits(draft, work + (wl - t), t, row);
+      if (rc) break;
+      memcpy(dl + (size_t)i * V, row, sizeof(double) * (size_t)V);
+      oracle_probs_from_logits(row, V, o, q);
+      prop[i] = oracle_sample_from_distribution(q, V, rng);
+      work[wl++] = prop[i];
+    }
+    if (rc) break;
+    dtok += G;
+    const int ctx_len = len + G < C ? len + G : C;
+    memcpy(work, ids, sizeof(int32_t) * (size_t)len);
+    memcpy(work + len, prop, sizeof(int32_t) * (size_t)G);
+    rc = oracle_forward(target, work + (len + G - ctx_len), ctx_len, tl);
+    if (rc) break;
+    calls++;
+    const int base = ctx_len - G - 1;
+    int acc = 0;
+    const int got = oracle_speculative_round(tl + (size_t)base * V, dl, prop, G, V, max_new - (len - n), o, rng,
+                                             ids + len, &acc);
+    acc_total += acc;
+    len += got;
+  }
+  if (rc == 0) memcpy(out_ids, ids, sizeof(int32_t) * (size_t)(n + max_new));
+  if (stats) {
+    stats[0] = calls;
+    stats[1] = dtok;
+    stats[2] = acc_total;
+  }
+  free(ids); free(dl); free(tl); free(row); free(q); free(prop); free(work);
+  return rc;
+}

@@ -125,6 +125,16 @@ int oracle_check_trajectories(const OracleModel* m, const int32_t* prompts, int 
                               int nnew, double tol, int threads, int32_t* fails, int32_t* first_fail,
                               int32_t* near_ties, double* max_gap);
 
+/* ---- Brain/Reasoning/SpeculativeSampling.ts ---- */
+/* One verification round on given logits (target [g+1][V], draft [g][V]); returns the ids appended. */
+int oracle_speculative_round(const double* target, const double* draft, const int32_t* proposals, int g, int V,
+                             int budget, const OracleSampling* o, uint32_t* rng, int32_t* out, int* accepted);
+/* SpeculativeSample (:38-115): out_ids receives prompt + max_new ids; stats [target calls, draft tokens,
+ * accepted tokens] (nullable). */
+int oracle_speculative_sample(const OracleModel* target, const OracleModel* draft, const int32_t* prompt, int n,
+                              int max_new, const OracleSampling* o, uint32_t* rng, int gamma, int32_t* out_ids,
+                              int32_t* stats);
+
 const char* oracle_last_error(void);
 
 #ifdef __cplusplus

@@ -130,6 +130,10 @@ def lib() -> ctypes.CDLL:
         L.oracle_decoder_cache_length.argtypes = [ctypes.c_void_p]
         L.oracle_decoder_destroy.argtypes = [ctypes.c_void_p]
         L.oracle_set_threads.argtypes = [_i32]
+        L.oracle_speculative_round.argtypes = [_dp, _dp, _ip, _i32, _i32, _i32, ctypes.POINTER(OracleSampling), _up,
+                                               _ip, ctypes.POINTER(ctypes.c_int)]
+        L.oracle_speculative_sample.argtypes = [ctypes.c_void_p, ctypes.c_void_p, _ip, _i32, _i32,
+                                                ctypes.POINTER(OracleSampling), _up, _i32, _ip, _ip]
         L.oracle_check_trajectories.argtypes = [ctypes.c_void_p, _ip, _i32, _i32, _ip, _i32, ctypes.c_double, _i32,
                                                 _ip, _ip, _ip, _dp]
         L.oracle_last_error.restype = ctypes.c_char_p
@@ -426,6 +430,37 @@ def sample_from_logits(logits, rng_state: int, temperature: float, top_k: int = 
     o = sampling(temperature, top_k, top_p)
     idx = lib().oracle_sample_from_logits(_d(lg), lg.size, ctypes.byref(o), _u(st))
     return int(idx), int(st[0])
+
+
+def speculative_round(target_logits, draft_logits, proposals, budget: int, rng_state: int, temperature: float,
+                      top_k: int = 0, top_p: float = 1.0):
+    """One SpeculativeSample verification round on given logits (target [g+1, V], draft [g, V]):
+    returns (ids appended, accepted proposals, the Rng state after the round)."""
+    t = np.ascontiguousarray(target_logits, dtype=np.float64)
+    d = np.ascontiguousarray(draft_logits, dtype=np.float64)
+    prop = np.ascontiguousarray(proposals, dtype=np.int32)
+    g, V = prop.size, t.shape[-1]
+    out = np.zeros(g + 1, dtype=np.int32)
+    st = np.array([rng_state & 0xFFFFFFFF], dtype=np.uint32)
+    acc = ctypes.c_int()
+    o = sampling(temperature, top_k, top_p)
+    n = lib().oracle_speculative_round(_d(t), _d(d), _i(prop), g, V, budget, ctypes.byref(o), _u(st), _i(out),
+                                       ctypes.byref(acc))
+    return out[:n].tolist(), int(acc.value), int(st[0])
+
+
+def speculative_sample(target: "Model", draft: "Model", prompt, max_new: int, rng_state: int, temperature: float,
+                       top_k: int = 0, top_p: float = 1.0, gamma: int = 4):
+    """SpeculativeSample (Brain/Reasoning/SpeculativeSampling.ts:38-115): ids, Rng state, [calls, drafted,
+    accepted]."""
+    prompt = np.ascontiguousarray(prompt, dtype=np.int32)
+    out = np.zeros(prompt.size + max_new, dtype=np.int32)
+    st = np.array([rng_state & 0xFFFFFFFF], dtype=np.uint32)
+    stats = np.zeros(3, dtype=np.int32)
+    o = sampling(temperature, top_k, top_p)
+    _check(lib().oracle_speculative_sample(target.handle, draft.handle, _i(prompt), prompt.size, max_new,
+                                           ctypes.byref(o), _u(st), gamma, _i(out), _i(stats)))
+    return out.tolist(), int(st[0]), stats.tolist()
 
 
 # ---- reference C kernels (oracle/_ref) --------------------------------------------------------

@@ -63,6 +63,7 @@ SIGNATURES = {
     "ShahdSetDecodeChains": (None, [ctypes.c_int]),
     "ShahdSetPersistentStep": (None, [ctypes.c_int]),
     "ShahdMatMulNTBF16Device": (ctypes.c_int, [_vp, _vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, _vp]),
+    "ShahdMatMulNTF32Device": (ctypes.c_int, [_vp, _vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, _vp]),
     "ShahdMatMulNTF32NoAlloc": (ctypes.c_int, [_fp, _fp, _fp, _i32, _i32, _i32, _i32]),
     "shahd_param_count": (_i64, [ctypes.POINTER(ShahdModelCfg)]),
     "shahd_init_params": (ctypes.c_int, [ctypes.POINTER(ShahdModelCfg), _u32, _fp, _i64]),
@@ -84,6 +85,8 @@ SIGNATURES = {
     "shahd_profile": (ctypes.c_int, [_vp, _i32]),
     "shahd_profile_read": (ctypes.c_int, [_vp, _i32, _dp, ctypes.POINTER(_i64), _dp]),
     "shahd_sample_logits": (ctypes.c_int, [_fp, _i32, _i32, ctypes.POINTER(ShahdSampling), _up, _ip]),
+    "shahd_speculative_round": (ctypes.c_int, [_fp, _fp, _ip, _ip, _ip, _i32, _i32, _i32, ctypes.POINTER(ShahdSampling),
+                                                _up, _ip, _ip, _ip]),
     "shahd_last_error": (ctypes.c_char_p, []),
 }
 

@@ -127,3 +127,11 @@ def matmul_nt_bf16_device(a_ptr: int, bt_ptr: int, out_ptr: int, m: int, k: int,
     lib = _lib.load()
     _lib.check(lib.ShahdMatMulNTBF16Device(ctypes.c_void_p(a_ptr), ctypes.c_void_p(bt_ptr), ctypes.c_void_p(out_ptr),
                                            m, k, n, int(acc), ctypes.c_void_p(stream)))
+
+
+def matmul_nt_f32_device(a_ptr: int, bt_ptr: int, out_ptr: int, m: int, k: int, n: int, acc: bool = False,
+                         stream: int = 0) -> None:
+    """out[M,N] (+)= A[M,K] · Btᵀ with fp32 device operands on the tensor cores (split-TF32, three passes)."""
+    lib = _lib.load()
+    _lib.check(lib.ShahdMatMulNTF32Device(ctypes.c_void_p(a_ptr), ctypes.c_void_p(bt_ptr), ctypes.c_void_p(out_ptr),
+                                          m, k, n, int(acc), ctypes.c_void_p(stream)))

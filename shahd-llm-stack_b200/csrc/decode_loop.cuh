@@ -42,25 +42,32 @@ constexpr int kLoopCS = 16;                   // CTAs per cluster (non-portable 
 constexpr int kLoopRows = 16;                 // rows per cluster at most (the MMA's N)
 constexpr int kLoopWarps = 8;
 constexpr int kLoopThreads = 32 * kLoopWarps;
-constexpr int kLoopStageBytes = 128 * 64 * 2;  // one weight k-block: 128 rows x 64 bf16
+constexpr int kLoopBoxBytes = 128 * 64 * 2;    // one weight k-block: 128 rows x 64 bf16 (one TMA box)
+constexpr int kLoopMaxStageBoxes = 4;          // boxes of one ring stage (one barrier, one expect_tx) at most
 constexpr int kLoopOpBlock = kLoopRows * 128;  // one operand k-block: 16 rows x 64 bf16, swizzled
 constexpr int kLoopTmemCols = 512;
 constexpr int kTmQkv = 0, kTmO = 64, kTmUp = 128, kTmDown = 192, kTmHead = 256;
 constexpr int kLoopMaxTiles = 4;   // QKV / up tiles of one CTA, M-tiles of E (64 TMEM columns each region)
 constexpr int kLoopHeadChunk = 16; // head tiles per TMEM chunk (256 columns)
-constexpr int kLoopMaxStages = 12;
+constexpr int kLoopMaxStages = 6;
 
 struct LoopLayer {
   const float *qkv_c1, *qkv_c2, *up_c1, *up_c2, *b_fc, *b_proj;
 };
 
-// Shapes, pointers and the shared-memory plan of one launch (host-computed, passed by value).
+constexpr int kLoopMaxLayers = 16;
+constexpr int kLoopMaxMaps = 4 * kLoopMaxLayers + 1;
+
+// Shapes, pointers, weight tensor maps and the shared-memory plan of one launch (host-computed, passed by
+// value as a __grid_constant__ parameter: the TMA unit reads the descriptors from the parameter bank).
 struct LoopDesc {
+  CUtensorMap wmaps[kLoopMaxMaps];  // qkv, o, up, down of each layer, then the head; box 64 x 128
   int M, E, Ep, H, Hk, d, G, F, Fp, V, L, HDp, Nqkv, Nup;
   int norm, mlp_kind;
   int rows;    // rows per cluster
   int steps;   // decode steps of this launch
-  int stages;  // weight ring depth
+  int stages;       // weight ring depth
+  int stage_boxes;  // weight boxes per ring stage (1, 2 or 4): a phase's boxes are grouped into stages of this
   int gen0, out_ld;
   float eps, scale;
   const int* slot;  // [M]
@@ -72,11 +79,11 @@ struct LoopDesc {
   const float *wte, *wpe, *rope_cos, *rope_sin, *head_bias, *head_c1, *head_c2;
   KvView kv;
   const LoopLayer* layers;   // [L]
-  const CUtensorMap* wmaps;  // [4 L + 1]: qkv, o, up, down of each layer, then the head; box 64 x 128
   // dynamic shared memory plan: byte offsets from the 1024-aligned base
-  int off_xb, off_ctxb, off_actb, off_xf, off_qkv, off_opart, off_dpart, off_xs, off_att, off_sq, off_misc;
+  int off_xb, off_ctxb, off_actb, off_xf, off_qkv, off_opart, off_dpart, off_xs, off_att, off_sq, off_rope, off_misc;
+  int off_sched;  // the CTA's ring stages of one step: [per_step] LoopStage
   int max_items;
-  unsigned long long* trace;  // nullable: per-phase timestamps [trace_steps][L + 1][8] (diagnostics)
+  unsigned long long* trace;  // nullable: per-phase timestamps [trace_steps][L + 1][kLoopMarks] (diagnostics)
   int trace_steps;
 };
 
@@ -87,11 +94,18 @@ __host__ __device__ inline int LoopActKb(int mlp_kind) { return mlp_kind == 0 ? 
 struct LoopSched {
   int nkE, nkG, nE128, akb;
   int nq, no, nu, nh;      // tiles / M-tiles per phase of this CTA
-  int bq, bo, bu, bd, bh;  // weight blocks per phase
-  int per_layer, per_step;
+  int bq, bo, bu, bd, bh;  // weight blocks (boxes) per phase
+  int per_layer, per_step; // ring stages per layer and per step: a phase's boxes in groups of stage_boxes
 };
 
-__device__ __forceinline__ LoopSched MakeSched(const LoopDesc& D, int c, int n_items) {
+// One ring stage of a CTA's static schedule: up to four weight boxes (tensor map, x, y), built once per launch.
+struct LoopStage {
+  int nbox;
+  int map[kLoopMaxStageBoxes], x[kLoopMaxStageBoxes], y[kLoopMaxStageBoxes];
+  int pad[3];
+};
+
+__host__ __device__ inline LoopSched MakeSched(const LoopDesc& D, int c, int n_items) {
   LoopSched S;
   S.nkE = D.Ep / 64;
   S.nkG = CeilDiv(D.G * D.d, 64);
@@ -106,56 +120,21 @@ __device__ __forceinline__ LoopSched MakeSched(const LoopDesc& D, int c, int n_i
   S.bu = S.nu * S.nkE;
   S.bd = S.nu > 0 ? S.nE128 * S.nu * S.akb : 0;
   S.bh = S.nh * S.nkE;
-  S.per_layer = S.bq + S.bo + S.bu + S.bd;
-  S.per_step = D.L * S.per_layer + S.bh;
+  const int g = D.stage_boxes;
+  S.per_layer = CeilDiv(S.bq, g) + CeilDiv(S.bo, g) + CeilDiv(S.bu, g) + CeilDiv(S.bd, g);
+  S.per_step = D.L * S.per_layer + CeilDiv(S.bh, g);
   return S;
-}
-
-// Weight block b of this CTA's static schedule: tensor map index and box coordinates.
-__device__ __forceinline__ void BlockCoords(const LoopDesc& D, const LoopSched& S, int c, int g_item, int b, int& map,
-                                            int& x, int& y) {
-  const int rem = b % S.per_step;
-  if (rem >= D.L * S.per_layer) {  // LM head: tile c + h*CS, k-block kb
-    const int i = rem - D.L * S.per_layer;
-    map = 4 * D.L;
-    x = (i % S.nkE) * 64;
-    y = (c + (i / S.nkE) * kLoopCS) * 128;
-    return;
-  }
-  const int l = rem / S.per_layer;
-  int i = rem % S.per_layer;
-  if (i < S.bq) {
-    map = 4 * l;
-    x = (i % S.nkE) * 64;
-    y = (c + (i / S.nkE) * kLoopCS) * 128;
-    return;
-  }
-  i -= S.bq;
-  if (i < S.bo) {  // Wo rows mt, input columns of this CTA's head group
-    map = 4 * l + 1;
-    x = g_item * D.G * D.d + (i % S.nkG) * 64;
-    y = (i / S.nkG) * 128;
-    return;
-  }
-  i -= S.bo;
-  if (i < S.bu) {
-    map = 4 * l + 2;
-    x = (i % S.nkE) * 64;
-    y = (c + (i / S.nkE) * kLoopCS) * 128;
-    return;
-  }
-  i -= S.bu;  // W_down rows mt, the input columns of up tile u's activations
-  const int per_mt = S.nu * S.akb;
-  const int mt = i / per_mt, u = (i % per_mt) / S.akb, kb2 = i % S.akb;
-  const int t = c + u * kLoopCS;
-  map = 4 * l + 3;
-  x = t * 64 * S.akb + kb2 * 64;
-  y = mt * 128;
 }
 
 // Byte offset of element (row r, column k) of a [16 x K] bf16 operand in 128-byte-swizzled K-major k-blocks.
 __device__ __forceinline__ uint32_t OpOffset(int r, int k) {
   return (uint32_t)((k >> 6) * kLoopOpBlock) + Sw128Offset(r, (k & 63) >> 3) + (uint32_t)((k & 7) * 2);
+}
+
+__device__ __forceinline__ unsigned long long GlobalTimerNs() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
 }
 
 __device__ __forceinline__ bool MbarTestWait(uint64_t* bar, uint32_t parity) {
@@ -202,12 +181,6 @@ __device__ __forceinline__ void LoopBarrier() {
   ClusterSync();
 }
 
-__device__ __forceinline__ unsigned long long GlobalTimerNs() {
-  unsigned long long t;
-  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-  return t;
-}
-
 __device__ __forceinline__ void PrefetchBulkL2(const void* p, uint32_t bytes) {
   asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
 }
@@ -228,6 +201,13 @@ struct LoopMisc {
   int wci[4][kLoopRows];
 };
 
+// Position in a CTA's static schedule of weight k-blocks, advanced by increments: the one thread that walks
+// the schedule would otherwise spend about a microsecond per block on integer divisions.
+struct SchedCursor {
+  int l, ph, t, u, kb;  // layer (or L: the head), phase (0 qkv, 1 o, 2 up, 3 down, 4 head), tile, up tile, k-block
+  int bi;               // box index within the phase
+};
+
 struct LoopCtx {
   const LoopDesc& D;
   LoopSched S;
@@ -238,138 +218,353 @@ struct LoopCtx {
   int total;     // weight blocks of the whole launch
   int cons;      // blocks consumed (thread 0)
   int iss;       // blocks issued (thread 0)
+  int cst;       // ring slot of block `cons`, and the parity of its fill
+  uint32_t cpar;
+  int ist;       // ring slot of block `iss`, and the parity of that slot's current use
+  uint32_t ipar;
+  SchedCursor cur;  // schedule walker (builds the stage table)
+  const LoopStage* sched;  // [per_step] this CTA's ring stages of one step (shared memory)
+  int sidx;                // index in `sched` of stage `iss`
   uint32_t mma_phase;
+  unsigned long long wait_full_ns, wait_mma_ns;  // thread 0's time in weight-stage and MMA waits (tracing)
+  int blocking_topups;
+  unsigned long long issue_ns, topup_ns;  // thread 0's time inside IssuePhase and inside TopUp (tracing)
 };
 
-// Thread 0: issue weight loads while ring slots are free (non-blocking), up to `upto` blocks ahead of use.
-__device__ __forceinline__ void TopUp(LoopCtx& X, bool block_for_next) {
+__device__ __forceinline__ int PhaseTiles(const LoopSched& S, int ph) {
+  return ph == 0 ? S.nq : ph == 1 ? S.no : ph == 2 ? S.nu : ph == 3 ? (S.nu > 0 ? S.nE128 : 0) : S.nh;
+}
+__device__ __forceinline__ int PhaseKb(const LoopSched& S, int ph) {
+  return ph == 0 || ph == 2 || ph == 4 ? S.nkE : ph == 1 ? S.nkG : S.akb;
+}
+// Moves to the first phase with blocks at or after the cursor's phase (wrapping from the head to layer 0).
+__device__ __forceinline__ void SkipEmpty(const LoopSched& S, int L, SchedCursor& k) {
+  for (int guard = 0; guard < 8 * (L + 1) && PhaseTiles(S, k.ph) == 0; guard++) {
+    if (k.ph == 4) { k.ph = 0; k.l = 0; }
+    else if (k.ph == 3) { k.l++; k.ph = k.l == L ? 4 : 0; }
+    else k.ph++;
+  }
+}
+__device__ __forceinline__ int PhaseBoxes(const LoopSched& S, int ph) {
+  return ph == 0 ? S.bq : ph == 1 ? S.bo : ph == 2 ? S.bu : ph == 3 ? S.bd : S.bh;
+}
+__device__ __forceinline__ void Advance(const LoopSched& S, int L, SchedCursor& k) {
+  k.bi++;
+  if (++k.kb < PhaseKb(S, k.ph)) return;
+  k.kb = 0;
+  if (k.ph == 3 && ++k.u < S.nu) return;
+  k.u = 0;
+  if (++k.t < PhaseTiles(S, k.ph)) return;
+  k.t = 0;
+  k.bi = 0;
+  if (k.ph == 4) { k.ph = 0; k.l = 0; }
+  else if (k.ph == 3) { k.l++; k.ph = k.l == L ? 4 : 0; }
+  else k.ph++;
+  SkipEmpty(S, L, k);
+}
+__device__ __forceinline__ void CursorCoords(const LoopDesc& D, const LoopSched& S, int c, int g_item,
+                                             const SchedCursor& k, int& map, int& x, int& y) {
+  switch (k.ph) {
+    case 0: map = 4 * k.l; x = k.kb * 64; y = (c + k.t * kLoopCS) * 128; break;
+    case 1: map = 4 * k.l + 1; x = g_item * D.G * D.d + k.kb * 64; y = k.t * 128; break;
+    case 2: map = 4 * k.l + 2; x = k.kb * 64; y = (c + k.t * kLoopCS) * 128; break;
+    case 3: map = 4 * k.l + 3; x = (c + k.u * kLoopCS) * 64 * S.akb + k.kb * 64; y = k.t * 128; break;
+    default: map = 4 * D.L; x = k.kb * 64; y = (c + k.t * kLoopCS) * 128; break;
+  }
+}
+
+// Thread 0, once per launch: the CTA's ring stages of one step (every step repeats them), each the next
+// boxes of the current phase, at most stage_boxes of them (IssuePhase groups the boxes the same way).
+__device__ __forceinline__ void BuildStageTable(LoopCtx& X, LoopStage* table) {
   const LoopDesc& D = X.D;
+  for (int i = 0; i < X.S.per_step; i++) {
+    LoopStage st{};
+    st.nbox = min(D.stage_boxes, PhaseBoxes(X.S, X.cur.ph) - X.cur.bi);
+    for (int j = 0; j < st.nbox; j++) {
+      CursorCoords(D, X.S, X.c, X.g_item, X.cur, st.map[j], st.x[j], st.y[j]);
+      Advance(X.S, D.L, X.cur);
+    }
+    table[i] = st;
+  }
+}
+
+// Thread 0: fill ring stages while slots are free; with block_for_next, waits (bounded) for the slot of the
+// stage the consumer needs next.
+__device__ __forceinline__ void TopUpBody(LoopCtx& X, bool block_for_next) {
+  const LoopDesc& D = X.D;
+  const uint32_t stage_bytes = (uint32_t)D.stage_boxes * kLoopBoxBytes;
   while (X.iss < X.total && X.iss < X.cons + D.stages && !X.m->abort) {
-    const int st = X.iss % D.stages;
-    const uint32_t ph = ((X.iss / D.stages) & 1) ^ 1;  // the slot's previous use must have been released
-    if (X.iss >= D.stages) {
-      const bool need = block_for_next && X.iss == X.cons;
-      if (need) {
-        if (!MbarWaitBounded(&X.m->empty[st], ph, kWaitLimit)) {
+    if (X.iss >= D.stages) {  // the slot's previous use must have been released by its MMAs
+      if (block_for_next && X.iss == X.cons) {
+        X.blocking_topups++;
+        if (!MbarWaitBounded(&X.m->empty[X.ist], X.ipar ^ 1u, kWaitLimit)) {
           atomicCAS(&g_shahd_device_error, 0, kDevErrLoopTimeout);
           X.m->abort = 1;
           return;
         }
-      } else if (!MbarTestWait(&X.m->empty[st], ph)) {
+      } else if (!MbarTestWait(&X.m->empty[X.ist], X.ipar ^ 1u)) {
         return;
       }
     }
-    int map, x, y;
-    BlockCoords(D, X.S, X.c, X.g_item, X.iss, map, x, y);
-    MbarArriveExpectTx(&X.m->full[st], kLoopStageBytes);
-    TmaLoad2D(X.ring + (size_t)st * kLoopStageBytes, D.wmaps + map, &X.m->full[st], x, y);
+    const LoopStage& st = X.sched[X.sidx];
+    uint64_t* bar = &X.m->full[X.ist];
+    uint8_t* dst = X.ring + (size_t)X.ist * stage_bytes;
+    MbarArriveExpectTx(bar, (uint32_t)(st.nbox * kLoopBoxBytes));
+    for (int j = 0; j < st.nbox; j++) TmaLoad2D(dst + j * kLoopBoxBytes, &D.wmaps[st.map[j]], bar, st.x[j], st.y[j]);
     X.iss++;
+    if (++X.sidx == X.S.per_step) X.sidx = 0;
+    if (++X.ist == D.stages) {
+      X.ist = 0;
+      X.ipar ^= 1u;
+    }
   }
 }
+__device__ __forceinline__ void TopUp(LoopCtx& X, bool block_for_next) {
+  const unsigned long long t0 = X.D.trace ? GlobalTimerNs() : 0;
+  TopUpBody(X, block_for_next);
+  if (X.D.trace) X.topup_ns += GlobalTimerNs() - t0;
+}
 
-// Thread 0: MMAs of `nblk` consecutive schedule blocks into TMEM columns col0 + 16 * (block / per_tile),
-// accumulating over the `per_tile` k-blocks of a tile; `opb(k)` is the operand k-block of schedule block k
-// (relative), `kvalid` the valid K of the last k-block of a tile (64 = full). Commits mma_bar at the end.
-template <class OpAddr>
-__device__ __forceinline__ void IssuePhase(LoopCtx& X, int nblk, int per_tile, uint32_t col0, OpAddr opb, int kvalid_last,
-                                           int tile_of_block_div = 0) {
+// Thread 0: MMAs of the `nblk` boxes of a phase (or of a chunk of whole stages of it); box k accumulates into
+// TMEM columns col0 + 16 * (k / per_tile) with the operand's k-block (k % per_tile) at op_base (2 KB apart).
+// Boxes arrive in ring stages of up to stage_boxes; kvalid_last: valid K of the last k-block of a tile
+// (64 = full). Commits mma_bar at the end.
+__device__ __forceinline__ void IssuePhase(LoopCtx& X, int nblk, int per_tile, uint32_t col0, uint32_t op_base,
+                                           int kvalid_last) {
+  const unsigned long long t_issue = X.D.trace ? GlobalTimerNs() : 0;
   const uint32_t idesc = UmmaIdescBf16(128, 16);
-  for (int k = 0; k < nblk && !X.m->abort; k++) {
+  const uint64_t ring_desc = SmemDescSw128(SmemAddr(X.ring));
+  const uint64_t op_desc = SmemDescSw128(op_base);
+  int kin = 0;
+  uint32_t dcol = X.m->tmem + col0;
+  for (int done = 0; done < nblk && !X.m->abort;) {
+    const int nbox = min(X.D.stage_boxes, nblk - done);
     if (X.iss <= X.cons) TopUp(X, true);
     if (X.m->abort) break;
-    const int st = X.cons % X.D.stages;
-    const uint32_t ph = (X.cons / X.D.stages) & 1;
-    if (!MbarWaitBounded(&X.m->full[st], ph, kWaitLimit)) {
+    const unsigned long long tw = X.D.trace ? GlobalTimerNs() : 0;
+    const bool ok = MbarWaitBounded(&X.m->full[X.cst], X.cpar, kWaitLimit);
+    if (X.D.trace) X.wait_full_ns += GlobalTimerNs() - tw;
+    if (!ok) {
       atomicCAS(&g_shahd_device_error, 0, kDevErrLoopTimeout);
       X.m->abort = 1;
       break;
     }
     TcgenFenceAfter();
-    const int kin = k % per_tile;
-    const int tile = tile_of_block_div > 0 ? k / tile_of_block_div : k / per_tile;
-    const uint64_t ad = SmemDescSw128(SmemAddr(X.ring + (size_t)st * kLoopStageBytes));
-    const uint64_t bd = SmemDescSw128(opb(k));
-    const int kv = (kin == per_tile - 1) ? kvalid_last : 64;
-    for (int kk = 0; kk < kv / 16; kk++)
-      UmmaBf16(X.m->tmem + col0 + 16u * (uint32_t)tile, ad + (uint64_t)(kk * 2), bd + (uint64_t)(kk * 2), idesc,
-               (kin > 0 || kk > 0) ? 1u : 0u);
-    UmmaCommit(&X.m->empty[st]);
+    uint64_t ad = ring_desc + (uint64_t)(X.cst * ((X.D.stage_boxes * kLoopBoxBytes) >> 4));
+    for (int j = 0; j < nbox; j++, ad += (uint64_t)(kLoopBoxBytes >> 4)) {
+      const uint64_t bd = op_desc + (uint64_t)(kin * (kLoopOpBlock >> 4));
+      const int kv = (kin == per_tile - 1) ? kvalid_last : 64;
+      for (int kk = 0; kk < kv / 16; kk++)
+        UmmaBf16(dcol, ad + (uint64_t)(kk * 2), bd + (uint64_t)(kk * 2), idesc, (kin > 0 || kk > 0) ? 1u : 0u);
+      if (++kin == per_tile) {
+        kin = 0;
+        dcol += 16u;
+      }
+    }
+    UmmaCommit(&X.m->empty[X.cst]);
     X.cons++;
+    if (++X.cst == X.D.stages) {
+      X.cst = 0;
+      X.cpar ^= 1u;
+    }
+    done += nbox;
     TopUp(X, false);
   }
   UmmaCommit(&X.m->mma_bar);  // also completes (vacuously) when nothing was issued
+  if (X.D.trace) X.issue_ns += GlobalTimerNs() - t_issue;
 }
 
 // All threads: wait for the phase's MMAs (bounded), then fence for TMEM reads.
 __device__ __forceinline__ void WaitMma(LoopCtx& X) {
   const uint32_t ph = X.mma_phase & 1;
   X.mma_phase++;
-  if (!MbarWaitBounded(&X.m->mma_bar, ph, kWaitLimit)) {
+  const unsigned long long tw = X.D.trace ? GlobalTimerNs() : 0;
+  const bool ok = MbarWaitBounded(&X.m->mma_bar, ph, kWaitLimit);
+  if (X.D.trace) X.wait_mma_ns += GlobalTimerNs() - tw;
+  if (!ok) {
     atomicCAS(&g_shahd_device_error, 0, kDevErrLoopTimeout);
     X.m->abort = 1;
   }
   TcgenFenceAfter();
 }
 
-// Row statistics of the cluster's x rows (NormRow, CachedRowMath.ts:25-56): warp w takes rows w, w + 8.
-__device__ __forceinline__ void RowStats(const LoopDesc& D, const float* xf, LoopMisc* m, int warp, int lane) {
-  for (int r = warp; r < kLoopRows; r += kLoopWarps) {
-    const float* row = xf + (size_t)r * D.E;
-    float s1 = 0.f, s2 = 0.f;
-    for (int k = lane; k < D.E; k += 32) {
-      const float v = row[k];
-      s1 += v;
-      s2 += v * v;
+// Writes one row's norm statistics (NormRow, CachedRowMath.ts:25-56) from its warp-reduced sums.
+__device__ __forceinline__ void RowStatsFromSums(const LoopDesc& D, LoopMisc* m, int r, float s1, float s2, int lane) {
+  s1 = WarpSum(s1);
+  s2 = WarpSum(s2);
+  if (lane == 0) {
+    if (D.norm == kNormRms) {
+      m->mu[r] = 0.f;
+      m->is[r] = 1.0f / sqrtf(s2 / D.E + D.eps);
+    } else {
+      const float mu = s1 / D.E;
+      m->mu[r] = mu;
+      m->is[r] = 1.0f / sqrtf(fmaxf(s2 / D.E - mu * mu, 0.f) + D.eps);
     }
-    s1 = WarpSum(s1);
-    s2 = WarpSum(s2);
-    if (lane == 0) {
-      if (D.norm == kNormRms) {
-        m->mu[r] = 0.f;
-        m->is[r] = 1.0f / sqrtf(s2 / D.E + D.eps);
-      } else {
-        const float mu = s1 / D.E;
-        m->mu[r] = mu;
-        m->is[r] = 1.0f / sqrtf(fmaxf(s2 / D.E - mu * mu, 0.f) + D.eps);
+  }
+}
+
+// Stores 8 consecutive features of row r: fp32 into x, bf16 into the swizzled operand, and adds them to the
+// row's sums.
+__device__ __forceinline__ void PutChunk(const LoopDesc& D, float* xf, uint8_t* op, int r, int f, const float4& a,
+                                         const float4& b, float& s1, float& s2) {
+  *reinterpret_cast<float4*>(xf + (size_t)r * D.E + f) = a;
+  *reinterpret_cast<float4*>(xf + (size_t)r * D.E + f + 4) = b;
+  const float v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+#pragma unroll
+  for (int j = 0; j < 8; j++) {
+    s1 += v[j];
+    s2 += v[j] * v[j];
+  }
+  StoreNbf<8>(reinterpret_cast<bf16*>(op + OpOffset(r, f)), v);
+}
+
+constexpr int kLoopMaxChunks = 2;  // 8-feature chunks per lane and row (E <= 512)
+
+// One pass per row pair (warp w owns rows w and w + 8): the rows' embedding Wte[id] (+ Wpe[pos])
+// (Embedding.ts:14-26) into x, their norm statistics and the bf16 MMA operand of the first layer. Rows past
+// `nrows` are zero.
+__device__ __forceinline__ void EmbedRows(const LoopDesc& D, float* xf, uint8_t* op, LoopMisc* m, int nrows, int warp,
+                                          int lane) {
+  const int nc = D.E / 8;
+  float4 v[2][kLoopMaxChunks][2];
+#pragma unroll
+  for (int h = 0; h < 2; h++) {
+    const int r = warp + 8 * h;
+#pragma unroll
+    for (int i = 0; i < kLoopMaxChunks; i++) {
+      const int c8 = lane + 32 * i, f = 8 * c8;
+      v[h][i][0] = v[h][i][1] = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (c8 < nc && r < nrows) {
+        const float4* te = reinterpret_cast<const float4*>(D.wte + (size_t)m->tok[r] * D.E + f);
+        v[h][i][0] = __ldg(te);
+        v[h][i][1] = __ldg(te + 1);
+        if (D.wpe) {
+          const float4* pe = reinterpret_cast<const float4*>(D.wpe + (size_t)m->pos[r] * D.E + f);
+          const float4 p0 = __ldg(pe), p1 = __ldg(pe + 1);
+          v[h][i][0] = make_float4(v[h][i][0].x + p0.x, v[h][i][0].y + p0.y, v[h][i][0].z + p0.z, v[h][i][0].w + p0.w);
+          v[h][i][1] = make_float4(v[h][i][1].x + p1.x, v[h][i][1].y + p1.y, v[h][i][1].z + p1.z, v[h][i][1].w + p1.w);
+        }
       }
     }
   }
-}
-
-// bf16 operand [16 x Ep] from the fp32 rows (padding columns and rows past `nrows` are zero).
-__device__ __forceinline__ void BuildOperand(const LoopDesc& D, const float* xf, uint8_t* op, int nrows) {
-  const int chunks = D.Ep / 8;
-  for (int e = threadIdx.x; e < kLoopRows * chunks; e += kLoopThreads) {
-    const int r = e / chunks, k8 = (e % chunks) * 8;
-    float v[8];
 #pragma unroll
-    for (int j = 0; j < 8; j++) v[j] = (r < nrows && k8 + j < D.E) ? xf[(size_t)r * D.E + k8 + j] : 0.f;
-    StoreNbf<8>(reinterpret_cast<bf16*>(op + OpOffset(r, k8)), v);
-  }
-}
-
-// Gathers every owner's slice of E / CS features back into this CTA's x rows.
-__device__ __forceinline__ void PullSlices(const LoopDesc& D, float* xf, const float* xs, int nrows) {
-  const int EB = D.E / kLoopCS;
-  const int n4 = kLoopRows * D.E / 4;
-  for (int e = threadIdx.x; e < n4; e += kLoopThreads) {
-    const int r = e / (D.E / 4), f = (e % (D.E / 4)) * 4;
-    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-    if (r < nrows) v = LdPeer4(PeerAddr(xs + (size_t)r * EB + (f % EB), (uint32_t)(f / EB)));
-    *reinterpret_cast<float4*>(xf + (size_t)r * D.E + f) = v;
-  }
-}
-
-// Embeds the rows' current ids (+ learned position) into x (Embedding.ts:14-26).
-__device__ __forceinline__ void EmbedRows(const LoopDesc& D, float* xf, const LoopMisc* m, int nrows) {
-  for (int e = threadIdx.x; e < kLoopRows * D.E; e += kLoopThreads) {
-    const int r = e / D.E, k = e % D.E;
-    float v = 0.f;
-    if (r < nrows) {
-      v = __ldg(D.wte + (size_t)m->tok[r] * D.E + k);
-      if (D.wpe) v += __ldg(D.wpe + (size_t)m->pos[r] * D.E + k);
+  for (int h = 0; h < 2; h++) {
+    const int r = warp + 8 * h;
+    float s1 = 0.f, s2 = 0.f;
+#pragma unroll
+    for (int i = 0; i < kLoopMaxChunks; i++) {
+      const int c8 = lane + 32 * i;
+      if (c8 < nc) PutChunk(D, xf, op, r, 8 * c8, v[h][i][0], v[h][i][1], s1, s2);
     }
-    xf[e] = v;
+    RowStatsFromSums(D, m, r, s1, s2, lane);
+  }
+}
+
+// The start of a layer (and of the head), in the same shape: x rows gathered from their owners' slices of
+// E / CS features (each owner summed the down-projection partials of its slice), then the rows' norm
+// statistics and the bf16 operand. Remote loads of a warp's both rows are in flight before any is used.
+__device__ __forceinline__ void PullRows(const LoopDesc& D, float* xf, const float* xs, uint8_t* op, LoopMisc* m,
+                                         int nrows, int warp, int lane) {
+  const int EB = D.E / kLoopCS, nc = D.E / 8;
+  float4 v[2][kLoopMaxChunks][2];
+#pragma unroll
+  for (int h = 0; h < 2; h++) {
+    const int r = warp + 8 * h;
+#pragma unroll
+    for (int i = 0; i < kLoopMaxChunks; i++) {
+      const int c8 = lane + 32 * i, f = 8 * c8;
+      v[h][i][0] = v[h][i][1] = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (c8 < nc && r < nrows) {
+        v[h][i][0] = LdPeer4(PeerAddr(xs + (size_t)r * EB + (f % EB), (uint32_t)(f / EB)));
+        v[h][i][1] = LdPeer4(PeerAddr(xs + (size_t)r * EB + ((f + 4) % EB), (uint32_t)((f + 4) / EB)));
+      }
+    }
+  }
+#pragma unroll
+  for (int h = 0; h < 2; h++) {
+    const int r = warp + 8 * h;
+    float s1 = 0.f, s2 = 0.f;
+#pragma unroll
+    for (int i = 0; i < kLoopMaxChunks; i++) {
+      const int c8 = lane + 32 * i;
+      if (c8 < nc) PutChunk(D, xf, op, r, 8 * c8, v[h][i][0], v[h][i][1], s1, s2);
+    }
+    RowStatsFromSums(D, m, r, s1, s2, lane);
+  }
+}
+
+// The end of a layer: this CTA's slice of E / CS features of every row = x + b_proj + the down-projection
+// partials [16][E] of every up-tile owner, summed in owner order (all sixteen loads of a float4 in flight).
+__device__ __forceinline__ void ReduceDownSlice(const LoopDesc& D, const float* b_proj, const float* xf,
+                                                const float* dpart, float* xs, int nrows, int owners, int c) {
+  const int EB = D.E / kLoopCS;
+  for (int e = threadIdx.x; e < kLoopRows * (EB / 4); e += kLoopThreads) {
+    const int r = e / (EB / 4), fi = (e % (EB / 4)) * 4, f = c * EB + fi;
+    float4 v[kLoopCS];
+    if (r < nrows) {
+#pragma unroll
+      for (int o = 0; o < kLoopCS; o++)
+        v[o] = o < owners ? LdPeer4(PeerAddr(dpart + (size_t)r * D.E + f, (uint32_t)o)) : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    float4 sum = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (r < nrows)
+#pragma unroll
+      for (int o = 0; o < kLoopCS; o++)
+        if (o < owners) {
+          sum.x += v[o].x; sum.y += v[o].y; sum.z += v[o].z; sum.w += v[o].w;
+        }
+    const float sv[4] = {sum.x, sum.y, sum.z, sum.w};
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+      const float b = b_proj != nullptr ? b_proj[f + i] : 0.f;
+      xs[(size_t)r * EB + fi + i] = r < nrows ? xf[(size_t)r * D.E + f + i] + (sv[i] + b) : 0.f;
+    }
+  }
+}
+
+// The O reduction of P3 in the same shape: x += the partial O rows of the row's Hk attention items (kv heads in
+// order, every CTA alike), then statistics and operand.
+__device__ __forceinline__ void ReduceORows(const LoopDesc& D, float* xf, const float* opart, uint8_t* op, LoopMisc* m,
+                                            int nrows, int warp, int lane) {
+  const int nc = D.E / 8;
+#pragma unroll
+  for (int h = 0; h < 2; h++) {
+    const int r = warp + 8 * h;
+    float s1 = 0.f, s2 = 0.f;
+#pragma unroll
+    for (int i = 0; i < kLoopMaxChunks; i++) {
+      const int c8 = lane + 32 * i, f = 8 * c8;
+      if (c8 >= nc) continue;
+      float4 a = make_float4(0.f, 0.f, 0.f, 0.f), b = a;
+      if (r < nrows) {
+        float4 pa[4], pb[4];
+        float4 sa = make_float4(0.f, 0.f, 0.f, 0.f), sb = sa;
+        for (int g0 = 0; g0 < D.Hk; g0 += 4) {
+#pragma unroll
+          for (int u = 0; u < 4; u++) {  // up to eight remote loads in flight before the sums
+            const int i2 = r * D.Hk + g0 + u;
+            if (g0 + u < D.Hk) {
+              const float* src = opart + (size_t)(i2 / kLoopCS) * D.E + f;
+              pa[u] = LdPeer4(PeerAddr(src, (uint32_t)(i2 % kLoopCS)));
+              pb[u] = LdPeer4(PeerAddr(src + 4, (uint32_t)(i2 % kLoopCS)));
+            }
+          }
+#pragma unroll
+          for (int u = 0; u < 4; u++)
+            if (g0 + u < D.Hk) {
+              sa.x += pa[u].x; sa.y += pa[u].y; sa.z += pa[u].z; sa.w += pa[u].w;
+              sb.x += pb[u].x; sb.y += pb[u].y; sb.z += pb[u].z; sb.w += pb[u].w;
+            }
+        }
+        a = *reinterpret_cast<const float4*>(xf + (size_t)r * D.E + f);
+        b = *reinterpret_cast<const float4*>(xf + (size_t)r * D.E + f + 4);
+        a.x += sa.x; a.y += sa.y; a.z += sa.z; a.w += sa.w;
+        b.x += sb.x; b.y += sb.y; b.z += sb.z; b.w += sb.w;
+      }
+      PutChunk(D, xf, op, r, f, a, b, s1, s2);
+    }
+    RowStatsFromSums(D, m, r, s1, s2, lane);
   }
 }
 
@@ -488,7 +683,12 @@ __device__ __forceinline__ void AttendItemWarp(const LoopDesc& D, const float* s
 
 // Optional per-phase timestamps (globaltimer, ns) of thread 0 of CTA 0 of cluster 0, one row of kLoopMarks
 // per step; D.trace == nullptr (the default) records nothing.
-constexpr int kLoopMarks = 8;
+constexpr int kLoopMarks = 22;
+#define LOOP_VAL(step, layer, k, v)                                                                        \
+  do {                                                                                                     \
+    if (D.trace != nullptr && blockIdx.x == 0 && threadIdx.x == 0 && (step) < D.trace_steps)               \
+      D.trace[((size_t)(step) * (D.L + 1) + (layer)) * kLoopMarks + (k)] = (v);                           \
+  } while (0)
 #define LOOP_MARK(step, layer, k)                                                                          \
   do {                                                                                                     \
     if (D.trace != nullptr && blockIdx.x == 0 && threadIdx.x == 0 && (step) < D.trace_steps)               \
@@ -506,10 +706,11 @@ __global__ void __launch_bounds__(kLoopThreads, 1) DecodeLoopKernel(const __grid
   float* xf = reinterpret_cast<float*>(smem + D.off_xf);
   float* qkv = reinterpret_cast<float*>(smem + D.off_qkv);      // [nq][16][128]
   float* opart = reinterpret_cast<float*>(smem + D.off_opart);  // [items][E]
-  float* dpart = reinterpret_cast<float*>(smem + D.off_dpart);  // [E][16]
+  float* dpart = reinterpret_cast<float*>(smem + D.off_dpart);  // [16][E]
   float* xs = reinterpret_cast<float*>(smem + D.off_xs);        // [16][E / CS]
   float* att = reinterpret_cast<float*>(smem + D.off_att);      // [entries][2G + G*DD]
   float* sq = reinterpret_cast<float*>(smem + D.off_sq);        // [items][G][DD]
+  float* rope = reinterpret_cast<float*>(smem + D.off_rope);    // [2][16 rows][DD / 2]: this step's cos, sin
   LoopMisc* m = reinterpret_cast<LoopMisc*>(smem + D.off_misc);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -519,13 +720,22 @@ __global__ void __launch_bounds__(kLoopThreads, 1) DecodeLoopKernel(const __grid
   const int nrows = max(0, min(D.rows, D.M - r0));
   const int n_items = LoopCount(nrows * D.Hk, c);  // items i = c + j*CS, row i / Hk, kv head i % Hk
   const int g_item = c % D.Hk;                     // the same for all items of this CTA (CS % Hk == 0)
-  const int EB = D.E / kLoopCS;
   const int hd = D.H * DD;
   const int G = D.G;
   const int state_len = 2 * G + G * DD;
 
-  LoopCtx X{D, MakeSched(D, c, n_items), m, ring, c, g_item, 0, 0, 0, 0};
+  LoopCtx X{D, MakeSched(D, c, n_items), m, ring, c, g_item};
   X.total = D.steps * X.S.per_step;
+  X.cons = X.iss = 0;
+  X.cst = X.ist = 0;
+  X.cpar = X.ipar = 0;
+  X.cur = SchedCursor{0, 0, 0, 0, 0, 0};
+  if (X.total > 0) SkipEmpty(X.S, D.L, X.cur);
+  X.sched = reinterpret_cast<const LoopStage*>(smem + D.off_sched);
+  X.sidx = 0;
+  X.mma_phase = 0;
+  X.wait_full_ns = X.wait_mma_ns = X.issue_ns = X.topup_ns = 0;
+  X.blocking_topups = 0;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < D.stages; s++) {
@@ -536,6 +746,7 @@ __global__ void __launch_bounds__(kLoopThreads, 1) DecodeLoopKernel(const __grid
     m->abort = 0;
     m->issued = 0;
     FenceMbarInit();
+    for (int i = 0; i < 4 * D.L + 1; i++) PrefetchTmaDesc(&D.wmaps[i]);
   }
   if (threadIdx.x < kLoopRows) {
     const int r = threadIdx.x;
@@ -561,29 +772,41 @@ __global__ void __launch_bounds__(kLoopThreads, 1) DecodeLoopKernel(const __grid
   TcgenFenceBefore();
   __syncthreads();
   TcgenFenceAfter();
-  if (threadIdx.x == 0) TopUp(X, false);  // the first weight blocks stream in during the embedding
-  EmbedRows(D, xf, m, nrows);
+  if (threadIdx.x == 0 && X.total > 0) {
+    BuildStageTable(X, reinterpret_cast<LoopStage*>(smem + D.off_sched));
+    TopUp(X, false);  // the first weight stages stream in during the embedding
+  }
+  EmbedRows(D, xf, xb, m, nrows, warp, lane);
+  FenceProxyAsyncShared();
   LoopBarrier();  // every CTA of the cluster is running before any remote access
 
-  const int quad = warp & 3;  // TMEM lane quadrant of an epilogue warp (warps 0-3)
-  const int fl = quad * 32 + lane;  // tile-local output feature of an epilogue thread
-  const uint32_t tq = m->tmem + ((uint32_t)(quad * 32) << 16);
+  // Epilogues: warp w reads TMEM lane quadrant w % 4 (output features fl of a 128-feature tile) and the
+  // accumulator columns of rows (or items) 8 * rh .. 8 * rh + 7.
+  const int quad = warp & 3, rh = warp >> 2;
+  const int fl = quad * 32 + lane;
+  const uint32_t tq = m->tmem + ((uint32_t)(quad * 32) << 16) + 8u * (uint32_t)rh;
 
   for (int s = 0; s < D.steps; s++) {
     if (threadIdx.x < kLoopRows) {  // page of the step's position (the host assigned pages for the run)
       const int r = threadIdx.x;
       m->page[r] = r < nrows ? __ldcg(D.kv.block_table + (size_t)m->slot[r] * D.kv.max_blocks + m->pos[r] / kPageTokens) : -1;
     }
+    if (D.rope_cos != nullptr)  // the rows' RoPE angles of this step, read by every layer's QKV epilogue
+      for (int e = threadIdx.x; e < kLoopRows * (DD / 2); e += kLoopThreads) {
+        const int r = e / (DD / 2), i = e % (DD / 2);
+        const size_t at = (size_t)(r < nrows ? m->pos[r] : 0) * (DD / 2) + i;
+        rope[e] = __ldg(D.rope_cos + at);
+        rope[kLoopRows * (DD / 2) + e] = __ldg(D.rope_sin + at);
+      }
     for (int l = 0; l < D.L; l++) {
       const LoopLayer ly = D.layers[l];
       LOOP_MARK(s, l, 0);
       // ---------------- P1: gather x, norm1 statistics, QKV + RoPE + KV append ----------------
-      if (l > 0) PullSlices(D, xf, xs, nrows);
-      __syncthreads();
-      RowStats(D, xf, m, warp, lane);
-      BuildOperand(D, xf, xb, nrows);
+      if (l > 0) PullRows(D, xf, xs, xb, m, nrows, warp, lane);  // layer 0: from the embedding
+      LOOP_MARK(s, l, 1);
       FenceProxyAsyncShared();
       __syncthreads();
+      LOOP_MARK(s, l, 2);
       if (warp >= 4) {  // this layer's cached K/V rows of the CTA's attention items into L2
         for (int j = warp - 4; j < n_items; j += kLoopWarps - 4) {
           const int i = c + j * kLoopCS, r = i / D.Hk;
@@ -597,28 +820,31 @@ __global__ void __launch_bounds__(kLoopThreads, 1) DecodeLoopKernel(const __grid
         }
       }
       if (X.S.nq > 0) {
-        if (warp == 0) ISSUE_PHASE(X, X.S.bq, X.S.nkE, kTmQkv, [&](int k) { return SmemAddr(xb + (k % X.S.nkE) * kLoopOpBlock); }, 64);
+        if (warp == 0) ISSUE_PHASE(X, X.S.bq, X.S.nkE, kTmQkv, SmemAddr(xb), 64);
         WaitMma(X);
-        if (warp < 4 && !m->abort) {
+        LOOP_MARK(s, l, 3);
+        if (!m->abort) {
           for (int q = 0; q < X.S.nq; q++) {
             const int f = (c + q * kLoopCS) * 128 + fl;
-            uint32_t u[16];
-            TmemLoad16(tq + kTmQkv + 16u * q, u);
+            uint32_t u[8];
+            TmemLoad8(tq + kTmQkv + 16u * q, u);
             TmemWaitLd();
             const bool fok = f < D.Nqkv;
             const float c1 = (D.norm == kNormLayer && fok) ? ly.qkv_c1[f] : 0.f;
             const float c2 = (D.norm == kNormLayer && fok) ? ly.qkv_c2[f] : 0.f;
-            const bool rope = D.rope_cos != nullptr && f < (D.H + D.Hk) * DD;
+            const bool rope_f = D.rope_cos != nullptr && f < (D.H + D.Hk) * DD;
             const int j = f % DD;
-            for (int r = 0; r < kLoopRows; r++) {
-              float v = __uint_as_float(u[r]);
+#pragma unroll
+            for (int jr = 0; jr < 8; jr++) {
+              const int r = 8 * rh + jr;
+              float v = __uint_as_float(u[jr]);
               v = D.norm == kNormLayer ? m->is[r] * (v - m->mu[r] * c1) + c2 : v * m->is[r];
               const float partner = __shfl_xor_sync(0xffffffffu, v, 1);  // RoPE pair (2i, 2i+1)
               if (r >= nrows || !fok) continue;
               const int p = m->pos[r];
-              if (rope) {
-                const float cs = __ldg(D.rope_cos + (size_t)p * (DD / 2) + (j >> 1));
-                const float sn = __ldg(D.rope_sin + (size_t)p * (DD / 2) + (j >> 1));
+              if (rope_f) {
+                const float cs = rope[r * (DD / 2) + (j >> 1)];
+                const float sn = rope[kLoopRows * (DD / 2) + r * (DD / 2) + (j >> 1)];
                 v = (j & 1) ? partner * sn + v * cs : v * cs - partner * sn;
               }
               if (f < hd) {
@@ -639,11 +865,11 @@ __global__ void __launch_bounds__(kLoopThreads, 1) DecodeLoopKernel(const __grid
         }
       }
       if (threadIdx.x == 0) TopUp(X, false);
-      LOOP_MARK(s, l, 1);
+      LOOP_MARK(s, l, 4);
       TcgenFenceBefore();
       LoopBarrier();
       TcgenFenceAfter();
-      LOOP_MARK(s, l, 2);
+      LOOP_MARK(s, l, 5);
       // ---------------- P2: attention of this CTA's items, then their partial O rows ----------------
       for (int e = threadIdx.x; e < n_items * G * DD; e += kLoopThreads) {
         const int jj = e / (G * DD), hf = e % (G * DD);
@@ -684,61 +910,55 @@ __global__ void __launch_bounds__(kLoopThreads, 1) DecodeLoopKernel(const __grid
       }
       FenceProxyAsyncShared();
       __syncthreads();
-      LOOP_MARK(s, l, 3);
+      LOOP_MARK(s, l, 6);
       if (X.S.no > 0) {
         const int kgd = G * DD - (X.S.nkG - 1) * 64;  // valid K of the last k-block
-        if (warp == 0) ISSUE_PHASE(X, X.S.bo, X.S.nkG, kTmO, [&](int k) { return SmemAddr(ctxb + (k % X.S.nkG) * kLoopOpBlock); }, kgd);
+        if (warp == 0) ISSUE_PHASE(X, X.S.bo, X.S.nkG, kTmO, SmemAddr(ctxb), kgd);
         WaitMma(X);
-        if (warp < 4 && !m->abort) {
+        LOOP_MARK(s, l, 7);
+        if (!m->abort && 8 * rh < n_items) {
           for (int mt = 0; mt < X.S.nE128; mt++) {
             const int f = mt * 128 + fl;
-            uint32_t u[16];
-            TmemLoad16(tq + kTmO + 16u * mt, u);
+            uint32_t u[8];
+            TmemLoad8(tq + kTmO + 16u * mt, u);
             TmemWaitLd();
             if (f < D.E)
-              for (int jj = 0; jj < n_items; jj++) opart[(size_t)jj * D.E + f] = __uint_as_float(u[jj]);
+#pragma unroll
+              for (int jr = 0; jr < 8; jr++)
+                if (8 * rh + jr < n_items) opart[(size_t)(8 * rh + jr) * D.E + f] = __uint_as_float(u[jr]);
           }
         }
       }
       if (threadIdx.x == 0) TopUp(X, false);
-      LOOP_MARK(s, l, 4);
+      LOOP_MARK(s, l, 8);
       TcgenFenceBefore();
       LoopBarrier();
       TcgenFenceAfter();
-      LOOP_MARK(s, l, 5);
+      LOOP_MARK(s, l, 9);
       // ---------------- P3: O reduction + residual (every CTA, all rows), norm2, MLP up, partial down ----------
-      for (int e = threadIdx.x; e < nrows * (D.E / 4); e += kLoopThreads) {
-        const int r = e / (D.E / 4), f = (e % (D.E / 4)) * 4;
-        float4 acc = *reinterpret_cast<float4*>(xf + (size_t)r * D.E + f);
-        float4 sum = make_float4(0.f, 0.f, 0.f, 0.f);
-        for (int g = 0; g < D.Hk; g++) {  // heads in order (the reference sums the per-head projections)
-          const int i = r * D.Hk + g;
-          const float4 v = LdPeer4(PeerAddr(opart + (size_t)(i / kLoopCS) * D.E + f, (uint32_t)(i % kLoopCS)));
-          sum.x += v.x; sum.y += v.y; sum.z += v.z; sum.w += v.w;
-        }
-        acc.x += sum.x; acc.y += sum.y; acc.z += sum.z; acc.w += sum.w;
-        *reinterpret_cast<float4*>(xf + (size_t)r * D.E + f) = acc;
-      }
-      __syncthreads();
-      RowStats(D, xf, m, warp, lane);
-      BuildOperand(D, xf, xb, nrows);
+      ReduceORows(D, xf, opart, xb, m, nrows, warp, lane);
+      LOOP_MARK(s, l, 10);
       FenceProxyAsyncShared();
       __syncthreads();
+      LOOP_MARK(s, l, 11);
       if (X.S.nu > 0) {
-        if (warp == 0) ISSUE_PHASE(X, X.S.bu, X.S.nkE, kTmUp, [&](int k) { return SmemAddr(xb + (k % X.S.nkE) * kLoopOpBlock); }, 64);
+        if (warp == 0) ISSUE_PHASE(X, X.S.bu, X.S.nkE, kTmUp, SmemAddr(xb), 64);
         WaitMma(X);
-        if (warp < 4 && !m->abort) {
+        LOOP_MARK(s, l, 12);
+        if (!m->abort) {
           for (int uu = 0; uu < X.S.nu; uu++) {
             const int f = (c + uu * kLoopCS) * 128 + fl;
-            uint32_t u[16];
-            TmemLoad16(tq + kTmUp + 16u * uu, u);
+            uint32_t u[8];
+            TmemLoad8(tq + kTmUp + 16u * uu, u);
             TmemWaitLd();
             const bool fok = f < D.Nup;
             const float c1 = (D.norm == kNormLayer && fok) ? ly.up_c1[f] : 0.f;
             const float c2 = (D.norm == kNormLayer && fok) ? ly.up_c2[f] : 0.f;
             const float bfc = (D.mlp_kind == 0 && fok) ? ly.b_fc[f] : 0.f;
-            for (int r = 0; r < kLoopRows; r++) {
-              float v = __uint_as_float(u[r]);
+#pragma unroll
+            for (int jr = 0; jr < 8; jr++) {
+              const int r = 8 * rh + jr;
+              float v = __uint_as_float(u[jr]);
               v = D.norm == kNormLayer ? m->is[r] * (v - m->mu[r] * c1) + c2 : v * m->is[r];
               const float partner = __shfl_xor_sync(0xffffffffu, v, 1);  // gate (even) / up (odd) pair
               if (D.mlp_kind == 0) {
@@ -760,89 +980,72 @@ __global__ void __launch_bounds__(kLoopThreads, 1) DecodeLoopKernel(const __grid
         }
         FenceProxyAsyncShared();
         __syncthreads();
-        if (warp == 0) ISSUE_PHASE(X, X.S.bd, X.S.nu * X.S.akb, kTmDown,
-                     [&](int k) { return SmemAddr(actb + (k % (X.S.nu * X.S.akb)) * kLoopOpBlock); }, 64);
+        LOOP_MARK(s, l, 13);
+        if (warp == 0) ISSUE_PHASE(X, X.S.bd, X.S.nu * X.S.akb, kTmDown, SmemAddr(actb), 64);
         WaitMma(X);
-        if (warp < 4 && !m->abort) {
+        LOOP_MARK(s, l, 14);
+        if (!m->abort) {
           for (int mt = 0; mt < X.S.nE128; mt++) {
             const int f = mt * 128 + fl;
-            uint32_t u[16];
-            TmemLoad16(tq + kTmDown + 16u * mt, u);
+            uint32_t u[8];
+            TmemLoad8(tq + kTmDown + 16u * mt, u);
             TmemWaitLd();
             if (f < D.E)
 #pragma unroll
-              for (int i = 0; i < 4; i++)
-                reinterpret_cast<float4*>(dpart + (size_t)f * kLoopRows)[i] =
-                    make_float4(__uint_as_float(u[4 * i]), __uint_as_float(u[4 * i + 1]), __uint_as_float(u[4 * i + 2]),
-                                __uint_as_float(u[4 * i + 3]));
+              for (int jr = 0; jr < 8; jr++) dpart[(size_t)(8 * rh + jr) * D.E + f] = __uint_as_float(u[jr]);
           }
         }
       }
       if (threadIdx.x == 0) TopUp(X, false);
-      LOOP_MARK(s, l, 6);
+      LOOP_MARK(s, l, 15);
       TcgenFenceBefore();
       LoopBarrier();
       TcgenFenceAfter();
-      LOOP_MARK(s, l, 7);
+      LOOP_MARK(s, l, 16);
       // ---------------- P4: this CTA's slice of features: down partials of every up-tile owner + residual ------
-      {
-        const int owners = min(kLoopCS, CeilDiv(D.Nup, 128));
-        for (int e = threadIdx.x; e < EB * (kLoopRows / 4); e += kLoopThreads) {
-          const int fi = e / (kLoopRows / 4), r4 = (e % (kLoopRows / 4)) * 4;
-          const int f = c * EB + fi;
-          float4 sum = make_float4(0.f, 0.f, 0.f, 0.f);
-          for (int o = 0; o < owners; o++) {
-            const float4 v = LdPeer4(PeerAddr(dpart + (size_t)f * kLoopRows + r4, (uint32_t)o));
-            sum.x += v.x; sum.y += v.y; sum.z += v.z; sum.w += v.w;
-          }
-          const float b = (D.mlp_kind == 0) ? ly.b_proj[f] : 0.f;
-          const float sv[4] = {sum.x, sum.y, sum.z, sum.w};
-#pragma unroll
-          for (int i = 0; i < 4; i++) {
-            const int r = r4 + i;
-            xs[(size_t)r * EB + fi] = r < nrows ? xf[(size_t)r * D.E + f] + (sv[i] + b) : 0.f;
-          }
-        }
-      }
+      ReduceDownSlice(D, D.mlp_kind == 0 ? ly.b_proj : nullptr, xf, dpart, xs, nrows,
+                      min(kLoopCS, CeilDiv(D.Nup, 128)), c);
       if (threadIdx.x == 0) TopUp(X, false);
+      LOOP_VAL(s, l, 17, X.wait_full_ns);
+      LOOP_VAL(s, l, 18, X.wait_mma_ns);
+      LOOP_VAL(s, l, 19, (unsigned long long)(X.iss - X.cons));
+      LOOP_VAL(s, l, 20, X.issue_ns);
+      LOOP_VAL(s, l, 21, X.topup_ns);
       LoopBarrier();
     }
     // ---------------- head: final norm, LM head tiles, per-row argmax candidates ----------------
     LOOP_MARK(s, D.L, 0);
-    PullSlices(D, xf, xs, nrows);
-    __syncthreads();
-    RowStats(D, xf, m, warp, lane);
-    BuildOperand(D, xf, xb, nrows);
+    PullRows(D, xf, xs, xb, m, nrows, warp, lane);
     FenceProxyAsyncShared();
     __syncthreads();
     {
-      float bv[kLoopRows];
-      int bi[kLoopRows];
+      float bv[8];
+      int bi[8];
 #pragma unroll
-      for (int r = 0; r < kLoopRows; r++) {
-        bv[r] = -INFINITY;
-        bi[r] = 0x7fffffff;
+      for (int jr = 0; jr < 8; jr++) {
+        bv[jr] = -INFINITY;
+        bi[jr] = 0x7fffffff;
       }
       for (int h0 = 0; h0 < X.S.nh; h0 += kLoopHeadChunk) {
         const int nchunk = min(kLoopHeadChunk, X.S.nh - h0);
-        if (warp == 0) ISSUE_PHASE(X, nchunk * X.S.nkE, X.S.nkE, kTmHead, [&](int k) { return SmemAddr(xb + (k % X.S.nkE) * kLoopOpBlock); },
-                     64);
+        if (warp == 0) ISSUE_PHASE(X, nchunk * X.S.nkE, X.S.nkE, kTmHead, SmemAddr(xb), 64);
         WaitMma(X);
-        if (warp < 4 && !m->abort) {
+        if (!m->abort) {
           for (int hh = 0; hh < nchunk; hh++) {
             const int vid = (c + (h0 + hh) * kLoopCS) * 128 + fl;
-            uint32_t u[16];
-            TmemLoad16(tq + kTmHead + 16u * hh, u);
+            uint32_t u[8];
+            TmemLoad8(tq + kTmHead + 16u * hh, u);
             TmemWaitLd();
             if (vid < D.V) {
               const float c1 = D.norm == kNormLayer ? D.head_c1[vid] : 0.f;
               const float c2 = D.norm == kNormLayer ? D.head_c2[vid] : 0.f;
               const float b = D.head_bias[vid];
 #pragma unroll
-              for (int r = 0; r < kLoopRows; r++) {
-                float v = __uint_as_float(u[r]);
+              for (int jr = 0; jr < 8; jr++) {
+                const int r = 8 * rh + jr;
+                float v = __uint_as_float(u[jr]);
                 v = (D.norm == kNormLayer ? m->is[r] * (v - m->mu[r] * c1) + c2 : v * m->is[r]) + b;
-                ArgmaxMerge(bv[r], bi[r], v, vid);
+                ArgmaxMerge(bv[jr], bi[jr], v, vid);
                 if (D.logits && r < nrows) D.logits[((size_t)(r0 + r) * D.out_ld + D.gen0 + s) * D.V + vid] = v;
               }
             }
@@ -852,18 +1055,18 @@ __global__ void __launch_bounds__(kLoopThreads, 1) DecodeLoopKernel(const __grid
         __syncthreads();  // TMEM chunk read before the next chunk's MMAs overwrite it
         TcgenFenceAfter();
       }
-      if (warp < 4) {
+      {
 #pragma unroll
-        for (int r = 0; r < kLoopRows; r++) {
+        for (int jr = 0; jr < 8; jr++) {
 #pragma unroll
           for (int off = 16; off > 0; off >>= 1) {
-            const float ov = __shfl_xor_sync(0xffffffffu, bv[r], off);
-            const int oi = __shfl_xor_sync(0xffffffffu, bi[r], off);
-            ArgmaxMerge(bv[r], bi[r], ov, oi);
+            const float ov = __shfl_xor_sync(0xffffffffu, bv[jr], off);
+            const int oi = __shfl_xor_sync(0xffffffffu, bi[jr], off);
+            ArgmaxMerge(bv[jr], bi[jr], ov, oi);
           }
           if (lane == 0) {
-            m->wcv[warp][r] = bv[r];
-            m->wci[warp][r] = bi[r];
+            m->wcv[quad][8 * rh + jr] = bv[jr];
+            m->wci[quad][8 * rh + jr] = bi[jr];
           }
         }
       }
@@ -885,10 +1088,17 @@ __global__ void __launch_bounds__(kLoopThreads, 1) DecodeLoopKernel(const __grid
     if (threadIdx.x < kLoopRows) {
       const int r = threadIdx.x;
       if (r < nrows) {
+        float cv[kLoopCS];
+        int ci[kLoopCS];
+#pragma unroll
+        for (int o = 0; o < kLoopCS; o++) {
+          cv[o] = LdPeer(PeerAddr(&m->cand_v[r], (uint32_t)o));
+          ci[o] = LdPeerI(PeerAddr(&m->cand_i[r], (uint32_t)o));
+        }
         float v = -INFINITY;
         int i = 0x7fffffff;
-        for (int o = 0; o < kLoopCS; o++)
-          ArgmaxMerge(v, i, LdPeer(PeerAddr(&m->cand_v[r], (uint32_t)o)), LdPeerI(PeerAddr(&m->cand_i[r], (uint32_t)o)));
+#pragma unroll
+        for (int o = 0; o < kLoopCS; o++) ArgmaxMerge(v, i, cv[o], ci[o]);
         const int id = i == 0x7fffffff ? 0 : i;
         if (c == 0) D.out_ids[(size_t)(r0 + r) * D.out_ld + D.gen0 + s] = id;
         m->tok[r] = id;
@@ -896,7 +1106,7 @@ __global__ void __launch_bounds__(kLoopThreads, 1) DecodeLoopKernel(const __grid
       }
     }
     __syncthreads();
-    if (s + 1 < D.steps) EmbedRows(D, xf, m, nrows);
+    if (s + 1 < D.steps) EmbedRows(D, xf, xb, m, nrows, warp, lane);
     LOOP_MARK(s, D.L, 3);
   }
   // write the rows' state back (the host's view of the decode loop continues from here)

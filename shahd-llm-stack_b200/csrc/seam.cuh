@@ -17,7 +17,8 @@ namespace shahd {
 int g_umma_min_rows = 17;
 bool g_use_pdl = true;
 int g_decode_chains = 0;  // 0 = automatic
-int g_persistent_step = 1;  // greedy generate runs its decode steps in the persistent cluster loop
+int g_persistent_step = 0;  // 1: greedy generate runs its decode steps in the persistent cluster loop
+bool g_scalar_seam = false;  // SetScalarKernels(1): the f32 seam keeps exact fp32 FMA chains on CUDA cores
 
 // ---- thread-local last error --------------------------------------------------------------------
 static thread_local std::string t_error;
@@ -194,7 +195,7 @@ static void RunSeam(const char* op, Layout lay, const T* a, const T* b, T* out, 
   const size_t na = (size_t)m * k, nb = lay == kTN ? (size_t)m * n : (size_t)k * n;
   const size_t no = lay == kTN ? (size_t)k * n : (size_t)m * n;
   // f32 NT / NN with enough rows: split-TF32 tensor-core GEMM (A, A lo, B as [n,k], B lo, C, NN: B as given)
-  const bool tc = sizeof(T) == 4 && lay != kTN && Tf32Eligible(m, k, n);
+  const bool tc = sizeof(T) == 4 && lay != kTN && !g_scalar_seam && Tf32Eligible(m, k, n);
   const size_t need = tc ? (2 * Align64(na) + 2 * Align64((size_t)n * k) + Align64(no) + (lay == kNN ? Align64(nb) : 0)) *
                                sizeof(T)
                          : (na + nb + no) * sizeof(T) + 256;
@@ -466,7 +467,10 @@ void SetKernelThreads(int n) { (void)n; }
 
 int ShahdCpuSupportsAvx2Fma(void) { return DeviceOk(); }
 
-void SetScalarKernels(int force) { g_umma_min_rows = force ? 0x7fffffff : 17; }
+void SetScalarKernels(int force) {
+  g_umma_min_rows = force ? 0x7fffffff : 17;
+  g_scalar_seam = force != 0;
+}
 
 int ShahdGpuAvailable(void) { return DeviceOk(); }
 
@@ -484,6 +488,66 @@ int ShahdDeviceErrorFlag(void) {
   int v = 0;
   if (cudaMemcpyFromSymbol(&v, g_shahd_device_error, sizeof(int)) != cudaSuccess) return -1;
   return v;
+}
+
+int ShahdMatMulNTF32Device(const float* a, const float* bt, float* out, int m, int k, int n, int acc, void* stream) {
+  const char* op = "ShahdMatMulNTF32Device";
+  ClearError();
+  if (!CheckDims(op, m, k, n)) return SHAHD_EINVAL;
+  if (!a || !bt || !out) {
+    SetError("%s: null pointer", op);
+    return SHAHD_EINVAL;
+  }
+  if ((reinterpret_cast<uintptr_t>(out) & 15) || k % 4 != 0) {
+    SetError("%s: out must be 16-byte aligned and K a multiple of 4 (16-byte rows for TMA), got K=%d", op, k);
+    return SHAHD_EINVAL;
+  }
+  if (!DeviceOk()) {
+    SetError("%s: no usable sm_100 device", op);
+    return SHAHD_ENODEV;
+  }
+  int dev = 0;
+  SHAHD_CUDA_TRY(cudaGetDevice(&dev));
+  const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  Workspace& w = WorkspaceFor(dev);
+  std::lock_guard<std::mutex> g(w.mu);
+  const size_t na = Align64((size_t)m * k), nb = Align64((size_t)n * k);
+  const size_t need = 2 * (na + nb) * sizeof(float);
+  if (w.cap < need) {
+    SHAHD_CUDA_TRY(cudaStreamSynchronize(st));  // the old workspace may still be read by queued work
+    if (w.buf) cudaFree(w.buf);
+    w.buf = nullptr;
+    w.cap = 0;
+    SHAHD_CUDA_TRY(cudaMalloc(&w.buf, need));
+    w.cap = need;
+  }
+  float* ah = static_cast<float*>(w.buf);
+  float* al = ah + na;
+  float* bh = al + na;
+  float* bl = bh + nb;
+  // the caller's operands stay untouched: the split reads them and writes both parts to the workspace
+  const size_t ea = (size_t)m * k, eb = (size_t)n * k;
+  SplitTf32Kernel<<<std::min<size_t>(4 * NumSMs(dev), (ea + 255) / 256), 256, 0, st>>>(a, ah, al, ea);
+  SplitTf32Kernel<<<std::min<size_t>(4 * NumSMs(dev), (eb + 255) / 256), 256, 0, st>>>(bt, bh, bl, eb);
+  CUtensorMap tah, tal, tbh, tbl;
+  if (!MakeTmaF32(ah, m, k, &tah) || !MakeTmaF32(al, m, k, &tal) || !MakeTmaF32(bh, n, k, &tbh) ||
+      !MakeTmaF32(bl, n, k, &tbl)) {
+    SetError("%s: cuTensorMapEncodeTiled failed", op);
+    return SHAHD_ECUDA;
+  }
+  if (!EnsureKernelAttrs((const void*)GemmNtTf32x3Kernel, kT32Smem)) {
+    TakeLaunchError(nullptr);
+    SetError("%s: the GEMM kernel's shared-memory limit could not be set", op);
+    return SHAHD_ECUDA;
+  }
+  const int tiles = CeilDiv(n, kT32BN) * CeilDiv(m, kT32BM);
+  GemmNtTf32x3Kernel<<<std::min(tiles, NumSMs(dev)), kT32Threads, kT32Smem, st>>>(tah, tal, tbh, tbl, out, m, n, k, acc);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    SetError("%s: launch failed: %s", op, cudaGetErrorString(e));
+    return SHAHD_ECUDA;
+  }
+  return SHAHD_OK;
 }
 
 int ShahdMatMulNTBF16Device(const void* a, const void* bt, float* out, int m, int k, int n, int acc, void* stream) {

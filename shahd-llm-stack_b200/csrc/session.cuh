@@ -112,7 +112,7 @@ struct ShahdSession {
   // persistent cluster decode loop: weight tensor maps (box 64 x 128) and per-layer constants in device memory
   int loop_state = -1;  // -1 not set up yet, 0 unavailable for this model/device, 1 ready
   shahd::LoopLayer* d_loop_layers = nullptr;
-  CUtensorMap* d_loop_wmaps = nullptr;
+  std::vector<CUtensorMap> loop_wmaps;  // copied into every launch's parameters
   int loop_max_clusters = 0;  // clusters of kLoopCS CTAs resident at once with the loop's shared memory
   float* d_loop_logits = nullptr;  // recorded logits of shahd_generate_logits [rows, steps, V]
   size_t loop_logits_cap = 0;
@@ -889,17 +889,21 @@ size_t LoopPlan(const ShahdSession* s, int rows, LoopDesc* D) {
   const int max_items = CeilDiv(rows * s->Hk, kLoopCS);
   const int nq = CeilDiv(CeilDiv(s->Nqkv, 128), kLoopCS), nu = CeilDiv(CeilDiv(s->Nup, 128), kLoopCS);
   const int gd = s->G * s->d;
-  size_t off = 0;
-  auto take = [&](size_t bytes, size_t align) {
-    off = (off + align - 1) / align * align;
-    const size_t at = off;
-    off += bytes;
-    return (int)at;
-  };
-  // everything after the ring; the ring depth is chosen last
-  size_t tail = 0;
-  {
-    off = 0;
+  // the shape fields the per-CTA schedule depends on (CTA 0 holds the most tiles and attention items)
+  D->E = s->E; D->Ep = s->Ep; D->H = s->H; D->Hk = s->Hk; D->d = s->d; D->G = s->G; D->F = s->F; D->Fp = s->Fp;
+  D->V = s->V; D->L = s->L; D->HDp = s->HDp; D->Nqkv = s->Nqkv; D->Nup = s->Nup; D->mlp_kind = s->cfg.mlp_kind;
+  const size_t budget = kLoopSmemBudget - 1024;  // the kernel aligns its base to 1024 bytes
+  for (int boxes = kLoopMaxStageBoxes; boxes >= 1; boxes /= 2) {
+    D->stage_boxes = boxes;
+    const LoopSched S0 = MakeSched(*D, 0, max_items);
+    size_t off = 0;
+    auto take = [&](size_t bytes, size_t align) {
+      off = (off + align - 1) / align * align;
+      const size_t at = off;
+      off += bytes;
+      return (int)at;
+    };
+    // everything after the ring; the ring depth is chosen last
     D->off_xb = take((size_t)(s->Ep / 64) * kLoopOpBlock, 1024);
     D->off_ctxb = take((size_t)CeilDiv(gd, 64) * kLoopOpBlock, 1024);
     D->off_actb = take((size_t)nu * LoopActKb(s->cfg.mlp_kind) * kLoopOpBlock, 1024);
@@ -910,19 +914,22 @@ size_t LoopPlan(const ShahdSession* s, int rows, LoopDesc* D) {
     D->off_xs = take((size_t)kLoopRows * (s->E / kLoopCS) * 4, 16);
     D->off_att = take((size_t)std::max(kLoopWarps, max_items) * (2 * s->G + gd) * 4, 16);
     D->off_sq = take((size_t)max_items * gd * 4, 16);
+    D->off_rope = take((size_t)2 * kLoopRows * (s->d / 2) * 4, 16);
+    D->off_sched = take((size_t)std::max(1, S0.per_step) * sizeof(LoopStage), 16);
     D->off_misc = take(sizeof(LoopMisc), 16);
-    tail = off;
+    const size_t tail = off;
+    const size_t stage_bytes = (size_t)boxes * kLoopBoxBytes;
+    if (tail + 2 * stage_bytes > budget) continue;  // at least two stages in flight
+    const int stages = (int)std::min<size_t>(kLoopMaxStages, (budget - tail) / stage_bytes);
+    const int ring = stages * (int)stage_bytes;
+    D->off_xb += ring; D->off_ctxb += ring; D->off_actb += ring; D->off_xf += ring; D->off_qkv += ring;
+    D->off_opart += ring; D->off_dpart += ring; D->off_xs += ring; D->off_att += ring; D->off_sq += ring;
+    D->off_rope += ring; D->off_sched += ring; D->off_misc += ring;
+    D->stages = stages;
+    D->max_items = max_items;
+    return ring + tail + 1024;
   }
-  const size_t budget = kLoopSmemBudget - 1024;  // the kernel aligns its base to 1024 bytes
-  if (tail + 4 * (size_t)kLoopStageBytes > budget) return 0;
-  const int stages = (int)std::min<size_t>(kLoopMaxStages, (budget - tail) / kLoopStageBytes);
-  const int ring = stages * kLoopStageBytes;
-  D->off_xb += ring; D->off_ctxb += ring; D->off_actb += ring; D->off_xf += ring; D->off_qkv += ring;
-  D->off_opart += ring; D->off_dpart += ring; D->off_xs += ring; D->off_att += ring; D->off_sq += ring;
-  D->off_misc += ring;
-  D->stages = stages;
-  D->max_items = max_items;
-  return ring + tail + 1024;
+  return 0;
 }
 
 // The decode loop runs greedy decode steps of models whose shapes fit its fixed work split: head_dim 32 or
@@ -933,11 +940,12 @@ bool LoopSetup(ShahdSession* s) {
   if (s->loop_state >= 0) return s->loop_state == 1;
   s->loop_state = 0;
   if (!(s->d == 32 || s->d == 64) || s->G > 4 || kLoopCS % s->Hk != 0) return false;
-  if (s->E % 64 != 0 || s->E > 512 || s->Ep != s->E) return false;
+  if (s->E % 64 != 0 || s->E > 512 || s->Ep != s->E || s->L > kLoopMaxLayers) return false;
   if (CeilDiv(CeilDiv(s->Nqkv, 128), kLoopCS) > kLoopMaxTiles || CeilDiv(CeilDiv(s->Nup, 128), kLoopCS) > kLoopMaxTiles ||
       CeilDiv(s->E, 128) > kLoopMaxTiles)
     return false;
-  LoopDesc D{};
+  static thread_local LoopDesc D;
+  D = LoopDesc{};
   if (LoopPlan(s, kLoopRows, &D) == 0) return false;
   // every plan (any rows per cluster: fewer rows leave room for a deeper weight ring) fits the budget
   const size_t smem = kLoopSmemBudget;
@@ -977,11 +985,10 @@ bool LoopSetup(ShahdSession* s) {
     const Layer& Ly = s->layers[l];
     ly[l] = LoopLayer{Ly.qkv_c1, Ly.qkv_c2, Ly.up_c1, Ly.up_c2, Ly.b_fc, Ly.b_proj};
   }
-  if (DevAlloc(s, &s->d_loop_wmaps, wm.size()) != SHAHD_OK || DevAlloc(s, &s->d_loop_layers, ly.size()) != SHAHD_OK)
+  if (DevAlloc(s, &s->d_loop_layers, ly.size()) != SHAHD_OK) return false;
+  if (cudaMemcpy(s->d_loop_layers, ly.data(), sizeof(LoopLayer) * ly.size(), cudaMemcpyHostToDevice) != cudaSuccess)
     return false;
-  if (cudaMemcpy(s->d_loop_wmaps, wm.data(), sizeof(CUtensorMap) * wm.size(), cudaMemcpyHostToDevice) != cudaSuccess ||
-      cudaMemcpy(s->d_loop_layers, ly.data(), sizeof(LoopLayer) * ly.size(), cudaMemcpyHostToDevice) != cudaSuccess)
-    return false;
+  s->loop_wmaps = wm;
   s->loop_max_clusters = nclusters;
   s->loop_state = 1;
   return true;
@@ -1010,7 +1017,8 @@ double LoopBytes(const ShahdSession* s, const std::vector<int>& len, int n, int 
 // step k land in out[:, gen0 + k]. logits (nullable, device [n, steps, V]) records every step's logits.
 int LaunchLoop(ShahdSession* s, int n, int steps, int* d_out, int out_ld, int gen0, float* logits) {
   const int rows = LoopRows(s, n);
-  LoopDesc D{};
+  static thread_local LoopDesc D;  // 8 KB of tensor maps: kept off the stack
+  D = LoopDesc{};
   const size_t smem = LoopPlan(s, rows, &D);
   D.M = n; D.E = s->E; D.Ep = s->Ep; D.H = s->H; D.Hk = s->Hk; D.d = s->d; D.G = s->G; D.F = s->F; D.Fp = s->Fp;
   D.V = s->V; D.L = s->L; D.HDp = s->HDp; D.Nqkv = s->Nqkv; D.Nup = s->Nup;
@@ -1028,7 +1036,7 @@ int LaunchLoop(ShahdSession* s, int n, int steps, int* d_out, int out_ld, int ge
   D.head_bias = s->head_bias; D.head_c1 = s->head_c1; D.head_c2 = s->head_c2;
   D.kv = KvView{s->kv_pool, s->d_block_table, s->max_blocks, s->Hk, s->d, s->page_elems};
   D.layers = s->d_loop_layers;
-  D.wmaps = s->d_loop_wmaps;
+  std::copy(s->loop_wmaps.begin(), s->loop_wmaps.end(), D.wmaps);
   D.trace = nullptr;
   D.trace_steps = 0;
   if (std::getenv("SHAHD_LOOP_TRACE") != nullptr) {
@@ -1896,3 +1904,83 @@ extern "C" int shahd_sample_logits(const float* logits, int32_t rows, int32_t vo
 }
 
 extern "C" const char* shahd_last_error(void) { return GetError(); }
+
+extern "C" int shahd_speculative_round(const float* target_logits, const float* draft_logits, const int32_t* proposals,
+                                       const int32_t* g, const int32_t* budget, int32_t n, int32_t gamma,
+                                       int32_t vocab, const ShahdSampling* opts, uint32_t* rng_states,
+                                       int32_t* out_ids, int32_t* out_count, int32_t* accepted) {
+  const char* op = "shahd_speculative_round";
+  ClearError();
+  if (!target_logits || !draft_logits || !proposals || !g || !budget || !opts || !rng_states || !out_ids ||
+      !out_count || !accepted || n < 1 || gamma < 1 || vocab < 1) {
+    SetError("%s: null buffer or n, gamma, vocab < 1 (n=%d gamma=%d vocab=%d)", op, n, gamma, vocab);
+    return SHAHD_EINVAL;
+  }
+  if (!(opts->temperature > 0) || !std::isfinite(opts->temperature) || std::isnan(opts->top_p)) {
+    SetError("%s: SpeculativeSample needs a finite temperature > 0 and a numeric top_p (greedy speculative "
+             "decoding verifies argmax ids instead)", op);
+    return SHAHD_EINVAL;
+  }
+  if (vocab > (1 << 22)) {
+    SetError("%s: seeded sampling supports vocabularies up to %d ids, got %d", op, 1 << 22, vocab);
+    return SHAHD_EINVAL;
+  }
+  for (int i = 0; i < n; i++) {
+    if (g[i] < 0 || g[i] > gamma || budget[i] < 1) {
+      SetError("%s: sequence %d has g=%d (0..%d) and budget=%d (>= 1)", op, i, g[i], gamma, budget[i]);
+      return SHAHD_EINVAL;
+    }
+    for (int k = 0; k < g[i]; k++)
+      if (proposals[(size_t)i * gamma + k] < 0 || proposals[(size_t)i * gamma + k] >= vocab) {
+        SetError("%s: proposal %d of sequence %d is %d, outside [0,%d)", op, k, i, proposals[(size_t)i * gamma + k], vocab);
+        return SHAHD_EINVAL;
+      }
+  }
+  if (!DeviceOk()) {
+    SetError("%s: no usable sm_100 device", op);
+    return SHAHD_ENODEV;
+  }
+  int dev = 0;
+  SHAHD_CUDA_TRY(cudaGetDevice(&dev));
+  Workspace& w = WorkspaceFor(dev);
+  std::lock_guard<std::mutex> lk(w.mu);
+  const auto a256 = [](size_t b) { return (b + 255) / 256 * 256; };
+  const size_t nt = (size_t)n * (gamma + 1) * vocab, nd = (size_t)n * gamma * vocab;
+  const size_t bt = a256(nt * 4), bd = a256(nd * 4), bp = a256((size_t)n * gamma * 4), bn = a256((size_t)n * 4),
+               bo = a256((size_t)n * (gamma + 1) * 4);
+  const size_t need = bt + bd + bp + 3 * bn + bo + 2 * bn;
+  if (w.cap < need) {
+    if (w.buf) cudaFree(w.buf);
+    w.buf = nullptr;
+    w.cap = 0;
+    SHAHD_CUDA_TRY(cudaMalloc(&w.buf, need));
+    w.cap = need;
+  }
+  if (!w.stream) SHAHD_CUDA_TRY(cudaStreamCreateWithFlags(&w.stream, cudaStreamNonBlocking));
+  uint8_t* b = static_cast<uint8_t*>(w.buf);
+  float* d_t = reinterpret_cast<float*>(b);
+  float* d_d = reinterpret_cast<float*>(b + bt);
+  int* d_p = reinterpret_cast<int*>(b + bt + bd);
+  int* d_g = reinterpret_cast<int*>(b + bt + bd + bp);
+  int* d_b = reinterpret_cast<int*>(b + bt + bd + bp + bn);
+  uint32_t* d_rng = reinterpret_cast<uint32_t*>(b + bt + bd + bp + 2 * bn);
+  int* d_out = reinterpret_cast<int*>(b + bt + bd + bp + 3 * bn);
+  int* d_cnt = reinterpret_cast<int*>(b + bt + bd + bp + 3 * bn + bo);
+  int* d_acc = reinterpret_cast<int*>(b + bt + bd + bp + 3 * bn + bo + bn);
+  SHAHD_CUDA_TRY(cudaMemcpyAsync(d_t, target_logits, nt * 4, cudaMemcpyHostToDevice, w.stream));
+  SHAHD_CUDA_TRY(cudaMemcpyAsync(d_d, draft_logits, nd * 4, cudaMemcpyHostToDevice, w.stream));
+  SHAHD_CUDA_TRY(cudaMemcpyAsync(d_p, proposals, (size_t)n * gamma * 4, cudaMemcpyHostToDevice, w.stream));
+  SHAHD_CUDA_TRY(cudaMemcpyAsync(d_g, g, (size_t)n * 4, cudaMemcpyHostToDevice, w.stream));
+  SHAHD_CUDA_TRY(cudaMemcpyAsync(d_b, budget, (size_t)n * 4, cudaMemcpyHostToDevice, w.stream));
+  SHAHD_CUDA_TRY(cudaMemcpyAsync(d_rng, rng_states, (size_t)n * 4, cudaMemcpyHostToDevice, w.stream));
+  const SpecArgs sa{d_t, d_d, d_p, d_g, d_b, gamma, vocab, d_rng, (float)opts->temperature, opts->top_k, opts->top_p,
+                    d_out, d_cnt, d_acc};
+  SpecRoundKernel<<<n, kSampleThreads, 0, w.stream>>>(sa);
+  SHAHD_CUDA_TRY(cudaGetLastError());
+  SHAHD_CUDA_TRY(cudaMemcpyAsync(out_ids, d_out, (size_t)n * (gamma + 1) * 4, cudaMemcpyDeviceToHost, w.stream));
+  SHAHD_CUDA_TRY(cudaMemcpyAsync(out_count, d_cnt, (size_t)n * 4, cudaMemcpyDeviceToHost, w.stream));
+  SHAHD_CUDA_TRY(cudaMemcpyAsync(accepted, d_acc, (size_t)n * 4, cudaMemcpyDeviceToHost, w.stream));
+  SHAHD_CUDA_TRY(cudaMemcpyAsync(rng_states, d_rng, (size_t)n * 4, cudaMemcpyDeviceToHost, w.stream));
+  SHAHD_CUDA_TRY(cudaStreamSynchronize(w.stream));
+  return SHAHD_OK;
+}

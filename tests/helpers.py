@@ -1,6 +1,7 @@
 """Shared test helpers: the package import, config conversion to the oracle, parity metrics."""
 from __future__ import annotations
 
+import contextlib
 import importlib
 
 import numpy as np
@@ -12,6 +13,18 @@ from oracle import oracle as O  # noqa: E402
 # north_star tolerances: per-step logits within max-abs 2e-2 (BF16) / 1e-4 (TF32/FP32) of the logit range
 TOL_BF16 = 2e-2
 TOL_F32 = 1e-4
+
+
+@contextlib.contextmanager
+def decode_loop(enable: bool):
+    """Greedy generate through the persistent cluster decode loop (True) or per-kernel step chains (False, the
+    library default), restoring the default afterwards."""
+    lib = pkg.load()
+    lib.ShahdSetPersistentStep(1 if enable else 0)
+    try:
+        yield
+    finally:
+        lib.ShahdSetPersistentStep(0)
 
 
 def oracle_shape(cfg, precision: str = "F32") -> O.Shape:

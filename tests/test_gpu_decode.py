@@ -10,7 +10,7 @@ tiles (ShahdSetTensorCoreMinRows(1)).
 import numpy as np
 import pytest
 
-from tests.helpers import ARCHS, O, TOL_BF16, greedy_agrees, oracle_shape, pkg, range_rel_err
+from tests.helpers import ARCHS, O, TOL_BF16, decode_loop, greedy_agrees, oracle_shape, pkg, range_rel_err
 
 pytestmark = pytest.mark.gpu
 
@@ -174,8 +174,7 @@ def test_launch_modes_give_identical_ids():
     p = pkg.init_params(cfg, w.weight_seed)
     prompts = np.stack([O.uniform_ids(40, cfg.vocab_size, seed=500 + i) for i in range(8)])
     lib = pkg.load()
-    lib.ShahdSetPersistentStep(0)  # the per-kernel step chain, where programmatic launch applies
-    try:
+    with decode_loop(False):  # the per-kernel step chain, where programmatic launch applies
         with pkg.Session(cfg, p, max_seqs=8) as sess:
             a = sess.generate(prompts, 20)
             lib.ShahdSetProgrammaticLaunch(0)
@@ -183,8 +182,6 @@ def test_launch_modes_give_identical_ids():
                 b = sess.generate(prompts, 20)
             finally:
                 lib.ShahdSetProgrammaticLaunch(1)
-    finally:
-        lib.ShahdSetPersistentStep(1)
     assert np.array_equal(a, b)
     assert lib.ShahdDeviceErrorFlag() == 0
 
@@ -198,15 +195,12 @@ def test_decode_chains_agree_up_to_near_ties():
     prompts = np.stack([O.uniform_ids(96, cfg.vocab_size, seed=700 + i) for i in range(64)])
     lib = pkg.load()
     outs = {}
-    lib.ShahdSetPersistentStep(0)  # chains split the per-kernel step path
-    try:
+    with decode_loop(False):  # chains split the per-kernel step path
         with pkg.Session(cfg, p, max_seqs=64) as sess:
             for chains in (1, 2, 4):
                 lib.ShahdSetDecodeChains(chains)
                 outs[chains] = sess.generate(prompts, 24)
             lib.ShahdSetDecodeChains(0)
-    finally:
-        lib.ShahdSetPersistentStep(1)
     model = O.Model(oracle_shape(cfg, "F32"), p.astype(np.float64))
     for chains in (2, 4):
         for i in np.nonzero((outs[chains] != outs[1]).any(axis=1))[0][:4]:
@@ -237,9 +231,9 @@ def test_microchat_generate_spot_check_and_determinism():
 
 
 def test_decode_loop_agrees_with_per_kernel_path():
-    # greedy generate runs its decode steps in the persistent cluster loop by default; with it off, the same
-    # steps run as per-kernel launch chains (different tiles, reduction order and attention split). Both must
-    # pass the oracle's teacher-forced check, and may only differ from one another at near ties.
+    # greedy generate runs its decode steps as per-kernel launch chains by default; with the persistent cluster
+    # loop on, the same steps run in one launch (different tiles, reduction order and attention split). Both
+    # must pass the oracle's teacher-forced check, and may only differ from one another at near ties.
     w = pkg.configs.MICROCHAT
     cfg = w.model
     p = pkg.init_params(cfg, w.weight_seed)
@@ -247,12 +241,9 @@ def test_decode_loop_agrees_with_per_kernel_path():
     lib = pkg.load()
     res = {}
     for mode in (1, 0):
-        lib.ShahdSetPersistentStep(mode)
-        try:
+        with decode_loop(mode == 1):
             with pkg.Session(cfg, p, max_seqs=40) as sess:
                 res[mode] = sess.generate(prompts, 24)
-        finally:
-            lib.ShahdSetPersistentStep(1)
     assert lib.ShahdDeviceErrorFlag() == 0
     model = O.Model(oracle_shape(cfg, "F32"), p.astype(np.float64))
     for mode in (0, 1):

@@ -12,9 +12,15 @@ the decode loop), and every id must be the oracle's argmax outside near ties.
 import numpy as np
 import pytest
 
-from tests.helpers import O, TOL_BF16, greedy_agrees, oracle_shape, pkg, range_rel_err
+from tests.helpers import O, TOL_BF16, decode_loop, greedy_agrees, oracle_shape, pkg, range_rel_err
 
 pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(autouse=True)
+def _loop_on():
+    with decode_loop(True):  # an opt-in path: every test of this file runs greedy generate through it
+        yield
 
 LOOP_ARCHS = [
     ("E256 d64 GQA4/2 SwiGLU RmsNorm RoPE",

@@ -5,6 +5,8 @@
   prefix (CachedForward.ts:113-150 + ArgmaxOf, Distribution.ts:19-30): it must be the oracle's argmax unless
   the oracle's top-2 margin is within 2e-2 of the logit range. The ids must also be the ones recorded in
   tests/golden/microchat_job.json (what bench.py compares its own output with).
+* The same job through the opt-in persistent decode loop: every id checked the same way, and the logits of
+  four rows at every step.
 * The same 64 rows stepped through shahd_step to position 511 (the batched tensor-core projections, the
   split-K down projection, decode attention over up to eight 64-position pages): the logits of four rows
   are compared with the oracle at every step (CachedForwardStep, CachedForward.ts:94-96).
@@ -19,7 +21,7 @@ import os
 import numpy as np
 import pytest
 
-from tests.helpers import O, TOL_BF16, greedy_agrees, oracle_shape, pkg, range_rel_err
+from tests.helpers import O, TOL_BF16, decode_loop, greedy_agrees, oracle_shape, pkg, range_rel_err
 
 pytestmark = pytest.mark.gpu
 
@@ -54,14 +56,17 @@ def test_microchat_bench_job_every_row_every_step():
         "moved (a near tie flipped); regenerate it with tests/golden/make_microchat_job.py", got)
 
 
-def test_microchat_bench_job_logits_of_four_rows_every_step():
-    # the bench path itself (the persistent decode loop over the bench's 64 sequences, positions 127..510):
-    # logits recorded at every step, four rows compared with the oracle decoder pushed the GPU's ids
+def test_microchat_bench_job_through_the_decode_loop_logits_of_four_rows_every_step():
+    # the bench's job (64 sequences, positions 127..510) through the opt-in persistent decode loop: logits
+    # recorded at every step, four rows compared with the oracle decoder pushed the GPU's ids, and every id of
+    # every row judged by the oracle teacher-forced on its own prefix
     w = pkg.configs.MICROCHAT
     params, model = _model(w.model, w.weight_seed)
     prompts = pkg.sharding.shard_prompts(w, 0)
-    with pkg.Session(w.model, params, max_seqs=w.seqs) as sess:
+    with decode_loop(True), pkg.Session(w.model, params, max_seqs=w.seqs) as sess:
         ids, logits = sess.generate_logits(prompts, w.new_tokens)
+    chk = model.check_trajectories(prompts, ids, TOL_BF16)
+    assert int(chk["fails"].sum()) == 0, np.nonzero(chk["fails"])[0][:8]
     worst = 0.0
     for i in (0, 21, 42, 63):
         dec = O.Decoder(model, prompts[i])

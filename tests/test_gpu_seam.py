@@ -113,11 +113,17 @@ def test_bf16_tensor_core_matmul_nt(m, k, n):
 
 # ---- f32 seam on the tensor cores (split-TF32, three tcgen05 kind::tf32 passes) ---------------------
 # The operator-sweep shapes of the MatMulNT config: fp32 A[M,K], B[N,K] ~ N(0,1); M >= 64 takes the
-# tensor cores, M = 1 the CUDA-core kernel. The bar is north_star's 1e-4 of the output range for TF32/fp32
-# and FfiGuard's 1e-4 scaled error (Tests/FfiGuard.Test.ts:146-200). Reference: an f64 product of the
-# same f32 inputs (numpy's f64 matmul for the large shapes: the oracle's f64 dot product, only faster).
+# tensor cores, M = 1 the CUDA-core kernel. The bar is north_star's: within 1e-4 of the output range for
+# TF32/fp32. (FfiGuard's max(|want|, 1)-scaled 1e-4, Tests/FfiGuard.Test.ts:146-200, is a bar for exact fp32
+# FMA chains; its shapes all have fewer than 64 rows and keep the CUDA-core kernel, which SetScalarKernels
+# forces, as the reference's test does.) Reference: an f64 product of the same f32 inputs (numpy's f64
+# matmul for the large shapes: the oracle's f64 dot product, only faster).
 
 SWEEP_NK = [(768, 256), (1024, 256), (256, 1024), (4096, 256), (4096, 1024)]
+
+
+def range_err(got, want):
+    return float(np.abs(got - want).max()) / float(want.max() - want.min())
 
 
 @pytest.mark.parametrize("m", [1, 64, 1024])
@@ -129,13 +135,11 @@ def test_f32_matmul_nt_sweep_shapes(gpu, m, n, k):
     want = a.astype(np.float64) @ bt.astype(np.float64).T
     out = np.full(m * n, 7, np.float32)
     gpu.MatMulNtInto(a.ravel(), bt.ravel(), out, m, k, n)
-    rng_w = float(want.max() - want.min())
-    assert float(np.abs(out.reshape(m, n) - want).max()) / rng_w < 1e-4
-    assert scaled(out, want.ravel()) < 1e-4
+    assert range_err(out.reshape(m, n), want) < 1e-4
     seed = rng.standard_normal(m * n).astype(np.float32)
     acc = seed.copy()
     gpu.MatMulNtAcc(a.ravel(), bt.ravel(), acc, m, k, n)
-    assert scaled(acc, want.ravel() + seed) < 1e-4
+    assert range_err(acc, want.ravel() + seed) < 1e-4
 
 
 def test_f32_matmul_nt_largest_sweep_shape(gpu):
@@ -146,7 +150,7 @@ def test_f32_matmul_nt_largest_sweep_shape(gpu):
     out = np.empty(m * n, np.float32)
     gpu.MatMulNtInto(a.ravel(), bt.ravel(), out, m, k, n)
     want = a.astype(np.float64) @ bt.astype(np.float64).T
-    assert float(np.abs(out.reshape(m, n) - want).max()) / float(want.max() - want.min()) < 1e-4
+    assert range_err(out.reshape(m, n), want) < 1e-4
 
 
 @pytest.mark.parametrize("m,k,n", [(64, 256, 768), (300, 100, 130), (1024, 1024, 256)])
@@ -156,6 +160,43 @@ def test_f32_matmul_nn_on_tensor_cores(gpu, m, k, n):
     b = rng.standard_normal((k, n), dtype=np.float32)
     out = np.full(m * n, 7, np.float32)
     gpu.MatMulInto(a.ravel(), b.ravel(), out, m, k, n)
-    want = (a.astype(np.float64) @ b.astype(np.float64)).ravel()
-    assert scaled(out, want) < 1e-4
+    assert range_err(out.reshape(m, n), a.astype(np.float64) @ b.astype(np.float64)) < 1e-4
+    assert pkg._lib.load().ShahdDeviceErrorFlag() == 0
+
+
+def test_scalar_kernels_force_exact_fp32_chains(gpu):
+    # SetScalarKernels(1) (matmul.go:111-118) forces the CUDA-core kernel: FfiGuard's scaled bar then holds at
+    # tensor-core-sized shapes too
+    m, k, n = 256, 128, 512
+    rng = np.random.default_rng(6)
+    a = rng.standard_normal((m, k), dtype=np.float32)
+    bt = rng.standard_normal((n, k), dtype=np.float32)
+    out = np.empty(m * n, np.float32)
+    gpu.SetScalarKernels(True)
+    try:
+        gpu.MatMulNtInto(a.ravel(), bt.ravel(), out, m, k, n)
+    finally:
+        gpu.SetScalarKernels(False)
+    assert scaled(out, (a.astype(np.float64) @ bt.astype(np.float64).T).ravel()) < 1e-4
+
+
+@pytest.mark.parametrize("m,k,n", [(64, 256, 768), (1024, 1024, 4096), (200, 40, 72)])
+def test_f32_device_tensor_core_matmul_nt(m, k, n):
+    import torch
+    g = torch.Generator(device="cpu").manual_seed(2)
+    a = torch.randn(m, k, generator=g).cuda()
+    bt = torch.randn(n, k, generator=g).cuda()
+    a0, b0 = a.clone(), bt.clone()
+    out = torch.full((m, n), 7.0, device="cuda")
+    pkg.backend.matmul_nt_f32_device(a.data_ptr(), bt.data_ptr(), out.data_ptr(), m, k, n, acc=False)
+    torch.cuda.synchronize()
+    ref = a.double() @ bt.double().T
+    rng = float(ref.max() - ref.min())
+    assert float((out.double() - ref).abs().max()) / rng < 1e-4
+    assert torch.equal(a, a0) and torch.equal(bt, b0)  # the operands are not modified
+    seed = torch.randn(m, n, generator=g).cuda()
+    acc = seed.clone()
+    pkg.backend.matmul_nt_f32_device(a.data_ptr(), bt.data_ptr(), acc.data_ptr(), m, k, n, acc=True)
+    torch.cuda.synchronize()
+    assert float((acc.double() - (ref + seed.double())).abs().max()) / rng < 1e-4
     assert pkg._lib.load().ShahdDeviceErrorFlag() == 0
