@@ -37,7 +37,9 @@ PROMPT_SEED_BASE = 1000  # sequence g's prompt: floor(NextFloat() * vocab) from 
 
 # The decode workloads as plain data, so the reference arm runs without the GPU package. They equal
 # shahd-llm-stack_b200/configs.py (tests/test_bench_contract.py checks it). `ref_sample`: sequences and
-# new tokens of one reference-arm step (None: the whole job).
+# new tokens of one reference-arm step (None: the whole job). `scaling` "strong": `seqs` is the whole job,
+# split over the ranks (Phase2Modern-style: 4096 sequences over 1/2/4/8 GPUs); otherwise every rank runs
+# `seqs` sequences of its own (weak scaling).
 WORKLOADS = {
     "foundry": dict(name="foundry-shape E128 L4 H4 GeGlu F512 ctx256 V4096", embed_dim=128, num_layers=4, num_heads=4,
                     kv_heads=4, block_size=256, vocab_size=4096, mlp_hidden=512, position_scheme="Learned",
@@ -50,7 +52,7 @@ WORKLOADS = {
     "phase2": dict(name="Phase2Modern-style E1024 L16 H16/4 SwiGlu F2816 ctx2048 V32768", embed_dim=1024,
                    num_layers=16, num_heads=16, kv_heads=4, block_size=2048, vocab_size=32768, mlp_hidden=2816,
                    position_scheme="Rope", norm_kind="RmsNorm", mlp_kind="SwiGlu", weight_seed=4, seqs=4096,
-                   prompt_len=512, new_tokens=512, ref_sample=(1, 8)),
+                   prompt_len=512, new_tokens=512, ref_sample=(1, 8), scaling="strong"),
 }
 _SHAPE_KEYS = ("embed_dim", "num_layers", "num_heads", "kv_heads", "block_size", "vocab_size", "mlp_hidden",
                "position_scheme", "norm_kind", "mlp_kind")
@@ -240,8 +242,8 @@ def run_reference(args, rank: int, world: int) -> None:
     value = seqs * new / (ms / 1000.0)
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-        "dtype": "f64", "data": "synthetic",
+        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": wd.get("scaling", "weak"),
+        "vs_baseline": None, "dtype": "f64", "data": "synthetic",
         "config": {"workload": wd["name"], "seqs_per_gpu": seqs, "prompt_len": wd["prompt_len"], "new_tokens": new,
                    "global_batch": seqs, "seq_len": wd["prompt_len"] + new,
                    "sample_of": f"{wd['seqs']} sequences x {wd['new_tokens']} new tokens per GPU",
@@ -266,9 +268,17 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
     torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
     pkg = package()
+    import dataclasses
+
     w = pkg.configs.WORKLOADS[args.workload]
+    strong = WORKLOADS[args.workload].get("scaling") == "strong"
+    if strong:  # the job's sequences are split over the ranks
+        if w.seqs % world:
+            raise SystemExit(f"{w.name}: {w.seqs} sequences do not split over {world} GPUs")
+        w = dataclasses.replace(w, seqs=w.seqs // world)
+    if args.seqs is not None:
+        w = dataclasses.replace(w, seqs=args.seqs)
     if args.new_tokens is not None:
-        import dataclasses
         w = dataclasses.replace(w, new_tokens=args.new_tokens)
     cfg = w.model
     params = pkg.init_params(cfg, w.weight_seed)
@@ -277,7 +287,10 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
         lib.ShahdSetDecodeChains(args.chains)
     if args.tc_min_rows:
         lib.ShahdSetTensorCoreMinRows(args.tc_min_rows)
-    sess = pkg.Session(cfg, params, max_seqs=w.seqs, device=local_rank)
+    # a KV pool of the job's size: every sequence's pages up to prompt + new positions (Phase2Modern-style:
+    # 4096 x 16 pages of 1 MiB = 64 GiB on one GPU)
+    kv_pages = w.seqs * -(-min(w.prompt_len + w.new_tokens, cfg.block_size) // 64)
+    sess = pkg.Session(cfg, params, max_seqs=w.seqs, device=local_rank, kv_pages=kv_pages)
     prompts = prompts_for(w, rank)
     offs = np.arange(0, (w.seqs + 1) * w.prompt_len, w.prompt_len, dtype=np.int32)
     d_prompts = torch.from_numpy(prompts.reshape(-1).copy()).to(dev)
@@ -346,7 +359,8 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
 
     # e2e through the host-buffer C ABI: prompts H2D, ids D2H inside the timed region
     e2e_ms = []
-    for i in range(args.warmup + args.steps):
+    e2e_warm = args.warmup if args.workload == "microchat" else 1  # the device leg already warmed the session
+    for i in range(e2e_warm + args.steps):
         flush.zero_()
         torch.cuda.synchronize(dev)
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -354,7 +368,7 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
         sess.generate(prompts, w.new_tokens)
         e1.record(stream)
         torch.cuda.synchronize(dev)
-        if i >= args.warmup:
+        if i >= e2e_warm:
             e2e_ms.append(e0.elapsed_time(e1))
     te = torch.tensor([sum(e2e_ms)], dtype=torch.float64, device=dev)
     if dist is not None:
@@ -411,7 +425,8 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
                for k, v in prof.items() if v["launches"] > 0}
     expected = None
     gpath = os.path.join(ROOT, "tests", "golden", "microchat_job.json")
-    if w.name == pkg.configs.MICROCHAT.name and w.new_tokens == pkg.configs.MICROCHAT.new_tokens and os.path.exists(gpath):
+    mc = pkg.configs.MICROCHAT
+    if (w.name, w.seqs, w.new_tokens) == (mc.name, mc.seqs, mc.new_tokens) and rank == 0 and os.path.exists(gpath):
         with open(gpath) as f:
             expected = json.load(f)["checksum"]
     output_check = {"expected_checksum_per_rank": expected,
@@ -419,7 +434,7 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
                     "how": "tests/golden/microchat_job.json: the ids of rank 0's 64 sequences, every id checked against "
                            "the oracle teacher-forced on its own prefix"}
     cpu = goffi = None
-    if world == 1:  # the reference's CPU path on this host, rank 0 at N=1 only
+    if world == 1 and not args.skip_cpu:  # the reference's CPU path on this host, rank 0 at N=1 only
         threads = os.cpu_count() or 1
         wd = WORKLOADS[args.workload]
         seqs, new = (w.seqs, w.new_tokens) if wd["ref_sample"] is None else wd["ref_sample"]
@@ -427,11 +442,14 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
         goffi = goffi_projection_bound(wd, threads)
     line = {
         "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "strong" if strong else "weak",
+        "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic",
         "config": {"workload": w.name, "seqs_per_gpu": w.seqs, "prompt_len": w.prompt_len, "new_tokens": w.new_tokens,
                    "global_batch": world * w.seqs, "seq_len": w.prompt_len + w.new_tokens,
                    "parallelism": f"sequence shards x{world} (full weight replica per GPU, no collective in the step)",
+                   "weights_l2_resident": 2.0 * cfg.matrix_params() < 63e6,
+                   "kv_pool_bytes": int(kv_pages) * cfg.num_layers * cfg.kv * 2 * 64 * cfg.head_dim * 2,
                    "weights": f"reference init seed {w.weight_seed} (fp32 master -> bf16)",
                    "l2": "flushed (512 MiB write) before every timed step", "output_checksums": checksums},
         "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": int(prompts.nbytes + offs.nbytes),
@@ -532,6 +550,9 @@ def main() -> None:
     ap.add_argument("--tc-min-rows", type=int, default=0, help="rows from which projections use tensor cores (0 = default)")
     ap.add_argument("--new-tokens", type=int, default=None,
                     help="override the workload's new tokens per sequence (small ncu captures only)")
+    ap.add_argument("--seqs", type=int, default=None,
+                    help="override the sequences per GPU (1: the batch-1 decode line)")
+    ap.add_argument("--skip-cpu", action="store_true", help="leave out the CPU baselines (long secondary legs)")
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))

@@ -82,6 +82,11 @@ void ShahdSetDecodeChains(int chains);
  * shapes measured) runs one CUDA-graph-replayed launch chain per step. Results agree within the parity
  * tolerance. Process-wide; no counterpart in the reference. */
 void ShahdSetPersistentStep(int enable);
+/* 1 (default): causal prefill attention of head_dim 64 runs on the tensor cores (tcgen05 Q.K^T and P.V tiles
+ * in TMEM, bf16 operands, fp32 softmax and accumulation); 0: the CUDA-core tile kernel (fp32 queries and
+ * products). Both agree with the oracle within the parity tolerance. Process-wide; no counterpart in the
+ * reference. */
+void ShahdSetTensorCorePrefillAttention(int enable);
 /* First error code a kernel recorded for a bounded device-side wait that gave up (0 = none). */
 int ShahdDeviceErrorFlag(void);
 /* Device-pointer MatMulNT on the tensor cores: out[M,N] (+)= a[M,K] @ btᵀ with a, bt bf16 row-major

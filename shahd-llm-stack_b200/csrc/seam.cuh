@@ -17,6 +17,7 @@ namespace shahd {
 int g_umma_min_rows = 17;
 bool g_use_pdl = true;
 int g_decode_chains = 0;  // 0 = automatic
+int g_umma_prefill_attn = 1;  // causal prefill attention of head_dim 64 on the tensor cores
 int g_persistent_step = 0;  // 1: greedy generate runs its decode steps in the persistent cluster loop
 bool g_scalar_seam = false;  // SetScalarKernels(1): the f32 seam keeps exact fp32 FMA chains on CUDA cores
 
@@ -483,6 +484,7 @@ void ShahdSetProgrammaticLaunch(int enable) { g_use_pdl = enable != 0; }
 void ShahdSetDecodeChains(int chains) { g_decode_chains = chains < 0 ? 0 : chains; }
 
 void ShahdSetPersistentStep(int enable) { g_persistent_step = enable != 0; }
+void ShahdSetTensorCorePrefillAttention(int enable) { g_umma_prefill_attn = enable != 0; }
 
 int ShahdDeviceErrorFlag(void) {
   int v = 0;

@@ -22,6 +22,7 @@
 #include "decode_kernels.cuh"
 #include "params.h"
 #include "prefill_attention.cuh"
+#include "prefill_attention_umma.cuh"
 #include "sampling.cuh"
 #include "decode_loop.cuh"
 #include "umma_linear.cuh"
@@ -98,6 +99,8 @@ struct ShahdSession {
   int kv_pages, max_blocks;
   int* d_block_table;
   int* h_block_table = nullptr;  // pinned mirror
+  CUtensorMap kv_tmap;     // the pool as rows of d dims (head_dim 64): TMA source of the tensor-core prefill attention
+  bool kv_tmap_ok = false;
   std::vector<int> free_pages;
   std::vector<int> h_len;
   int* d_seq_len;
@@ -451,6 +454,9 @@ int EnqueueStep(ShahdSession* s, const StepPlan& p, cudaStream_t st, int r0 = 0,
       Timed(s, st, pk + kProfAttention, attn_fixed, [&] {
         if (rows_kernel) {
           LaunchAttnRows(s->d, s->G, dim3(rsplit, s->Hk, M), s->num_sms, st, aa);
+        } else if (tiled && s->d == kFaD && g_umma_prefill_attn && s->kv_tmap_ok) {
+          const FaArgs fa{s->kv_tmap, pa, s->L, CeilDiv(p.plan_qblocks * kPfQ, kFaQ)};
+          LaunchPdl(PrefillAttnUmmaKernel, dim3(fa.qblocks, s->H, p.plan_n), dim3(kFaThreads), kFaSmemLaunch, st, fa);
         } else if (tiled) {
           if (s->d == 64) LaunchPdl(PrefillAttnKernel<64>, pg, dim3(kPfThreads), PrefillAttnSmem(64), st, pa);
           else if (s->d == 32) LaunchPdl(PrefillAttnKernel<32>, pg, dim3(kPfThreads), PrefillAttnSmem(32), st, pa);
@@ -1350,6 +1356,13 @@ extern "C" int shahd_session_create(const ShahdModelCfg* cfg, const void* params
   // ---- KV pool + tables ----
   const int R = s->max_seqs;
   if ((rc = DevAlloc(s, &s->kv_pool, s->page_elems * (size_t)s->kv_pages)) != SHAHD_OK) return fail(rc);
+  // positions a page has not been written at hold zeros: a masked key's probability is exactly zero, and the
+  // tensor-core P.V must not meet a non-finite leftover there
+  cudaMemset(s->kv_pool, 0, sizeof(bf16) * s->page_elems * (size_t)s->kv_pages);
+  if (s->d == kFaD) {
+    const long long rows = (long long)s->page_elems / s->d * s->kv_pages;
+    s->kv_tmap_ok = rows < (1LL << 31) && MakeTmaBf16(s->kv_pool, (int)rows, s->d, s->d, kPageTokens, &s->kv_tmap);
+  }
   if ((rc = DevAlloc(s, &s->d_block_table, (size_t)R * s->max_blocks)) != SHAHD_OK) return fail(rc);
   if ((rc = DevAlloc(s, &s->d_seq_len, (size_t)R)) != SHAHD_OK) return fail(rc);
   if (cudaMallocHost(&s->h_block_table, sizeof(int) * (size_t)R * s->max_blocks) != cudaSuccess ||
@@ -1412,7 +1425,8 @@ extern "C" int shahd_session_create(const ShahdModelCfg* cfg, const void* params
       !EnsureKernelAttrs((const void*)AttnDecodeKernel<128>, AttnSmemBytes(128)) ||
       !EnsureKernelAttrs((const void*)PrefillAttnKernel<32>, PrefillAttnSmem(32)) ||
       !EnsureKernelAttrs((const void*)PrefillAttnKernel<64>, PrefillAttnSmem(64)) ||
-      !EnsureKernelAttrs((const void*)PrefillAttnKernel<128>, PrefillAttnSmem(128))) {
+      !EnsureKernelAttrs((const void*)PrefillAttnKernel<128>, PrefillAttnSmem(128)) ||
+      !EnsureKernelAttrs((const void*)PrefillAttnUmmaKernel, kFaSmemLaunch)) {
     TakeLaunchError(nullptr);
     SetError("shahd_session_create: kernel attributes could not be set on device %d", s->device);
     return fail(SHAHD_ECUDA);

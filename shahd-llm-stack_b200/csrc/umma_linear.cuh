@@ -35,6 +35,7 @@ constexpr int kUmmaThreads = 128;
 extern int g_umma_min_rows;
 extern int g_decode_chains;
 extern int g_persistent_step;
+extern int g_umma_prefill_attn;
 #define kUmmaMinRows (::shahd::g_umma_min_rows)
 
 // Tile width: prefill-sized row counts take wide tiles; decode-sized ones the narrowest tile whose grid
