@@ -87,6 +87,13 @@ void ShahdSetPersistentStep(int enable);
  * products). Both agree with the oracle within the parity tolerance. Process-wide; no counterpart in the
  * reference. */
 void ShahdSetTensorCorePrefillAttention(int enable);
+/* Decode-row attention kernel: 0 automatic (default: page streaming for rows attending >= 384 cached
+ * positions on average when rows x kv heads fill the SMs, read-ahead rows otherwise), 1 the read-ahead rows
+ * kernel (32-position warp tasks, K/V rows in registers), 2 the page-ring kernel (64-position pages by bulk
+ * copies into a three-page ring, block-wide phases), 3 the page-streaming kernel (a producer warp's bulk
+ * copies into a six-page ring, one page per compute warp, no block-wide barrier per page). Results agree
+ * within the parity tolerance. Process-wide tuning hook; no counterpart in the reference. */
+void ShahdSetDecodeAttentionKernel(int mode);
 /* First error code a kernel recorded for a bounded device-side wait that gave up (0 = none). */
 int ShahdDeviceErrorFlag(void);
 /* Device-pointer MatMulNT on the tensor cores: out[M,N] (+)= a[M,K] @ btᵀ with a, bt bf16 row-major

@@ -17,7 +17,8 @@ namespace shahd {
 int g_umma_min_rows = 17;
 bool g_use_pdl = true;
 int g_decode_chains = 0;  // 0 = automatic
-int g_umma_prefill_attn = 1;  // causal prefill attention of head_dim 64 on the tensor cores
+int g_umma_prefill_attn = 1;
+int g_decode_attn_kernel = 0;  // decode-row attention: 0 automatic, 1 read-ahead rows, 2 page ring, 3 page streaming  // causal prefill attention of head_dim 64 on the tensor cores
 int g_persistent_step = 0;  // 1: greedy generate runs its decode steps in the persistent cluster loop
 bool g_scalar_seam = false;  // SetScalarKernels(1): the f32 seam keeps exact fp32 FMA chains on CUDA cores
 
@@ -485,6 +486,7 @@ void ShahdSetDecodeChains(int chains) { g_decode_chains = chains < 0 ? 0 : chain
 
 void ShahdSetPersistentStep(int enable) { g_persistent_step = enable != 0; }
 void ShahdSetTensorCorePrefillAttention(int enable) { g_umma_prefill_attn = enable != 0; }
+void ShahdSetDecodeAttentionKernel(int mode) { g_decode_attn_kernel = mode < 0 || mode > 3 ? 0 : mode; }
 
 int ShahdDeviceErrorFlag(void) {
   int v = 0;

@@ -23,6 +23,7 @@
 #include "params.h"
 #include "prefill_attention.cuh"
 #include "prefill_attention_umma.cuh"
+#include "attn_pages.cuh"
 #include "sampling.cuh"
 #include "decode_loop.cuh"
 #include "umma_linear.cuh"
@@ -322,6 +323,29 @@ void LaunchAttnRows(int d, int G, dim3 grid, int num_sms, cudaStream_t st, const
   else (wide ? LaunchAttnRowsDW<128, 8> : LaunchAttnRowsDW<128, 4>)(G, grid, st, aa);
 }
 
+template <int D>
+void LaunchAttnPagesD(int G, dim3 grid, cudaStream_t st, const AttnArgs& aa) {
+  if (G == 1) LaunchPdl(AttnPagesKernel<D, 1>, grid, dim3(kApThreads), ApSmemBytes(D, 1), st, aa);
+  else if (G == 2) LaunchPdl(AttnPagesKernel<D, 2>, grid, dim3(kApThreads), ApSmemBytes(D, 2), st, aa);
+  else if (G <= 4) LaunchPdl(AttnPagesKernel<D, 4>, grid, dim3(kApThreads), ApSmemBytes(D, 4), st, aa);
+  else LaunchPdl(AttnPagesKernel<D, 8>, grid, dim3(kApThreads), ApSmemBytes(D, 8), st, aa);
+}
+
+// Decode-row attention streaming 64-position pages (head_dim 32, 64 or 128, G <= kMaxGroup).
+void LaunchAttnPages(int d, int G, dim3 grid, cudaStream_t st, const AttnArgs& aa) {
+  if (d == 64) LaunchAttnPagesD<64>(G, grid, st, aa);
+  else if (d == 32) LaunchAttnPagesD<32>(G, grid, st, aa);
+  else LaunchAttnPagesD<128>(G, grid, st, aa);
+}
+
+template <int D>
+bool EnsureAttnPagesAttrs() {
+  return EnsureKernelAttrs((const void*)AttnPagesKernel<D, 1>, ApSmemBytes(D, 1)) &&
+         EnsureKernelAttrs((const void*)AttnPagesKernel<D, 2>, ApSmemBytes(D, 2)) &&
+         EnsureKernelAttrs((const void*)AttnPagesKernel<D, 4>, ApSmemBytes(D, 4)) &&
+         EnsureKernelAttrs((const void*)AttnPagesKernel<D, 8>, ApSmemBytes(D, 8));
+}
+
 // A prefill-style step whose attention runs as query-block tiles (PrefillAttnKernel) rather than per row.
 bool PrefillTiled(const ShahdSession* s, const StepPlan& p) {
   return p.seq_plan != nullptr && p.plan_n > 0 && s->G <= kPfMaxG && (s->d == 32 || s->d == 64 || s->d == 128);
@@ -433,7 +457,12 @@ int EnqueueStep(ShahdSession* s, const StepPlan& p, cudaStream_t st, int r0 = 0,
       nsplit = std::max(1, std::min(s->max_blocks, CeilDiv(3 * s->num_sms / std::max(1, s->chains_hint), M * s->Hk)));
     // decode rows (one appended position per row, distinct slots): the read-ahead kernel, split only when
     // the rows and kv heads alone leave the SMs idle
-    const bool rows_kernel = p.pos_in == nullptr && s->G <= kMaxGroup && (s->d == 32 || s->d == 64 || s->d == 128);
+    // decode rows (one appended position per row): long cached lengths over a grid that fills the GPU go to
+    // the page-streaming kernel, the rest to the read-ahead rows kernel
+    const bool dec_rows = p.pos_in == nullptr && s->G <= kMaxGroup && (s->d == 32 || s->d == 64 || s->d == 128);
+    const bool long_rows = (double)p.attended >= (double)kApMinMeanLen * M && M * s->Hk >= s->num_sms;
+    const bool pages_kernel = dec_rows && (g_decode_attn_kernel == 3 || (g_decode_attn_kernel == 0 && long_rows));
+    const bool rows_kernel = dec_rows && !pages_kernel && g_decode_attn_kernel != 2;
     int rsplit = 1;
     if (r0 + M <= s->max_seqs && M * s->Hk < s->num_sms)
       rsplit = std::max(1, std::min(s->max_blocks, CeilDiv(2 * s->num_sms / std::max(1, s->chains_hint), M * s->Hk)));
@@ -452,7 +481,9 @@ int EnqueueStep(ShahdSession* s, const StepPlan& p, cudaStream_t st, int r0 = 0,
                                (float)(1.0 / std::sqrt((double)s->d)), p.seq_plan, s->max_seqs, p.plan_i0};
       const dim3 pg(p.plan_qblocks, s->Hk, p.plan_n);
       Timed(s, st, pk + kProfAttention, attn_fixed, [&] {
-        if (rows_kernel) {
+        if (pages_kernel) {
+          LaunchAttnPages(s->d, s->G, ag, st, aa);
+        } else if (rows_kernel) {
           LaunchAttnRows(s->d, s->G, dim3(rsplit, s->Hk, M), s->num_sms, st, aa);
         } else if (tiled && s->d == kFaD && g_umma_prefill_attn && s->kv_tmap_ok) {
           const FaArgs fa{s->kv_tmap, pa, s->L, CeilDiv(p.plan_qblocks * kPfQ, kFaQ)};
@@ -1426,7 +1457,8 @@ extern "C" int shahd_session_create(const ShahdModelCfg* cfg, const void* params
       !EnsureKernelAttrs((const void*)PrefillAttnKernel<32>, PrefillAttnSmem(32)) ||
       !EnsureKernelAttrs((const void*)PrefillAttnKernel<64>, PrefillAttnSmem(64)) ||
       !EnsureKernelAttrs((const void*)PrefillAttnKernel<128>, PrefillAttnSmem(128)) ||
-      !EnsureKernelAttrs((const void*)PrefillAttnUmmaKernel, kFaSmemLaunch)) {
+      !EnsureKernelAttrs((const void*)PrefillAttnUmmaKernel, kFaSmemLaunch) || !EnsureAttnPagesAttrs<32>() ||
+      !EnsureAttnPagesAttrs<64>() || !EnsureAttnPagesAttrs<128>()) {
     TakeLaunchError(nullptr);
     SetError("shahd_session_create: kernel attributes could not be set on device %d", s->device);
     return fail(SHAHD_ECUDA);

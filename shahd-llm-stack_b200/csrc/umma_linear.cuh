@@ -36,6 +36,7 @@ extern int g_umma_min_rows;
 extern int g_decode_chains;
 extern int g_persistent_step;
 extern int g_umma_prefill_attn;
+extern int g_decode_attn_kernel;
 #define kUmmaMinRows (::shahd::g_umma_min_rows)
 
 // Tile width: prefill-sized row counts take wide tiles; decode-sized ones the narrowest tile whose grid

@@ -1,4 +1,5 @@
-"""Decode-row attention launch shapes against the oracle (CachedForward.ts:76-84 per row).
+"""Decode-row attention launch shapes against the oracle (CachedForward.ts:76-84 per row), on each of the
+three decode attention kernels.
 
 The decode attention picks its launch from the step's rows and kv heads: one CTA per (row, kv head) when
 they fill the GPU, position splits merged through partials when they leave SMs idle. Each case below
@@ -22,8 +23,22 @@ CASES = [
 ]
 
 
+# 0: the automatic choice (read-ahead rows kernel at these lengths), 2: the page-ring kernel, 3: the
+# page-streaming kernel (producer warp, one page per compute warp)
+KERNELS = {"auto": 0, "page ring": 2, "page streaming": 3}
+
+
+@pytest.fixture
+def decode_attention_kernel(request):
+    lib = pkg.load()
+    lib.ShahdSetDecodeAttentionKernel(KERNELS[request.param])
+    yield request.param
+    lib.ShahdSetDecodeAttentionKernel(0)
+
+
+@pytest.mark.parametrize("decode_attention_kernel", list(KERNELS), indirect=True)
 @pytest.mark.parametrize("label,arch,rows", CASES, ids=[c[0] for c in CASES])
-def test_decode_attention_paths_match_oracle(label, arch, rows):
+def test_decode_attention_paths_match_oracle(label, arch, rows, decode_attention_kernel):
     cfg = pkg.ModelConfig(num_layers=2, block_size=128, vocab_size=256, mlp_hidden=2 * arch["embed_dim"],
                           position_scheme="Rope", norm_kind="RmsNorm", mlp_kind="SwiGlu", **arch)
     p = pkg.init_params(cfg, 11)
@@ -44,3 +59,4 @@ def test_decode_attention_paths_match_oracle(label, arch, rows):
             toks[i] = int(nxt[i])
             decs[i].push(toks[i])
     assert worst < TOL_BF16, (label, worst)
+    assert pkg.load().ShahdDeviceErrorFlag() == 0
