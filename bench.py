@@ -537,13 +537,174 @@ def run_matmul_sweep(args, rank: int) -> None:
     print(json.dumps(line), flush=True)
 
 
+FA = dict(seqs=256, heads=8, kv_heads=2, head_dim=64, prompt=512, steps=64, rope_base=10000.0, seed=3)
+
+
+def fused_attention_inputs():
+    """Q/K/V ~ N(0,1) (numpy default_rng(seed 3), fp32) for every prompt and decode position of every sequence."""
+    n, T = FA["seqs"], FA["prompt"] + FA["steps"]
+    rng = np.random.default_rng(FA["seed"])
+    q = rng.standard_normal((n, T, FA["heads"], FA["head_dim"]), dtype=np.float32)
+    k = rng.standard_normal((n, T, FA["kv_heads"], FA["head_dim"]), dtype=np.float32)
+    v = rng.standard_normal((n, T, FA["kv_heads"], FA["head_dim"]), dtype=np.float32)
+    return q, k, v
+
+
+def fused_attention_cpu(q, k, v, seqs: int, threads: int) -> dict:
+    """The oracle restatement of the reference's attention (RoPE, CausalSoftmax, @ V) on `seqs` sequences of
+    the workload, one sequence per host thread (the C oracle releases the GIL)."""
+    from concurrent.futures import ThreadPoolExecutor
+
+    from oracle import oracle as O
+
+    t0 = time.perf_counter()
+    with ThreadPoolExecutor(threads) as ex:
+        list(ex.map(lambda i: O.fused_attention(q[i], k[i], v[i], FA["rope_base"]), range(seqs)))
+    dt = time.perf_counter() - t0
+    T = FA["prompt"] + FA["steps"]
+    return {"value": seqs * T / dt, "unit": "positions/s", "cores": threads, "kind": "port", "cpu": cpu_model(),
+            "sample": f"{seqs} sequences x {T} positions (causal attention of every position = prefill + decode "
+                      f"outputs), f64, {threads} threads, {dt:.1f} s"}
+
+
+def run_fused_attention(args, rank: int, world: int, local_rank: int) -> None:
+    """FusedAttention with RoPE (base 10000) + GQA, 8 query heads over 2 kv heads, head_dim 64: causal prefill of
+    512 positions of 256 sequences, then 64 one-token decode steps (shahd_attention_prefill / _decode). A step
+    is the whole job; value = positions/s (prefill + decode). Inputs resident in HBM; e2e copies them from
+    pinned host memory and the outputs back inside the timed region. Every rank runs its own 256 sequences."""
+    import torch
+
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300))
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    pkg = package()
+    n, T, S = FA["seqs"], FA["prompt"], FA["steps"]
+    H, Hk, d = FA["heads"], FA["kv_heads"], FA["head_dim"]
+    q, k, v = fused_attention_inputs()
+    hq, hk, hv = (torch.from_numpy(x).pin_memory() for x in (q, k, v))
+    dq, dk, dv = (x.to(dev) for x in (hq, hk, hv))
+    pq, pk, pv = (x[:, :T].contiguous() for x in (dq, dk, dv))  # prefill inputs
+    sq, sk, sv = ([x[:, T + i].contiguous() for i in range(S)] for x in (dq, dk, dv))  # decode inputs
+    out_p = torch.empty((n, T, H, d), dtype=torch.float32, device=dev)
+    out_d = torch.empty((S, n, H, d), dtype=torch.float32, device=dev)
+    host_out_p = torch.empty(out_p.shape, dtype=torch.float32).pin_memory()
+    host_out_d = torch.empty(out_d.shape, dtype=torch.float32).pin_memory()
+    flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=dev)
+    stream = torch.cuda.Stream(device=dev)
+    torch.cuda.set_stream(stream)
+    op = pkg.FusedAttention(n, H, Hk, d, T + S, FA["rope_base"], device=local_rank)
+    st = stream.cuda_stream
+
+    def job(ev=None):
+        if ev:
+            ev[0].record(stream)
+        op.prefill(pq.data_ptr(), pk.data_ptr(), pv.data_ptr(), n, T, out_p.data_ptr(), st)
+        if ev:
+            ev[1].record(stream)
+        for i in range(S):
+            op.decode(sq[i].data_ptr(), sk[i].data_ptr(), sv[i].data_ptr(), n, out_d[i].data_ptr(), st)
+        if ev:
+            ev[2].record(stream)
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize(dev)
+
+    for _ in range(args.warmup):
+        job()
+    barrier()
+    clocks = ClockSampler(None) if rank == 0 else None
+    if clocks:
+        clocks.start()
+    evs = []
+    for _ in range(args.steps):
+        flush.zero_()
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+        job(ev)
+        evs.append(ev)
+    barrier()
+    clk = clocks.stop() if clocks else None
+    pre_ms = statistics.mean(e[0].elapsed_time(e[1]) for e in evs)
+    dec_ms = statistics.mean(e[1].elapsed_time(e[2]) for e in evs)
+    t = torch.tensor([pre_ms + dec_ms], dtype=torch.float64, device=dev)
+    if dist is not None:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    positions = world * n * (T + S)
+    # e2e: inputs from pinned host memory and outputs back to it, inside the timed region
+    e2e = []
+    for i in range(1 + args.steps):
+        flush.zero_()
+        torch.cuda.synchronize(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for dst, src in ((dq, hq), (dk, hk), (dv, hv)):
+            dst.copy_(src, non_blocking=True)
+        pq.copy_(dq[:, :T])
+        pk.copy_(dk[:, :T])
+        pv.copy_(dv[:, :T])
+        for j in range(S):
+            sq[j].copy_(dq[:, T + j])
+            sk[j].copy_(dk[:, T + j])
+            sv[j].copy_(dv[:, T + j])
+        job()
+        host_out_p.copy_(out_p, non_blocking=True)
+        host_out_d.copy_(out_d, non_blocking=True)
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+        if i >= 1:
+            e2e.append(e0.elapsed_time(e1))
+    op.close()
+    if dist is not None:
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    peaks, peak_kind = load_peaks()
+    pre_flops = n * 4.0 * H * d * T * (T + 1) / 2  # Q.K^T and P.V over the causal triangle
+    dec_bytes = sum(n * (2 * Hk * d * 2 * (T + i + 1) + 2 * Hk * d * 2 + 2 * H * d * 4) for i in range(S))
+    pre_tflops = pre_flops / (pre_ms / 1000.0) / 1e12
+    dec_gbs = dec_bytes / (dec_ms / 1000.0) / 1e9
+    cpu = None
+    if world == 1 and not args.skip_cpu:
+        threads = os.cpu_count() or 1
+        cpu = fused_attention_cpu(q, k, v, n, threads)
+    line = {
+        "metric": "FusedAttention (RoPE + GQA) positions/s: causal prefill 512 + 64 decode steps, 256 sequences",
+        "value": positions / (ms / 1000.0), "unit": "positions/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": "FusedAttention Hq8 Hk2 d64 RoPE10000, 256 sequences, prefill 512 + 64 decode steps",
+                   "inputs": "Q/K/V ~ N(0,1), numpy default_rng(3), fp32 in HBM; K/V cached in bf16",
+                   "l2": "flushed (512 MiB write) before every timed step"},
+        "e2e": {"value": positions / (statistics.mean(e2e) / 1000.0), "unit": "positions/s",
+                "h2d_bytes_per_step": int(q.nbytes + k.nbytes + v.nbytes),
+                "d2h_bytes_per_step": int(host_out_p.numel() * 4 + host_out_d.numel() * 4)},
+        "prefill": {"ms": pre_ms, "tflops": pre_tflops, "frac_of_bf16_peak": pre_tflops / peaks["bf16_tflops"],
+                    "flops": pre_flops},
+        "decode": {"ms_per_step": dec_ms / S, "gbs": dec_gbs, "frac_of_hbm": dec_gbs / peaks["hbm_gbs"],
+                   "bytes_per_step": dec_bytes / S},
+        "roofline": {"bound": "hbm", "achieved": dec_gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                     "frac": dec_gbs / peaks["hbm_gbs"], "traffic": None, "kernel": "decode attention (page streaming)",
+                     "peak_source": peak_kind},
+        "cpu_baseline": cpu, "clocks": clk, "gpu_launches": args.steps * (2 + 3 * S),
+    }
+    print(json.dumps(line), flush=True)
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", default="microchat", choices=sorted(WORKLOADS) + ["matmul_sweep"])
+    ap.add_argument("--workload", default="microchat", choices=sorted(WORKLOADS) + ["matmul_sweep", "fused_attention"])
     ap.add_argument("--no-extras", action="store_true",
                     help="time the steps only (no e2e, profile or CPU legs): the profiling command line")
     ap.add_argument("--chains", type=int, default=0, help="concurrent decode chains (0 = library default)")
@@ -565,6 +726,24 @@ def main() -> None:
                               "decode workloads carry it"}), flush=True)
         else:
             run_matmul_sweep(args, rank)
+    elif args.workload == "fused_attention":
+        if args.impl == "reference":
+            if rank == 0:
+                q, k, v = fused_attention_inputs()
+                threads = os.cpu_count() or 1
+                vals = [fused_attention_cpu(q, k, v, FA["seqs"], threads) for _ in range(args.steps)]
+                value = statistics.mean(x["value"] for x in vals)
+                print(json.dumps({"impl": "reference", "metric": "FusedAttention (RoPE + GQA) positions/s: causal prefill "
+                                  "512 + 64 decode steps, 256 sequences", "value": value, "unit": "positions/s",
+                                  "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
+                                  "scaling": "weak", "vs_baseline": None, "dtype": "f64", "data": "synthetic",
+                                  "config": {"workload": "FusedAttention Hq8 Hk2 d64 RoPE10000, 256 sequences, prefill "
+                                             "512 + 64 decode steps"},
+                                  "cpu_baseline": {**vals[0], "value": value},
+                                  "e2e": {"value": value, "unit": "positions/s", "h2d_bytes_per_step": 0,
+                                          "d2h_bytes_per_step": 0}}), flush=True)
+        else:
+            run_fused_attention(args, rank, world, local_rank)
     elif args.impl == "reference":
         run_reference(args, rank, world)
     else:

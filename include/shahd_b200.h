@@ -267,6 +267,27 @@ int shahd_speculative_round(const float* target_logits, const float* draft_logit
                             const ShahdSampling* opts, uint32_t* rng_states, int32_t* out_ids, int32_t* out_count,
                             int32_t* accepted);
 
+/* ---- FusedAttention operator (MultiHeadAttention.ts:46-74 attention core + AttendRow, CachedRowMath.ts:60-86) ----
+ * Causal prefill, then 1-token decode steps, on given Q, K, V over a device-resident paged cache of K (after
+ * RoPE) and V rows in bf16; fp32 softmax and accumulation. num_heads query heads over kv_heads kv heads (head
+ * h reads kv head h / (num_heads / kv_heads), at most 8 per kv head), head_dim 32, 64 or 128, up to
+ * `capacity` positions per sequence, RoPE base rope_base (<= 0: no RoPE; pairs (2i, 2i+1) rotated by
+ * position * base^(-2i/d), RotaryEmbedding.ts:17-75), scale 1/sqrt(head_dim). All Q/K/V/out pointers are
+ * fp32 device memory; calls are asynchronous on `stream` (0 = the operator's own stream). Returns a status. */
+typedef struct ShahdAttention ShahdAttention;
+int shahd_attention_create(int32_t max_seqs, int32_t num_heads, int32_t kv_heads, int32_t head_dim, int32_t capacity,
+                           double rope_base, int32_t device, ShahdAttention** out);
+int shahd_attention_destroy(ShahdAttention* a);
+/* Cached positions of sequence `slot` (-1 for a bad slot). */
+int32_t shahd_attention_length(ShahdAttention* a, int32_t slot);
+/* Sequences 0..n-1 restart at position 0: q [n, T, num_heads, d], k and v [n, T, kv_heads, d] (before RoPE);
+ * out [n, T, num_heads, d] = CausalSoftmax(scale * RoPE(Q) RoPE(K)^T) V per head (CausalSoftmax.ts:17-33). */
+int shahd_attention_prefill(ShahdAttention* a, const float* q, const float* k, const float* v, int32_t n, int32_t T,
+                            float* out, void* stream);
+/* One step for sequences 0..n-1 at their cached lengths p: q [n, num_heads, d], k and v [n, kv_heads, d] are
+ * position p's rows (before RoPE); they are appended, and out [n, num_heads, d] attends over positions 0..p. */
+int shahd_attention_decode(ShahdAttention* a, const float* q, const float* k, const float* v, int32_t n, float* out,
+                           void* stream);
 const char* shahd_last_error(void);
 
 #ifdef __cplusplus

@@ -1225,3 +1225,70 @@ int oracle_speculative_sample(const OracleModel* target, const OracleModel* draf
   free(ids); free(dl); free(tl); free(row); free(q); free(prop); free(work);
   return rc;
 }
+
+/* FusedAttention of one sequence: the attention core of MultiHeadAttention.Forward (MultiHeadAttention.ts:46-74)
+ * on given Q, K, V. ApplyRope(X, 0) (RotaryEmbedding.ts:63-75, RopeFrequencies :17-22 with base `rope_base`,
+ * none when rope_base <= 0) on Q and K at positions 0..T-1, then per query head h with kv head h / (H / Hk):
+ * CausalSoftmax(MatMulNT(Q_h, K_kv), 1/sqrt(d)) (CausalSoftmax.ts:17-33) @ V_kv. Row p of the result is also
+ * what AttendRow (CachedRowMath.ts:60-86) gives a decode step at position p over the cached rows 0..p.
+ * Layouts: q and out [T][H][d], k and v [T][Hk][d]. */
+int oracle_fused_attention(const double* q, const double* k, const double* v, int T, int H, int Hk, int d,
+                           double rope_base, double* out) {
+  if (T < 1 || H < 1 || Hk < 1 || H % Hk != 0 || d < 2 || d % 2 != 0) return Fail("oracle_fused_attention: bad shape");
+  const int G = H / Hk, half = d / 2;
+  const double scale = 1.0 / sqrt((double)d);
+  double* qr = (double*)malloc(sizeof(double) * (size_t)T * H * d);
+  double* kr = (double*)malloc(sizeof(double) * (size_t)T * Hk * d);
+  double* sc = (double*)malloc(sizeof(double) * (size_t)T);
+  if (!qr || !kr || !sc) {
+    free(qr);
+    free(kr);
+    free(sc);
+    return Fail("oracle_fused_attention: out of memory");
+  }
+  memcpy(qr, q, sizeof(double) * (size_t)T * H * d);
+  memcpy(kr, k, sizeof(double) * (size_t)T * Hk * d);
+  if (rope_base > 0) {
+    for (int t = 0; t < T; t++)
+      for (int i = 0; i < half; i++) {
+        const double ang = t * pow(rope_base, (-2.0 * i) / d);
+        const double c = cos(ang), s = sin(ang);
+        for (int h = 0; h < H + Hk; h++) {
+          double* row = h < H ? qr + ((size_t)t * H + h) * d : kr + ((size_t)t * Hk + (h - H)) * d;
+          const double x0 = row[2 * i], x1 = row[2 * i + 1];
+          row[2 * i] = x0 * c - x1 * s;
+          row[2 * i + 1] = x0 * s + x1 * c;
+        }
+      }
+  }
+  for (int h = 0; h < H; h++) {
+    const int g = h / G;
+    for (int i = 0; i < T; i++) {
+      const double* qi = qr + ((size_t)i * H + h) * d;
+      double mx = -INFINITY;
+      for (int j = 0; j <= i; j++) {
+        const double* kj = kr + ((size_t)j * Hk + g) * d;
+        double dot = 0;
+        for (int e = 0; e < d; e++) dot += qi[e] * kj[e];
+        sc[j] = dot * scale;
+        mx = fmax(mx, sc[j]);
+      }
+      double sum = 0;
+      for (int j = 0; j <= i; j++) {
+        sc[j] = exp(sc[j] - mx);
+        sum += sc[j];
+      }
+      double* o = out + ((size_t)i * H + h) * d;
+      for (int e = 0; e < d; e++) o[e] = 0;
+      for (int j = 0; j <= i; j++) {
+        const double w = sc[j] / sum;
+        const double* vj = v + ((size_t)j * Hk + g) * d;
+        for (int e = 0; e < d; e++) o[e] += w * vj[e];
+      }
+    }
+  }
+  free(qr);
+  free(kr);
+  free(sc);
+  return 0;
+}

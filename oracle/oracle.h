@@ -135,6 +135,10 @@ int oracle_speculative_sample(const OracleModel* target, const OracleModel* draf
                               int max_new, const OracleSampling* o, uint32_t* rng, int gamma, int32_t* out_ids,
                               int32_t* stats);
 
+/* FusedAttention (MultiHeadAttention.ts:46-74 core with RoPE and CausalSoftmax) of one sequence on given Q, K,
+ * V; q/out [T][H][d], k/v [T][Hk][d]; rope_base <= 0: no RoPE. Row p equals a decode step's AttendRow. */
+int oracle_fused_attention(const double* q, const double* k, const double* v, int T, int H, int Hk, int d,
+                           double rope_base, double* out);
 const char* oracle_last_error(void);
 
 #ifdef __cplusplus

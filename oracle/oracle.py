@@ -136,6 +136,7 @@ def lib() -> ctypes.CDLL:
                                                 ctypes.POINTER(OracleSampling), _up, _i32, _ip, _ip]
         L.oracle_check_trajectories.argtypes = [ctypes.c_void_p, _ip, _i32, _i32, _ip, _i32, ctypes.c_double, _i32,
                                                 _ip, _ip, _ip, _dp]
+        L.oracle_fused_attention.argtypes = [_dp, _dp, _dp, _i32, _i32, _i32, _i32, ctypes.c_double, _dp]
         L.oracle_last_error.restype = ctypes.c_char_p
         _LIB = L
     return _LIB
@@ -466,6 +467,20 @@ def speculative_sample(target: "Model", draft: "Model", prompt, max_new: int, rn
 # ---- reference C kernels (oracle/_ref) --------------------------------------------------------
 
 _REF = None
+
+
+def fused_attention(q: np.ndarray, k: np.ndarray, v: np.ndarray, rope_base: float = 10000.0) -> np.ndarray:
+    """FusedAttention of one sequence (MultiHeadAttention.ts:46-74 core: RoPE on Q and K, CausalSoftmax,
+    @ V; GQA head h reads kv head h / (H / Hk)); q [T, H, d], k and v [T, Hk, d] -> [T, H, d], f64. Row p
+    is also a decode step's AttendRow (CachedRowMath.ts:60-86) over rows 0..p."""
+    q = np.ascontiguousarray(q, dtype=np.float64)
+    k = np.ascontiguousarray(k, dtype=np.float64)
+    v = np.ascontiguousarray(v, dtype=np.float64)
+    T, H, d = q.shape
+    Hk = k.shape[1]
+    out = np.empty((T, H, d), dtype=np.float64)
+    _check(lib().oracle_fused_attention(_d(q), _d(k), _d(v), T, H, Hk, d, float(rope_base), _d(out)))
+    return out
 
 
 def ref_lib() -> ctypes.CDLL | None:

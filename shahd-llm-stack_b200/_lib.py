@@ -89,6 +89,12 @@ SIGNATURES = {
     "shahd_sample_logits": (ctypes.c_int, [_fp, _i32, _i32, ctypes.POINTER(ShahdSampling), _up, _ip]),
     "shahd_speculative_round": (ctypes.c_int, [_fp, _fp, _ip, _ip, _ip, _i32, _i32, _i32, ctypes.POINTER(ShahdSampling),
                                                 _up, _ip, _ip, _ip]),
+    "shahd_attention_create": (ctypes.c_int, [_i32, _i32, _i32, _i32, _i32, ctypes.c_double, _i32,
+                                               ctypes.POINTER(_vp)]),
+    "shahd_attention_destroy": (ctypes.c_int, [_vp]),
+    "shahd_attention_length": (_i32, [_vp, _i32]),
+    "shahd_attention_prefill": (ctypes.c_int, [_vp, _vp, _vp, _vp, _i32, _i32, _vp, _vp]),
+    "shahd_attention_decode": (ctypes.c_int, [_vp, _vp, _vp, _vp, _i32, _vp, _vp]),
     "shahd_last_error": (ctypes.c_char_p, []),
 }
 

@@ -2,6 +2,7 @@
 // g_shahd_device_error flag and one set of template instantiations.
 #include "seam.cuh"
 #include "session.cuh"
+#include "attention_op.cuh"
 
 // ---- MatMulNTF32 without device allocation ------------------------------------------------------
 // MatMulNTF32 stages its operands in a per-device workspace that it grows with cudaFree + cudaMalloc

@@ -35,6 +35,13 @@ def compute_goldens() -> dict:
         out[f"{name}_step_logits"] = logits
         sids, st = model.cached_generate(prompt, 12, temperature=0.8, top_k=20, top_p=0.9, rng_state=11)
         out[f"{name}_sampled_ids"] = np.append(sids, np.int32(st & 0x7FFFFFFF)).astype(np.int64)
+    # FusedAttention restatement (RoPE base 10000, GQA 4/2, causal), Q/K/V N(0,1) seed 3
+    rng = np.random.default_rng(3)
+    out["fa_q"] = rng.standard_normal((12, 4, 8))
+    out["fa_k"] = rng.standard_normal((12, 2, 8))
+    out["fa_v"] = rng.standard_normal((12, 2, 8))
+    out["fa_base"] = np.array(10000.0)
+    out["fa_out"] = O.fused_attention(out["fa_q"], out["fa_k"], out["fa_v"], 10000.0)
     R = O.ref_lib()
     if R is not None:
         rng = np.random.default_rng(2)
