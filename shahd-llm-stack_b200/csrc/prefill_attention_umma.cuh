@@ -6,12 +6,15 @@
 // One CTA per (128-query block, query head, sequence of the chunk); 6 warps:
 //   warps 0-3  one query row per thread (TMEM lane = row): the block's queries into shared memory as the
 //              bf16 A operand, then per 64-position page the online softmax of the row's scores, the bf16
-//              probabilities as the A operand of P.V, and the fp32 context accumulated in registers;
-//   warp 4     one thread issues the MMAs: S = Q.K^T (M 128, N 64 keys, K 64 dims) into TMEM columns 0-63,
-//              O_page = P.V (M 128, N 64 dims, K 64 keys) into columns 64-127 or 128-191 (alternating, so
-//              the softmax warps read one page's O while the next page's is computed);
+//              probabilities as the A operand of P.V (two alternating buffers, so page j's probabilities
+//              are written while page j-1's P.V still reads its own), and the fp32 context accumulated in
+//              registers;
+//   warp 4     one thread issues the MMAs: S = Q.K^T (M 128, N 64 keys, K 64 dims) into TMEM columns 0-63
+//              or 64-127 (alternating: page j+1's scores are computed while the softmax warps work on
+//              page j), O_page = P.V (M 128, N 64 dims, K 64 keys) into columns 128-191 or 192-255
+//              (alternating, so the softmax warps read one page's O while the next page's is computed);
 //   warp 5     one thread streams the kv head's K and V blocks of every page the block can see by TMA
-//              (128-byte swizzle, a 2-stage ring; this GPU's own memory, no multicast).
+//              (128-byte swizzle, a 3-stage ring; this GPU's own memory, no multicast).
 // K blocks are the K-major B operand of S; V blocks ([position][dim], dims contiguous) are the MN-major B
 // operand of P.V. Key t counts for query position q iff t <= q (CausalSoftmax). Running max and sum per row
 // in fp32 (exp of (s - max) * scale); the context is normalized once at the end.
@@ -25,22 +28,22 @@ namespace shahd {
 
 constexpr int kFaQ = 128;                        // query rows per CTA (one query head)
 constexpr int kFaD = 64;                         // head_dim served
-constexpr int kFaStages = 2;                     // K/V ring depth (pages)
+constexpr int kFaStages = 3;                     // K/V ring depth (pages)
 constexpr int kFaThreads = 192;                  // 4 softmax warps, 1 MMA warp, 1 TMA warp
-constexpr uint32_t kFaTmemCols = 256;            // S [64] + two O pages [64 each] (power of two)
+constexpr uint32_t kFaTmemCols = 256;            // two S pages + two O pages, 64 columns each
 constexpr int kFaBlock = kPageTokens * kFaD * 2;  // one K or V block of a page: 64 positions x 64 dims, bf16
 constexpr int kFaTile = kFaQ * kFaD * 2;         // the Q or P operand: 128 rows x 128 B
 
 struct FaShared {
   uint64_t kv_full[kFaStages], kv_empty[kFaStages];
-  uint64_t q_ready, s_full, p_ready, o_full;
+  uint64_t q_ready, s_full[2], p_ready, o_full[2];  // s_full[b] / o_full[b]: pages j with j & 1 == b
   uint32_t tmem;
   volatile int abort;
 };
 
-// Q | P | ring of (K, V) blocks | barriers; 1024-byte aligned base for the swizzled tiles. Sized so that at
-// most two CTAs share an SM (their TMEM allocations then always fit the SM's 512 columns).
-constexpr int kFaSmemBytes = 1024 + 2 * kFaTile + kFaStages * 2 * kFaBlock + 256;
+// Q | P[2] | ring of (K, V) blocks | barriers; 1024-byte aligned base for the swizzled tiles. Sized so that
+// at most two CTAs share an SM (their TMEM allocations then always fit the SM's 512 columns).
+constexpr int kFaSmemBytes = 1024 + 3 * kFaTile + kFaStages * 2 * kFaBlock + 256;
 constexpr int kFaSmemLaunch = kFaSmemBytes > 100 * 1024 ? kFaSmemBytes : 100 * 1024;
 
 struct FaArgs {
@@ -87,8 +90,8 @@ __global__ void __launch_bounds__(kFaThreads) PrefillAttnUmmaKernel(const __grid
   extern __shared__ uint8_t fa_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(fa_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sQ = base;
-  uint8_t* sP = base + kFaTile;
-  uint8_t* ring = base + 2 * kFaTile;  // stage s: K block at ring + 2s*kFaBlock, V block right after
+  uint8_t* sP = base + kFaTile;        // P of page j at sP + (j & 1) * kFaTile
+  uint8_t* ring = base + 3 * kFaTile;  // stage s: K block at ring + 2s*kFaBlock, V block right after
   FaShared* sh = reinterpret_cast<FaShared*>(ring + kFaStages * 2 * kFaBlock);
   const PrefillAttnArgs& a = A.a;
   GridDepWait();
@@ -109,9 +112,11 @@ __global__ void __launch_bounds__(kFaThreads) PrefillAttnUmmaKernel(const __grid
       MbarInit(&sh->kv_empty[s], 1);
     }
     MbarInit(&sh->q_ready, kFaQ);
-    MbarInit(&sh->s_full, 1);
+    MbarInit(&sh->s_full[0], 1);
+    MbarInit(&sh->s_full[1], 1);
     MbarInit(&sh->p_ready, kFaQ);
-    MbarInit(&sh->o_full, 1);
+    MbarInit(&sh->o_full[0], 1);
+    MbarInit(&sh->o_full[1], 1);
     sh->abort = 0;
     FenceMbarInit();
   }
@@ -152,36 +157,36 @@ __global__ void __launch_bounds__(kFaThreads) PrefillAttnUmmaKernel(const __grid
       const uint32_t idesc_s = UmmaIdescBf16(kFaQ, kPageTokens);
       const uint32_t idesc_pv = UmmaIdescBf16(kFaQ, kFaD) | (1u << 16);  // B (V) MN-major
       const uint64_t qdesc = SmemDescSw128(SmemAddr(sQ));
-      const uint64_t pdesc = SmemDescSw128(SmemAddr(sP));
+      const uint64_t pdesc0 = SmemDescSw128(SmemAddr(sP));
+      // S of page j into TMEM columns 64 * (j & 1), committed to s_full[j & 1]
+      auto issue_s = [&](int j) -> bool {
+        const int st = j % kFaStages;
+        if (!FaWait(sh, &sh->kv_full[st], (uint32_t)((j / kFaStages) & 1))) return false;
+        TcgenFenceAfter();
+        const uint64_t kdesc = SmemDescSw128(SmemAddr(ring + (size_t)st * 2 * kFaBlock));
+        for (int kk = 0; kk < kFaD / 16; kk++)
+          UmmaBf16(tmem + 64u * (uint32_t)(j & 1), qdesc + (uint64_t)(2 * kk), kdesc + (uint64_t)(2 * kk), idesc_s,
+                   kk > 0 ? 1u : 0u);
+        UmmaCommit(&sh->s_full[j & 1]);
+        return true;
+      };
       bool ok = FaWait(sh, &sh->q_ready, 0);
       TcgenFenceAfter();
-      if (ok && FaWait(sh, &sh->kv_full[0], 0)) {
+      ok = ok && issue_s(0) && (npages < 2 || issue_s(1));
+      for (int j = 0; j < npages && ok; j++) {
+        const int st = j % kFaStages;
+        if (!FaWait(sh, &sh->p_ready, (uint32_t)(j & 1))) break;
         TcgenFenceAfter();
-        const uint64_t kdesc = SmemDescSw128(SmemAddr(ring));
-        for (int kk = 0; kk < kFaD / 16; kk++)
-          UmmaBf16(tmem, qdesc + (uint64_t)(2 * kk), kdesc + (uint64_t)(2 * kk), idesc_s, kk > 0 ? 1u : 0u);
-        UmmaCommit(&sh->s_full);
-        for (int j = 0; j < npages; j++) {
-          const int st = j % kFaStages;
-          if (!FaWait(sh, &sh->p_ready, (uint32_t)(j & 1))) break;
-          TcgenFenceAfter();
-          const uint64_t vdesc = SmemDescSw128Mn(SmemAddr(ring + (size_t)st * 2 * kFaBlock + kFaBlock));
-          const uint32_t ocol = tmem + 64u + 64u * (uint32_t)(j & 1);
-          for (int kk = 0; kk < kPageTokens / 16; kk++)  // 16 keys = two 8-row groups of V per step
-            UmmaBf16(ocol, pdesc + (uint64_t)(2 * kk), vdesc + (uint64_t)(kk * (2048 >> 4)), idesc_pv,
-                     kk > 0 ? 1u : 0u);
-          UmmaCommit(&sh->o_full);
-          UmmaCommit(&sh->kv_empty[st]);
-          if (j + 1 < npages) {
-            const int s1 = (j + 1) % kFaStages;
-            if (!FaWait(sh, &sh->kv_full[s1], (uint32_t)(((j + 1) / kFaStages) & 1))) break;
-            TcgenFenceAfter();
-            const uint64_t kdesc1 = SmemDescSw128(SmemAddr(ring + (size_t)s1 * 2 * kFaBlock));
-            for (int kk = 0; kk < kFaD / 16; kk++)
-              UmmaBf16(tmem, qdesc + (uint64_t)(2 * kk), kdesc1 + (uint64_t)(2 * kk), idesc_s, kk > 0 ? 1u : 0u);
-            UmmaCommit(&sh->s_full);
-          }
-        }
+        const uint64_t vdesc = SmemDescSw128Mn(SmemAddr(ring + (size_t)st * 2 * kFaBlock + kFaBlock));
+        const uint32_t ocol = tmem + 128u + 64u * (uint32_t)(j & 1);
+        const uint64_t pdesc = pdesc0 + (uint64_t)((j & 1) * (kFaTile >> 4));
+        for (int kk = 0; kk < kPageTokens / 16; kk++)  // 16 keys = two 8-row groups of V per step
+          UmmaBf16(ocol, pdesc + (uint64_t)(2 * kk), vdesc + (uint64_t)(kk * (2048 >> 4)), idesc_pv,
+                   kk > 0 ? 1u : 0u);
+        UmmaCommit(&sh->o_full[j & 1]);
+        UmmaCommit(&sh->kv_empty[st]);
+        // the softmax warps have read page j's scores (p_ready): its S columns take page j + 2
+        if (j + 2 < npages) ok = issue_s(j + 2);
       }
     }
   } else {  // softmax warps: thread = query row = TMEM lane
@@ -215,12 +220,13 @@ __global__ void __launch_bounds__(kFaThreads) PrefillAttnUmmaKernel(const __grid
     float m = -INFINITY, l = 0.f, alpha_prev = 0.f;
     bool ok = true;
     for (int j = 0; j < npages && ok; j++) {
-      ok = FaWait(sh, &sh->s_full, (uint32_t)(j & 1));
+      ok = FaWait(sh, &sh->s_full[j & 1], (uint32_t)((j >> 1) & 1));
       if (!ok) break;
       TcgenFenceAfter();
       uint32_t u[kPageTokens];
-      TmemLoad32(lane_base, u);
-      TmemLoad32(lane_base + 32u, u + 32);
+      const uint32_t scol = lane_base + 64u * (uint32_t)(j & 1);
+      TmemLoad32(scol, u);
+      TmemLoad32(scol + 32u, u + 32);
       TmemWaitLd();
       float p[kPageTokens];
       float mx = m;
@@ -239,19 +245,23 @@ __global__ void __launch_bounds__(kFaThreads) PrefillAttnUmmaKernel(const __grid
       }
       l = l * alpha + rs;
       m = mx;
-      // P.V of the previous page has finished reading sP once its O page is complete
-      if (j > 0) {
-        ok = FaWait(sh, &sh->o_full, (uint32_t)((j - 1) & 1));
-        if (!ok) break;
-        TcgenFenceAfter();
-      }
+      // P buffer j & 1 was last read by page j-2's P.V, whose completion this thread saw at page j-1
 #pragma unroll
-      for (int c = 0; c < 8; c++) StoreNbf<8>(reinterpret_cast<bf16*>(sP + Sw128Offset(qi, c)), p + 8 * c);
+      for (int c = 0; c < 8; c++)
+        StoreNbf<8>(reinterpret_cast<bf16*>(sP + (j & 1) * kFaTile + Sw128Offset(qi, c)), p + 8 * c);
       FenceProxyAsyncShared();
+      // page j-1's P.V complete: every thread has arrived for page j-1, so this thread's arrival below
+      // counts toward page j's phase of p_ready (a thread running a page ahead would complete the wrong
+      // phase), and its O page may be read
+      if (j > 0) {
+        ok = FaWait(sh, &sh->o_full[(j - 1) & 1], (uint32_t)(((j - 1) >> 1) & 1));
+        if (!ok) break;
+      }
       TcgenFenceBefore();
       MbarArrive(&sh->p_ready);
       if (j > 0) {  // o = o * alpha(j-1) + O_page(j-1) (the current page's P.V writes the other O buffer)
-        const uint32_t ocol = lane_base + 64u + 64u * (uint32_t)((j - 1) & 1);
+        TcgenFenceAfter();
+        const uint32_t ocol = lane_base + 128u + 64u * (uint32_t)((j - 1) & 1);
         TmemLoad32(ocol, u);
         TmemLoad32(ocol + 32u, u + 32);
         TmemWaitLd();
@@ -260,10 +270,10 @@ __global__ void __launch_bounds__(kFaThreads) PrefillAttnUmmaKernel(const __grid
       }
       alpha_prev = alpha;
     }
-    if (ok && FaWait(sh, &sh->o_full, (uint32_t)((npages - 1) & 1))) {
+    if (ok && FaWait(sh, &sh->o_full[(npages - 1) & 1], (uint32_t)(((npages - 1) >> 1) & 1))) {
       TcgenFenceAfter();
       uint32_t u[kFaD];
-      const uint32_t ocol = lane_base + 64u + 64u * (uint32_t)((npages - 1) & 1);
+      const uint32_t ocol = lane_base + 128u + 64u * (uint32_t)((npages - 1) & 1);
       TmemLoad32(ocol, u);
       TmemLoad32(ocol + 32u, u + 32);
       TmemWaitLd();
