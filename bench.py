@@ -287,6 +287,8 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
         lib.ShahdSetDecodeChains(args.chains)
     if args.tc_min_rows:
         lib.ShahdSetTensorCoreMinRows(args.tc_min_rows)
+    if args.fused_block >= 0:
+        lib.ShahdSetFusedAttentionBlock(args.fused_block)
     # a KV pool of the job's size: every sequence's pages up to prompt + new positions (Phase2Modern-style:
     # 4096 x 16 pages of 1 MiB = 64 GiB on one GPU)
     kv_pages = w.seqs * -(-min(w.prompt_len + w.new_tokens, cfg.block_size) // 64)
@@ -345,7 +347,8 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
             dist.destroy_process_group()
         if rank == 0:
             print(json.dumps({"ms_per_step": ms_per_step, "value": value, "gpu_launches": int(launches),
-                              "chains": args.chains, "tc_min_rows": args.tc_min_rows}), flush=True)
+                              "chains": args.chains, "tc_min_rows": args.tc_min_rows,
+                              "fused_block": args.fused_block}), flush=True)
         return
 
     # gather per-rank output checksums (the only collective, outside the timed region)
@@ -709,6 +712,9 @@ def main() -> None:
                     help="time the steps only (no e2e, profile or CPU legs): the profiling command line")
     ap.add_argument("--chains", type=int, default=0, help="concurrent decode chains (0 = library default)")
     ap.add_argument("--tc-min-rows", type=int, default=0, help="rows from which projections use tensor cores (0 = default)")
+    ap.add_argument("--fused-block", type=int, default=-1, choices=[-1, 0, 1],
+                    help="decode rows run the fused attention block where the model fits it (1) or the three-launch "
+                         "chain (0); -1 keeps the library default")
     ap.add_argument("--new-tokens", type=int, default=None,
                     help="override the workload's new tokens per sequence (small ncu captures only)")
     ap.add_argument("--seqs", type=int, default=None,

@@ -94,6 +94,13 @@ void ShahdSetTensorCorePrefillAttention(int enable);
  * copies into a six-page ring, one page per compute warp, no block-wide barrier per page). Results agree
  * within the parity tolerance. Process-wide tuning hook; no counterpart in the reference. */
 void ShahdSetDecodeAttentionKernel(int mode);
+/* Fused decode attention block: for decode rows whose rows x kv heads fill the SMs, and models whose Q/K/V
+ * rows of one kv head fit in shared memory twice per SM (head_dim 32 or 64, <= 4 query heads per kv head,
+ * embedding width <= 512), 1 runs norm + Q/K/V projection + RoPE + KV append + attention + output projection
+ * + residual in one launch per layer; 0 (the default) keeps the three-launch chain (QKV projection,
+ * attention, O projection). Results agree within the parity tolerance. Process-wide tuning hook; no
+ * counterpart in the reference. */
+void ShahdSetFusedAttentionBlock(int enable);
 /* First error code a kernel recorded for a bounded device-side wait that gave up (0 = none). */
 int ShahdDeviceErrorFlag(void);
 /* Device-pointer MatMulNT on the tensor cores: out[M,N] (+)= a[M,K] @ btᵀ with a, bt bf16 row-major

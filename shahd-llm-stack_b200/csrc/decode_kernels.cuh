@@ -635,6 +635,13 @@ __device__ __forceinline__ void BulkCopyG2S(void* dst, const void* src, uint32_t
                : "memory");
 }
 
+// Ampere-style 16-byte asynchronous copy global -> shared (both addresses 16-byte aligned), L2 only.
+__device__ __forceinline__ void CpAsync16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(SmemAddr(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void CpAsyncCommit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void CpAsyncWaitAll() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
 __host__ __device__ constexpr int AttnSmemBytes(int D) { return kAttnRing * 2 * kPageTokens * D * 2; }
 
 // Fast path: head_dim D (multiple of 8, 32..128) known at compile time. Dynamic shared memory holds the

@@ -2,6 +2,7 @@
 // and the device-pointer bf16 MatMulNT on the tensor cores.
 #include <cstdarg>
 #include <cstring>
+#include <map>
 #include <mutex>
 #include <set>
 #include <string>
@@ -20,6 +21,7 @@ int g_decode_chains = 0;  // 0 = automatic
 int g_umma_prefill_attn = 1;
 int g_decode_attn_kernel = 0;  // decode-row attention: 0 automatic, 1 read-ahead rows, 2 page ring, 3 page streaming  // causal prefill attention of head_dim 64 on the tensor cores
 int g_persistent_step = 0;  // 1: greedy generate runs its decode steps in the persistent cluster loop
+int g_fused_attn_block = 0;  // decode rows: norm + QKV + RoPE + attention + O projection in one launch where it fits
 bool g_scalar_seam = false;  // SetScalarKernels(1): the f32 seam keeps exact fp32 FMA chains on CUDA cores
 
 // ---- thread-local last error --------------------------------------------------------------------
@@ -44,24 +46,34 @@ cudaError_t TakeLaunchError(std::string* what) {
 }
 
 bool EnsureKernelAttrs(const void* fn, int smem_bytes, bool nonportable_cluster) {
+  // The dynamic shared memory attribute is an upper limit: per (device, kernel) it only ever grows to the
+  // largest request seen, so a kernel whose shared memory depends on the model shape keeps working for every
+  // session after a smaller one (setting it back down would fail the larger session's launches).
   static std::mutex mu;
-  static std::set<std::tuple<int, const void*, int, bool>> done;
+  static std::map<std::pair<int, const void*>, int> smem_set;
+  static std::set<std::pair<int, const void*>> nonportable_set;
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) {
     NoteLaunchError(cudaErrorInvalidDevice, "cudaGetDevice before setting kernel attributes");
     return false;
   }
-  const auto key = std::make_tuple(dev, fn, smem_bytes, nonportable_cluster);
+  const auto key = std::make_pair(dev, fn);
   std::lock_guard<std::mutex> g(mu);
-  if (done.count(key)) return true;
-  cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes);
-  if (e == cudaSuccess && nonportable_cluster) e = cudaFuncSetAttribute(fn, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+  cudaError_t e = cudaSuccess;
+  auto it = smem_set.find(key);
+  if (it == smem_set.end() || it->second < smem_bytes) {
+    e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes);
+    if (e == cudaSuccess) smem_set[key] = smem_bytes;
+  }
+  if (e == cudaSuccess && nonportable_cluster && !nonportable_set.count(key)) {
+    e = cudaFuncSetAttribute(fn, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+    if (e == cudaSuccess) nonportable_set.insert(key);
+  }
   if (e != cudaSuccess) {
     cudaGetLastError();
     NoteLaunchError(e, "cudaFuncSetAttribute");
     return false;
   }
-  done.insert(key);
   return true;
 }
 
@@ -487,6 +499,7 @@ void ShahdSetDecodeChains(int chains) { g_decode_chains = chains < 0 ? 0 : chain
 void ShahdSetPersistentStep(int enable) { g_persistent_step = enable != 0; }
 void ShahdSetTensorCorePrefillAttention(int enable) { g_umma_prefill_attn = enable != 0; }
 void ShahdSetDecodeAttentionKernel(int mode) { g_decode_attn_kernel = mode < 0 || mode > 3 ? 0 : mode; }
+void ShahdSetFusedAttentionBlock(int enable) { g_fused_attn_block = enable != 0; }
 
 int ShahdDeviceErrorFlag(void) {
   int v = 0;

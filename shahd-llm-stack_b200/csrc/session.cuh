@@ -24,6 +24,7 @@
 #include "prefill_attention.cuh"
 #include "prefill_attention_umma.cuh"
 #include "attn_pages.cuh"
+#include "attn_block.cuh"
 #include "sampling.cuh"
 #include "decode_loop.cuh"
 #include "umma_linear.cuh"
@@ -113,6 +114,7 @@ struct ShahdSession {
   int am_stride;
   float *part_o, *part_m, *part_l;
   int* attn_counter;
+  bool ab_ok = false;  // the model's shape fits the fused attention block (one kv head's weights next to a second CTA)
   // persistent cluster decode loop: weight tensor maps (box 64 x 128) and per-layer constants in device memory
   int loop_state = -1;  // -1 not set up yet, 0 unavailable for this model/device, 1 ready
   shahd::LoopLayer* d_loop_layers = nullptr;
@@ -399,6 +401,22 @@ bool EmbedsNext(const StepPlan& p) {
   return p.finish && p.head && p.cur_tok != nullptr && p.out_ids != nullptr;
 }
 
+// Position splits per (decode row, kv head) of the read-ahead rows kernel: enough CTAs to fill the GPU when
+// the rows and kv heads alone leave SMs idle, one split otherwise (and beyond max_seqs rows).
+int RowSplits(const ShahdSession* s, int M, int r0) {
+  if (r0 + M <= s->max_seqs && M * s->Hk < s->num_sms)
+    return std::max(1, std::min(s->max_blocks, CeilDiv(2 * s->num_sms / std::max(1, s->chains_hint), M * s->Hk)));
+  return 1;
+}
+
+// Whether a decode step of M rows (rows [r0, r0 + M)) runs the fused attention block: it is switched on, the
+// model fits it, the rows and kv heads fill the SMs with one CTA each, and the decode attention kernel is left
+// automatic (or set to the read-ahead rows kernel, whose task layout the block shares).
+bool UsesFusedBlock(const ShahdSession* s, int M, int r0) {
+  return s->ab_ok && g_fused_attn_block && g_decode_attn_kernel <= 1 && r0 + M <= s->max_seqs &&
+         RowSplits(s, M, r0) == 1;
+}
+
 // Enqueue one batched cached step (AdvanceOneToken + HeadLogitsRow for M rows) on `st`; returns the
 // number of kernels it launched.
 int EnqueueStep(ShahdSession* s, const StepPlan& p, cudaStream_t st, int r0 = 0, int chain = 0) {
@@ -463,46 +481,60 @@ int EnqueueStep(ShahdSession* s, const StepPlan& p, cudaStream_t st, int r0 = 0,
     const bool long_rows = (double)p.attended >= (double)kApMinMeanLen * M && M * s->Hk >= s->num_sms;
     const bool pages_kernel = dec_rows && (g_decode_attn_kernel == 3 || (g_decode_attn_kernel == 0 && long_rows));
     const bool rows_kernel = dec_rows && !pages_kernel && g_decode_attn_kernel != 2;
-    int rsplit = 1;
-    if (r0 + M <= s->max_seqs && M * s->Hk < s->num_sms)
-      rsplit = std::max(1, std::min(s->max_blocks, CeilDiv(2 * s->num_sms / std::max(1, s->chains_hint), M * s->Hk)));
+    const int rsplit = RowSplits(s, M, r0);
+    // decode rows that fill the SMs without position splits (any cached length): the attention half of each
+    // layer in one launch
+    const bool fused_block = dec_rows && UsesFusedBlock(s, M, r0);
     for (int l = 0; l < s->L; l++) {
       const Layer& Ly = s->layers[l];
-      // norm1 + QKV + RoPE + KV append (CachedForward.ts:66-73, :78-79)
-      const LinearArgs la = Lin(x, s->E, xb, s->Ep, R, M, s->E, s->Ep, Ly.w_qkv, s->Nqkv, eps, Ly.qkv_c1, Ly.qkv_c2);
-      const EpiQKV eq{q, kv, l, pos, p.slot, s->rope_cos, s->rope_sin, s->H, s->Hk, s->d};
-      Timed(s, st, pk + kProfLinear, LinearBytes(M, s->E, s->Ep, s->Nqkv), [&] { LaunchLinear(norm, la, eq, st); });
-      // attention over the cache (CachedForward.ts:76-80)
-      AttnArgs aa{q, ctx_f32, ctxb, s->HDp, kv, l, pos, p.slot, s->H, s->Hk, s->G, s->d,
-                  (float)(1.0 / std::sqrt((double)s->d)), s->max_blocks, part_o, part_m, part_l, counter};
-      dim3 ag(nsplit, s->Hk, M);
-      const bool tiled = PrefillTiled(s, p);
-      const PrefillAttnArgs pa{q, ctx_f32, ctxb, s->HDp, kv, l, s->H, s->Hk, s->G,
-                               (float)(1.0 / std::sqrt((double)s->d)), p.seq_plan, s->max_seqs, p.plan_i0};
-      const dim3 pg(p.plan_qblocks, s->Hk, p.plan_n);
-      Timed(s, st, pk + kProfAttention, attn_fixed, [&] {
-        if (pages_kernel) {
-          LaunchAttnPages(s->d, s->G, ag, st, aa);
-        } else if (rows_kernel) {
-          LaunchAttnRows(s->d, s->G, dim3(rsplit, s->Hk, M), s->num_sms, st, aa);
-        } else if (tiled && s->d == kFaD && g_umma_prefill_attn && s->kv_tmap_ok) {
-          const FaArgs fa{s->kv_tmap, pa, s->L, CeilDiv(p.plan_qblocks * kPfQ, kFaQ)};
-          LaunchPdl(PrefillAttnUmmaKernel, dim3(fa.qblocks, s->H, p.plan_n), dim3(kFaThreads), kFaSmemLaunch, st, fa);
-        } else if (tiled) {
-          if (s->d == 64) LaunchPdl(PrefillAttnKernel<64>, pg, dim3(kPfThreads), PrefillAttnSmem(64), st, pa);
-          else if (s->d == 32) LaunchPdl(PrefillAttnKernel<32>, pg, dim3(kPfThreads), PrefillAttnSmem(32), st, pa);
-          else LaunchPdl(PrefillAttnKernel<128>, pg, dim3(kPfThreads), PrefillAttnSmem(128), st, pa);
-        } else if (s->d == 64) LaunchPdl(AttnDecodeKernel<64>, ag, dim3(kAttnThreads), AttnSmemBytes(64), st, aa);
-        else if (s->d == 32) LaunchPdl(AttnDecodeKernel<32>, ag, dim3(kAttnThreads), AttnSmemBytes(32), st, aa);
-        else if (s->d == 128) LaunchPdl(AttnDecodeKernel<128>, ag, dim3(kAttnThreads), AttnSmemBytes(128), st, aa);
-        else LaunchPdl(AttnDecodeGenericKernel, ag, dim3(kAttnThreads), 0, st, aa);
-      }, attn_per_pos, AttendedPositions(s, p), chain);
-      // summed per-head Wo + residual (CachedForward.ts:81-84)
-      LinearArgs lo = Lin(ctx, hd, ctxb, s->HDp, R, M, hd, s->HDp, Ly.w_o, s->E, eps, nullptr, nullptr);
-      lo.ws = split_ws;
-      lo.ws_cnt = split_cnt;
-      Timed(s, st, pk + kProfLinear, LinearBytes(M, hd, s->HDp, s->E),
-            [&] { LaunchLinear(kNormNone, lo, EpiResid{x, xb, s->E, s->Ep, nullptr}, st); });
+      if (fused_block) {
+        // norm1 + QKV + RoPE + KV append + attention + summed per-head Wo + residual (CachedForward.ts:66-84).
+        // Layer 0 follows the embed / finish kernel, which writes the rows' positions: it reads them (and the
+        // cached rows) after the grid-dependency wait; later layers follow the MLP and read ahead.
+        const AttnBlockArgs ab{x, xb, s->E, s->Ep, s->Ep, Ly.qkv_c1, Ly.qkv_c2, norm, eps, Ly.w_o, s->HDp,
+                               s->rope_cos, s->rope_sin, kv, l, pos, p.slot, s->H, s->Hk, s->G,
+                               (float)(1.0 / std::sqrt((double)s->d)), l > 0 ? 1 : 0};
+        const double wbytes = LinearBytes(M, s->E, s->Ep, s->Nqkv) + LinearBytes(M, hd, s->HDp, s->E);
+        Timed(s, st, pk + kProfAttention, attn_fixed + wbytes,
+              [&] { LaunchAttnBlock(s->d, ab, Ly.w_qkv, s->Nqkv, M, st); }, attn_per_pos, AttendedPositions(s, p),
+              chain);
+      } else {
+        // norm1 + QKV + RoPE + KV append (CachedForward.ts:66-73, :78-79)
+        const LinearArgs la = Lin(x, s->E, xb, s->Ep, R, M, s->E, s->Ep, Ly.w_qkv, s->Nqkv, eps, Ly.qkv_c1, Ly.qkv_c2);
+        const EpiQKV eq{q, kv, l, pos, p.slot, s->rope_cos, s->rope_sin, s->H, s->Hk, s->d};
+        Timed(s, st, pk + kProfLinear, LinearBytes(M, s->E, s->Ep, s->Nqkv), [&] { LaunchLinear(norm, la, eq, st); });
+        // attention over the cache (CachedForward.ts:76-80)
+        AttnArgs aa{q, ctx_f32, ctxb, s->HDp, kv, l, pos, p.slot, s->H, s->Hk, s->G, s->d,
+                    (float)(1.0 / std::sqrt((double)s->d)), s->max_blocks, part_o, part_m, part_l, counter};
+        dim3 ag(nsplit, s->Hk, M);
+        const bool tiled = PrefillTiled(s, p);
+        const PrefillAttnArgs pa{q, ctx_f32, ctxb, s->HDp, kv, l, s->H, s->Hk, s->G,
+                                 (float)(1.0 / std::sqrt((double)s->d)), p.seq_plan, s->max_seqs, p.plan_i0};
+        const dim3 pg(p.plan_qblocks, s->Hk, p.plan_n);
+        Timed(s, st, pk + kProfAttention, attn_fixed, [&] {
+          if (pages_kernel) {
+            LaunchAttnPages(s->d, s->G, ag, st, aa);
+          } else if (rows_kernel) {
+            LaunchAttnRows(s->d, s->G, dim3(rsplit, s->Hk, M), s->num_sms, st, aa);
+          } else if (tiled && s->d == kFaD && g_umma_prefill_attn && s->kv_tmap_ok) {
+            const FaArgs fa{s->kv_tmap, pa, s->L, CeilDiv(p.plan_qblocks * kPfQ, kFaQ)};
+            LaunchPdl(PrefillAttnUmmaKernel, dim3(fa.qblocks, s->H, p.plan_n), dim3(kFaThreads), kFaSmemLaunch, st, fa);
+          } else if (tiled) {
+            if (s->d == 64) LaunchPdl(PrefillAttnKernel<64>, pg, dim3(kPfThreads), PrefillAttnSmem(64), st, pa);
+            else if (s->d == 32) LaunchPdl(PrefillAttnKernel<32>, pg, dim3(kPfThreads), PrefillAttnSmem(32), st, pa);
+            else LaunchPdl(PrefillAttnKernel<128>, pg, dim3(kPfThreads), PrefillAttnSmem(128), st, pa);
+          } else if (s->d == 64) LaunchPdl(AttnDecodeKernel<64>, ag, dim3(kAttnThreads), AttnSmemBytes(64), st, aa);
+          else if (s->d == 32) LaunchPdl(AttnDecodeKernel<32>, ag, dim3(kAttnThreads), AttnSmemBytes(32), st, aa);
+          else if (s->d == 128) LaunchPdl(AttnDecodeKernel<128>, ag, dim3(kAttnThreads), AttnSmemBytes(128), st, aa);
+          else LaunchPdl(AttnDecodeGenericKernel, ag, dim3(kAttnThreads), 0, st, aa);
+        }, attn_per_pos, AttendedPositions(s, p), chain);
+        // summed per-head Wo + residual (CachedForward.ts:81-84)
+        LinearArgs lo = Lin(ctx, hd, ctxb, s->HDp, R, M, hd, s->HDp, Ly.w_o, s->E, eps, nullptr, nullptr);
+        lo.ws = split_ws;
+        lo.ws_cnt = split_cnt;
+        Timed(s, st, pk + kProfLinear, LinearBytes(M, hd, s->HDp, s->E),
+              [&] { LaunchLinear(kNormNone, lo, EpiResid{x, xb, s->E, s->Ep, nullptr}, st); });
+      }
       // norm2 + MLP + residual (CachedForward.ts:86-87)
       const LinearArgs lu = Lin(x, s->E, xb, s->Ep, R, M, s->E, s->Ep, Ly.w_up, s->Nup, eps, Ly.up_c1, Ly.up_c2);
       Timed(s, st, pk + kProfLinear, LinearBytes(M, s->E, s->Ep, s->Nup), [&] {
@@ -1464,6 +1496,8 @@ extern "C" int shahd_session_create(const ShahdModelCfg* cfg, const void* params
     return fail(SHAHD_ECUDA);
   }
   cudaMemset(s->attn_counter, 0, sizeof(int) * (size_t)R * s->Hk);
+  s->ab_ok = AttnBlockFits(s->d, s->G, s->Hk, s->E, s->Ep) && EnsureAttnBlockAttrs(s->d, s->G, s->Ep);
+  TakeLaunchError(nullptr);
   cudaMemset(s->d_seq_len, 0, sizeof(int) * R);
   if (cudaDeviceSynchronize() != cudaSuccess) {
     SetError("shahd_session_create: device error during setup");
@@ -1771,8 +1805,8 @@ extern "C" int shahd_sync(ShahdSession* s) {
 
 extern "C" int32_t shahd_step_launches(ShahdSession* s, int32_t n) {
   if (!s) return -1;
-  (void)n;
-  return 1 + 5 * s->L + 2;  // embed + per layer (QKV, attention, O, up, down) + head + finish
+  // embed + per layer (QKV, attention, O, up, down | fused attention block, up, down) + head + finish
+  return 1 + (UsesFusedBlock(s, n, 0) ? 3 : 5) * s->L + 2;
 }
 
 extern "C" int shahd_profile(ShahdSession* s, int32_t enable) {
