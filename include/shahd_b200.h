@@ -101,6 +101,11 @@ void ShahdSetDecodeAttentionKernel(int mode);
  * attention, O projection). Results agree within the parity tolerance. Process-wide tuning hook; no
  * counterpart in the reference. */
 void ShahdSetFusedAttentionBlock(int enable);
+/* Batched-prefill projections (more than 128 rows): 1 (the default) runs them on the persistent
+ * warp-specialized tcgen05 kernel (TMA warp, MMA warp, eight epilogue warps, two TMEM accumulators, 128 x 256
+ * or 128 x 128 tiles) after a per-row norm-statistics pass; 0 keeps one 128 x 128 tile per CTA. Results agree
+ * within the parity tolerance. Process-wide tuning hook; no counterpart in the reference. */
+void ShahdSetPersistentPrefillProjections(int enable);
 /* First error code a kernel recorded for a bounded device-side wait that gave up (0 = none). */
 int ShahdDeviceErrorFlag(void);
 /* Device-pointer MatMulNT on the tensor cores: out[M,N] (+)= a[M,K] @ btᵀ with a, bt bf16 row-major

@@ -65,6 +65,7 @@ SIGNATURES = {
     "ShahdSetTensorCorePrefillAttention": (None, [ctypes.c_int]),
     "ShahdSetDecodeAttentionKernel": (None, [ctypes.c_int]),
     "ShahdSetFusedAttentionBlock": (None, [ctypes.c_int]),
+    "ShahdSetPersistentPrefillProjections": (None, [ctypes.c_int]),
     "ShahdMatMulNTBF16Device": (ctypes.c_int, [_vp, _vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, _vp]),
     "ShahdMatMulNTF32Device": (ctypes.c_int, [_vp, _vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, _vp]),
     "ShahdMatMulNTF32NoAlloc": (ctypes.c_int, [_fp, _fp, _fp, _i32, _i32, _i32, _i32]),

@@ -367,6 +367,7 @@ struct LinearArgs {
   float* ws;        // split-K partial tiles (tensor-core path, no norm), or nullptr: no split
   int* ws_cnt;      // [N tiles] arrival counters, zero between launches
   int kcluster;     // the split-K CTAs of a tile form a cluster and sum their partials in shared memory
+  const float* stats;  // [M][2] norm statistics (mean, 1/std) of the rows (persistent prefill kernel), or nullptr
 };
 
 // ---- SIMT linear (GEMV regime, few rows): out[m, n] = sum_k xhat[m, k] * W'[n, k] -------------------

@@ -95,7 +95,6 @@ __global__ void __launch_bounds__(kFaThreads) PrefillAttnUmmaKernel(const __grid
   FaShared* sh = reinterpret_cast<FaShared*>(ring + kFaStages * 2 * kFaBlock);
   const PrefillAttnArgs& a = A.a;
   GridDepWait();
-  GridDepLaunch();
   const int R = a.plan_stride, e = a.i0 + blockIdx.z;
   const int slot = a.plan[e], len = a.plan[2 * R + e], basepos = a.plan[4 * R + e];
   const int row0 = a.plan[3 * R + e] - a.plan[3 * R + a.i0];  // the sequence's first row in the chunk
@@ -128,6 +127,9 @@ __global__ void __launch_bounds__(kFaThreads) PrefillAttnUmmaKernel(const __grid
   __syncthreads();
   TcgenFenceAfter();
   const uint32_t tmem = sh->tmem;
+  // dependents may be scheduled only once this CTA holds its TMEM: a dependent CTA that took the SM's
+  // columns first would wait for this grid while this CTA waited for its columns
+  GridDepLaunch();
 
   if (warp == 5) {
     if (lane == 0) {  // TMA producer: K and V blocks of pages 0 .. npages-1

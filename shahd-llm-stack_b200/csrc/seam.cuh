@@ -10,6 +10,7 @@
 
 #include "../../include/shahd_b200.h"
 #include "common.cuh"
+#include "gemm_persist.cuh"
 #include "gemm_tf32.cuh"
 #include "umma_linear.cuh"
 
@@ -21,7 +22,8 @@ int g_decode_chains = 0;  // 0 = automatic
 int g_umma_prefill_attn = 1;
 int g_decode_attn_kernel = 0;  // decode-row attention: 0 automatic, 1 read-ahead rows, 2 page ring, 3 page streaming  // causal prefill attention of head_dim 64 on the tensor cores
 int g_persistent_step = 0;  // 1: greedy generate runs its decode steps in the persistent cluster loop
-int g_fused_attn_block = 0;  // decode rows: norm + QKV + RoPE + attention + O projection in one launch where it fits
+int g_fused_attn_block = 0;
+int g_persist_linear = 1;  // batched prefill projections on the persistent warp-specialized tcgen05 kernel  // decode rows: norm + QKV + RoPE + attention + O projection in one launch where it fits
 bool g_scalar_seam = false;  // SetScalarKernels(1): the f32 seam keeps exact fp32 FMA chains on CUDA cores
 
 // ---- thread-local last error --------------------------------------------------------------------
@@ -266,153 +268,8 @@ static void RunSeam(const char* op, Layout lay, const T* a, const T* b, T* out, 
   if (e != cudaSuccess) SetError("%s: device error: %s", op, cudaGetErrorString(e));
 }
 
-// ---- tcgen05 GEMM, both operands by TMA, warp-specialized, persistent ---------------------------
-
-constexpr int kGemmBN = 128;
-constexpr int kGemmStages = 4;
-constexpr int kGemmThreads = 192;  // warp 0 TMA, warp 1 MMA, warps 2..5 epilogue
-constexpr int kGemmStageBytes = (kUmmaBM + kGemmBN) * kUmmaBK * 2;
-constexpr int kGemmSmem = kGemmStages * kGemmStageBytes + 1024 + 256;
-
-__global__ void __launch_bounds__(kGemmThreads, 1)
-    GemmNtBf16Kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tb, float* out, int M,
-                     int N, int K, int acc) {
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kGemmStages * kGemmStageBytes);
-  uint64_t* empty = full + kGemmStages;
-  uint64_t* tfull = empty + kGemmStages;  // [2]
-  uint64_t* tempty = tfull + 2;           // [2]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
-  volatile int* s_abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int tiles_n = CeilDiv(N, kGemmBN), tiles = tiles_n * CeilDiv(M, kUmmaBM);
-  const int nk = CeilDiv(K, kUmmaBK);
-
-  if (threadIdx.x == 0) {
-    for (int s = 0; s < kGemmStages; s++) {
-      MbarInit(&full[s], 1);
-      MbarInit(&empty[s], 1);
-    }
-    for (int b = 0; b < 2; b++) {
-      MbarInit(&tfull[b], 1);
-      MbarInit(&tempty[b], 4);
-    }
-    *s_abort = 0;
-    FenceMbarInit();
-    PrefetchTmaDesc(&ta);
-    PrefetchTmaDesc(&tb);
-  }
-  __syncwarp();
-  if (warp == 1) {
-    TmemAlloc(tmem_slot, 2 * kGemmBN);
-    TmemRelinquish();
-  }
-  TcgenFenceBefore();
-  __syncthreads();
-  TcgenFenceAfter();
-  const uint32_t tmem = *tmem_slot;
-
-  if (warp == 0) {
-    if (lane == 0) {
-      int it = 0;
-      for (int t = blockIdx.x; t < tiles && !*s_abort; t += gridDim.x) {
-        const int m0 = (t / tiles_n) * kUmmaBM, n0 = (t % tiles_n) * kGemmBN;
-        for (int kb = 0; kb < nk; kb++, it++) {
-          const int s = it % kGemmStages;
-          if (!MbarWaitBounded(&empty[s], ((it / kGemmStages) & 1) ^ 1, kWaitLimit)) {
-            atomicCAS(&g_shahd_device_error, 0, kDevErrGemmTimeout);
-            *s_abort = 1;
-            break;
-          }
-          uint8_t* sa = smem + s * kGemmStageBytes;
-          MbarArriveExpectTx(&full[s], kGemmStageBytes);
-          TmaLoad2D(sa, &ta, &full[s], kb * kUmmaBK, m0);
-          TmaLoad2D(sa + kUmmaBM * kUmmaBK * 2, &tb, &full[s], kb * kUmmaBK, n0);
-        }
-      }
-    }
-  } else if (warp == 1) {
-    if (lane == 0) {
-      const uint32_t idesc = UmmaIdescBf16(kUmmaBM, kGemmBN);
-      int it = 0, tc = 0;
-      for (int t = blockIdx.x; t < tiles && !*s_abort; t += gridDim.x, tc++) {
-        const int buf = tc & 1;
-        if (!MbarWaitBounded(&tempty[buf], ((tc >> 1) & 1) ^ 1, kWaitLimit)) {
-          atomicCAS(&g_shahd_device_error, 0, kDevErrGemmTimeout);
-          *s_abort = 1;
-          break;
-        }
-        TcgenFenceAfter();
-        const uint32_t d = tmem + (uint32_t)(buf * kGemmBN);
-        for (int kb = 0; kb < nk; kb++, it++) {
-          const int s = it % kGemmStages;
-          if (!MbarWaitBounded(&full[s], (it / kGemmStages) & 1, kWaitLimit)) {
-            atomicCAS(&g_shahd_device_error, 0, kDevErrGemmTimeout);
-            *s_abort = 1;
-            break;
-          }
-          TcgenFenceAfter();
-          uint8_t* sa = smem + s * kGemmStageBytes;
-          const uint64_t ad = SmemDescSw128(SmemAddr(sa));
-          const uint64_t bd = SmemDescSw128(SmemAddr(sa + kUmmaBM * kUmmaBK * 2));
-#pragma unroll
-          for (int kk = 0; kk < kUmmaBK / 16; kk++)
-            UmmaBf16(d, ad + (uint64_t)(kk * 2), bd + (uint64_t)(kk * 2), idesc, (kb > 0 || kk > 0) ? 1u : 0u);
-          UmmaCommit(&empty[s]);
-        }
-        if (*s_abort) break;
-        UmmaCommit(&tfull[buf]);
-      }
-    }
-  } else {
-    // epilogue warps 2..5 own TMEM lane quadrants (warp % 4)
-    const int quad = warp & 3;
-    int tc = 0;
-    for (int t = blockIdx.x; t < tiles; t += gridDim.x, tc++) {
-      const int buf = tc & 1;
-      if (!MbarWaitBounded(&tfull[buf], (tc >> 1) & 1, kWaitLimit)) {
-        if (lane == 0) atomicCAS(&g_shahd_device_error, 0, kDevErrGemmTimeout);
-        *s_abort = 1;
-        break;
-      }
-      TcgenFenceAfter();
-      const int m0 = (t / tiles_n) * kUmmaBM, n0 = (t % tiles_n) * kGemmBN;
-      const int row = m0 + quad * 32 + lane;
-#pragma unroll 1
-      for (int c = 0; c < kGemmBN; c += 16) {
-        uint32_t u[16];
-        TmemLoad16(tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)(buf * kGemmBN + c), u);
-        TmemWaitLd();
-        if (row < M) {
-          float* o = out + (size_t)row * N + n0 + c;
-          if (n0 + c + 16 <= N && (N & 3) == 0) {
-#pragma unroll
-            for (int j = 0; j < 16; j += 4) {
-              float4 v = make_float4(__uint_as_float(u[j]), __uint_as_float(u[j + 1]), __uint_as_float(u[j + 2]),
-                                     __uint_as_float(u[j + 3]));
-              if (acc) {
-                const float4 p = *reinterpret_cast<const float4*>(o + j);
-                v.x += p.x; v.y += p.y; v.z += p.z; v.w += p.w;
-              }
-              *reinterpret_cast<float4*>(o + j) = v;
-            }
-          } else {
-            for (int j = 0; j < 16; j++)
-              if (n0 + c + j < N) o[j] = acc ? o[j] + __uint_as_float(u[j]) : __uint_as_float(u[j]);
-          }
-        }
-      }
-      TcgenFenceBefore();
-      __syncwarp();
-      if (lane == 0) MbarArrive(&tempty[buf]);
-    }
-  }
-  TcgenFenceBefore();
-  __syncthreads();
-  __syncwarp();
-  if (warp == 1) TmemDealloc(tmem, 2 * kGemmBN);
-}
+// ---- tcgen05 GEMM, both operands by TMA, warp-specialized, persistent: LinearPersistKernel (gemm_persist.cuh)
+// with an fp32 output epilogue ----------------------------------------------------------------------------
 
 static int NumSMs(int dev) {
   static int cache[64] = {0};
@@ -429,24 +286,21 @@ int GemmNtBf16(const void* a, const void* bt, float* out, int m, int k, int n, i
     SetError("ShahdMatMulNTBF16Device: K=%d must be a multiple of 8 (16-byte rows for TMA)", k);
     return SHAHD_EINVAL;
   }
-  CUtensorMap ta, tb;
-  if (!MakeTmaBf16(a, m, k, k, kUmmaBM, &ta) || !MakeTmaBf16(bt, n, k, k, kGemmBN, &tb)) {
-    SetError("ShahdMatMulNTBF16Device: cuTensorMapEncodeTiled failed");
-    return SHAHD_ECUDA;
-  }
-  if (!EnsureKernelAttrs((const void*)GemmNtBf16Kernel, kGemmSmem)) {
-    TakeLaunchError(nullptr);
-    SetError("ShahdMatMulNTBF16Device: the GEMM kernel's shared-memory limit could not be set");
-    return SHAHD_ECUDA;
-  }
-  int dev = 0;
-  cudaGetDevice(&dev);
-  const int tiles = CeilDiv(n, kGemmBN) * CeilDiv(m, kUmmaBM);
-  const int grid = tiles < NumSMs(dev) ? tiles : NumSMs(dev);
-  GemmNtBf16Kernel<<<grid, kGemmThreads, kGemmSmem, st>>>(ta, tb, out, m, n, k, acc);
-  cudaError_t e = cudaGetLastError();
+  LinearArgs la{};
+  la.ab = static_cast<const bf16*>(a);
+  la.ldab = k;
+  la.a_rows = m;
+  la.M = m;
+  la.K = k;
+  la.Kp = k;
+  la.w = static_cast<const bf16*>(bt);
+  la.N = n;
+  TakeLaunchError(nullptr);
+  LaunchPersistLinear<kNormNone, EpiF32Out>(la, EpiF32Out{out, n, acc}, st);
+  std::string what;
+  const cudaError_t e = TakeLaunchError(&what);
   if (e != cudaSuccess) {
-    SetError("ShahdMatMulNTBF16Device: launch failed: %s", cudaGetErrorString(e));
+    SetError("ShahdMatMulNTBF16Device: %s failed: %s", what.c_str(), cudaGetErrorString(e));
     return SHAHD_ECUDA;
   }
   return SHAHD_OK;
@@ -500,6 +354,7 @@ void ShahdSetPersistentStep(int enable) { g_persistent_step = enable != 0; }
 void ShahdSetTensorCorePrefillAttention(int enable) { g_umma_prefill_attn = enable != 0; }
 void ShahdSetDecodeAttentionKernel(int mode) { g_decode_attn_kernel = mode < 0 || mode > 3 ? 0 : mode; }
 void ShahdSetFusedAttentionBlock(int enable) { g_fused_attn_block = enable != 0; }
+void ShahdSetPersistentPrefillProjections(int enable) { g_persist_linear = enable != 0; }
 
 int ShahdDeviceErrorFlag(void) {
   int v = 0;

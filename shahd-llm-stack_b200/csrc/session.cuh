@@ -25,6 +25,7 @@
 #include "prefill_attention_umma.cuh"
 #include "attn_pages.cuh"
 #include "attn_block.cuh"
+#include "gemm_persist.cuh"
 #include "sampling.cuh"
 #include "decode_loop.cuh"
 #include "umma_linear.cuh"
@@ -114,6 +115,7 @@ struct ShahdSession {
   int am_stride;
   float *part_o, *part_m, *part_l;
   int* attn_counter;
+  float* row_stats = nullptr;  // [rows_cap][2] norm statistics of the prefill rows (persistent projections)
   bool ab_ok = false;  // the model's shape fits the fused attention block (one kv head's weights next to a second CTA)
   // persistent cluster decode loop: weight tensor maps (box 64 x 128) and per-layer constants in device memory
   int loop_state = -1;  // -1 not set up yet, 0 unavailable for this model/device, 1 ready
@@ -209,6 +211,14 @@ void LaunchSimt(const LinearArgs& la, const Epi& epi, cudaStream_t st) {
 
 template <int NORM, class Epi>
 void LaunchLinearNorm(const LinearArgs& la, const Epi& epi, cudaStream_t st) {
+  if constexpr (PersistUsed<NORM, Epi>::value) {
+    // batched prefill rows: the persistent warp-specialized kernel (norm statistics precomputed)
+    if (g_persist_linear && la.M > kUmmaBM && la.M >= kUmmaMinRows && UmmaLinearSupported(la) &&
+        (NORM == kNormNone || la.stats != nullptr)) {
+      LaunchPersistLinear<NORM, Epi>(la, epi, st);
+      return;
+    }
+  }
   if (la.M >= kUmmaMinRows && UmmaLinearSupported(la)) {
     LaunchUmmaLinear<NORM, Epi>(la, epi, st);
   } else if (la.M <= 1) {
@@ -225,6 +235,10 @@ void LaunchLinear(int norm, const LinearArgs& la, const Epi& epi, cudaStream_t s
   if (norm == kNormRms) LaunchLinearNorm<kNormRms, Epi>(la, epi, st);
   else if (norm == kNormLayer) LaunchLinearNorm<kNormLayer, Epi>(la, epi, st);
   else LaunchLinearNorm<kNormNone, Epi>(la, epi, st);
+}
+
+void LaunchRowStats(const float* x, int ldx, int K, int M, int norm, float eps, float* stats, cudaStream_t st) {
+  LaunchPdl(RowStatsKernel, dim3(CeilDiv(M, 8)), dim3(256), 0, st, x, ldx, K, M, norm, eps, stats);
 }
 
 // Number of argmax partial blocks the head launch produces per row.
@@ -482,6 +496,9 @@ int EnqueueStep(ShahdSession* s, const StepPlan& p, cudaStream_t st, int r0 = 0,
     const bool pages_kernel = dec_rows && (g_decode_attn_kernel == 3 || (g_decode_attn_kernel == 0 && long_rows));
     const bool rows_kernel = dec_rows && !pages_kernel && g_decode_attn_kernel != 2;
     const int rsplit = RowSplits(s, M, r0);
+    // batched prefill rows: norm-consuming projections on the persistent kernel after a row-statistics pass
+    const bool persist = g_persist_linear && M > kUmmaBM && M >= kUmmaMinRows;
+    float* stats = s->row_stats + 2 * (size_t)r0;
     // decode rows that fill the SMs without position splits (any cached length): the attention half of each
     // layer in one launch
     const bool fused_block = dec_rows && UsesFusedBlock(s, M, r0);
@@ -500,7 +517,11 @@ int EnqueueStep(ShahdSession* s, const StepPlan& p, cudaStream_t st, int r0 = 0,
               chain);
       } else {
         // norm1 + QKV + RoPE + KV append (CachedForward.ts:66-73, :78-79)
-        const LinearArgs la = Lin(x, s->E, xb, s->Ep, R, M, s->E, s->Ep, Ly.w_qkv, s->Nqkv, eps, Ly.qkv_c1, Ly.qkv_c2);
+        LinearArgs la = Lin(x, s->E, xb, s->Ep, R, M, s->E, s->Ep, Ly.w_qkv, s->Nqkv, eps, Ly.qkv_c1, Ly.qkv_c2);
+        if (persist) {
+          Timed(s, st, pk + kProfLinear, 8.0 * M * s->E, [&] { LaunchRowStats(x, s->E, s->E, M, norm, eps, stats, st); });
+          la.stats = stats;
+        }
         const EpiQKV eq{q, kv, l, pos, p.slot, s->rope_cos, s->rope_sin, s->H, s->Hk, s->d};
         Timed(s, st, pk + kProfLinear, LinearBytes(M, s->E, s->Ep, s->Nqkv), [&] { LaunchLinear(norm, la, eq, st); });
         // attention over the cache (CachedForward.ts:76-80)
@@ -536,7 +557,11 @@ int EnqueueStep(ShahdSession* s, const StepPlan& p, cudaStream_t st, int r0 = 0,
               [&] { LaunchLinear(kNormNone, lo, EpiResid{x, xb, s->E, s->Ep, nullptr}, st); });
       }
       // norm2 + MLP + residual (CachedForward.ts:86-87)
-      const LinearArgs lu = Lin(x, s->E, xb, s->Ep, R, M, s->E, s->Ep, Ly.w_up, s->Nup, eps, Ly.up_c1, Ly.up_c2);
+      LinearArgs lu = Lin(x, s->E, xb, s->Ep, R, M, s->E, s->Ep, Ly.w_up, s->Nup, eps, Ly.up_c1, Ly.up_c2);
+      if (persist) {
+        Timed(s, st, pk + kProfLinear, 8.0 * M * s->E, [&] { LaunchRowStats(x, s->E, s->E, M, norm, eps, stats, st); });
+        lu.stats = stats;
+      }
       Timed(s, st, pk + kProfLinear, LinearBytes(M, s->E, s->Ep, s->Nup), [&] {
         if (s->cfg.mlp_kind == 0) LaunchLinear(norm, lu, EpiReluFc{act, actb, s->F, s->Fp, Ly.b_fc}, st);
         else LaunchLinear(norm, lu, EpiGated{act_f32, actb, s->F, s->Fp, s->cfg.mlp_kind == 2}, st);
@@ -1456,6 +1481,7 @@ extern "C" int shahd_session_create(const ShahdModelCfg* cfg, const void* params
       (rc = DevAlloc(s, &s->part_m, (size_t)R * s->H * s->max_blocks)) != SHAHD_OK ||
       (rc = DevAlloc(s, &s->part_l, (size_t)R * s->H * s->max_blocks)) != SHAHD_OK ||
       (rc = DevAlloc(s, &s->attn_counter, (size_t)R * s->Hk)) != SHAHD_OK ||
+      (rc = DevAlloc(s, &s->row_stats, 2 * RC)) != SHAHD_OK ||
       (rc = DevAlloc(s, &s->d_slot, (size_t)R)) != SHAHD_OK || (rc = DevAlloc(s, &s->d_tok, (size_t)R)) != SHAHD_OK ||
       (rc = DevAlloc(s, &s->d_pos, RC)) != SHAHD_OK ||  // one position per row, prefill rows included
       (rc = DevAlloc(s, &s->d_next, (size_t)R)) != SHAHD_OK ||

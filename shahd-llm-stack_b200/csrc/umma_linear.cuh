@@ -10,8 +10,8 @@
 // decode reduction is split over a cluster of CTAs that sum their partial tiles through distributed
 // shared memory.
 //
-// GemmNtBf16Kernel: out[M,N] (+)= A[M,K] · B[N,K]ᵀ with both operands bf16 in global memory, both
-// fed by TMA, warp-specialized (producer warp, MMA warp, 4 epilogue warps) — the MatMulNT operator.
+// The batched-prefill projections and the MatMulNT operator run the persistent warp-specialized kernel of
+// gemm_persist.cuh instead.
 //
 // Every mbarrier wait is bounded; on timeout the kernel records an error code in g_shahd_device_error,
 // skips the remaining work, releases its TMEM and returns.
