@@ -280,6 +280,8 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
         w = dataclasses.replace(w, seqs=args.seqs)
     if args.new_tokens is not None:
         w = dataclasses.replace(w, new_tokens=args.new_tokens)
+    if args.prompt_len is not None:
+        w = dataclasses.replace(w, prompt_len=args.prompt_len)
     cfg = w.model
     params = pkg.init_params(cfg, w.weight_seed)
     lib = pkg.load()
@@ -289,6 +291,8 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
         lib.ShahdSetTensorCoreMinRows(args.tc_min_rows)
     if args.fused_block >= 0:
         lib.ShahdSetFusedAttentionBlock(args.fused_block)
+    if args.decode_attn >= 0:
+        lib.ShahdSetDecodeAttentionKernel(args.decode_attn)
     # a KV pool of the job's size: every sequence's pages up to prompt + new positions (Phase2Modern-style:
     # 4096 x 16 pages of 1 MiB = 64 GiB on one GPU)
     kv_pages = w.seqs * -(-min(w.prompt_len + w.new_tokens, cfg.block_size) // 64)
@@ -348,7 +352,7 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
         if rank == 0:
             print(json.dumps({"ms_per_step": ms_per_step, "value": value, "gpu_launches": int(launches),
                               "chains": args.chains, "tc_min_rows": args.tc_min_rows,
-                              "fused_block": args.fused_block}), flush=True)
+                              "fused_block": args.fused_block, "decode_attn": args.decode_attn}), flush=True)
         return
 
     # gather per-rank output checksums (the only collective, outside the timed region)
@@ -429,7 +433,8 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
     expected = None
     gpath = os.path.join(ROOT, "tests", "golden", "microchat_job.json")
     mc = pkg.configs.MICROCHAT
-    if (w.name, w.seqs, w.new_tokens) == (mc.name, mc.seqs, mc.new_tokens) and rank == 0 and os.path.exists(gpath):
+    if ((w.name, w.seqs, w.prompt_len, w.new_tokens) == (mc.name, mc.seqs, mc.prompt_len, mc.new_tokens) and rank == 0
+            and os.path.exists(gpath)):
         with open(gpath) as f:
             expected = json.load(f)["checksum"]
     output_check = {"expected_checksum_per_rank": expected,
@@ -712,6 +717,10 @@ def main() -> None:
                     help="time the steps only (no e2e, profile or CPU legs): the profiling command line")
     ap.add_argument("--chains", type=int, default=0, help="concurrent decode chains (0 = library default)")
     ap.add_argument("--tc-min-rows", type=int, default=0, help="rows from which projections use tensor cores (0 = default)")
+    ap.add_argument("--decode-attn", type=int, default=-1, choices=[-1, 0, 1, 2, 3],
+                    help="decode attention kernel (ShahdSetDecodeAttentionKernel); -1 keeps the library default")
+    ap.add_argument("--prompt-len", type=int, default=None,
+                    help="override the prompt length (profiling a short job at a long cached length)")
     ap.add_argument("--fused-block", type=int, default=-1, choices=[-1, 0, 1],
                     help="decode rows run the fused attention block where the model fits it (1) or the three-launch "
                          "chain (0); -1 keeps the library default")

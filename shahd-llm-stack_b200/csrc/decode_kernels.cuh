@@ -225,6 +225,18 @@ struct EpiResid {
   }
 };
 
+// The gate activations (SiluValue, Silu.ts:8-10: g / (1 + e^-g); GeluValue, Gelu.ts:7-14: the tanh form
+// 0.5 g (1 + tanh(sqrt(2/pi) (g + 0.044715 g^3)))) with tanh(u) = 1 - 2 / (1 + e^(2u)), from __expf and the
+// approximate divide (a few ulp, far below the bf16 rounding of the result); both saturate correctly (an
+// infinite exponential gives a zero quotient).
+__device__ __forceinline__ float GateAct(float g, int gelu) {
+  if (gelu) {
+    const float u = 0.7978845608028654f * (g + 0.044715f * g * g * g);  // sqrt(2/pi) (g + 0.044715 g^3)
+    return 0.5f * g * (2.0f - __fdividef(2.0f, 1.0f + __expf(2.0f * u)));
+  }
+  return __fdividef(g, 1.0f + __expf(-g));
+}
+
 // Gated MLP hidden: act[j] = Act(x·W1[:,j]) * (x·W3[:,j]) with W1/W3 interleaved per column pair
 // (MlpRow, CachedRowMath.ts:107-112; SiluValue Silu.ts:8-10; GeluValue Gelu.ts:7-14).
 struct EpiGated {
@@ -233,14 +245,7 @@ struct EpiGated {
   int F, ldb;
   int gelu;
   __device__ __forceinline__ void apply(int m, int n, float g, float u, int N) const {
-    float a;
-    if (gelu) {
-      const float c = 0.7978845608028654f;  // sqrt(2/pi)
-      a = 0.5f * g * (1.0f + tanhf(c * (g + 0.044715f * g * g * g)));
-    } else {
-      a = g * (1.0f / (1.0f + __expf(-g)));
-    }
-    const float h = a * u;
+    const float h = GateAct(g, gelu) * u;
     if (act) act[(size_t)m * F + (n >> 1)] = h;
     actb[(size_t)m * ldb + (n >> 1)] = __float2bfloat16_rn(h);
   }
@@ -251,15 +256,7 @@ struct EpiGated {
     float h[8];
 #pragma unroll
     for (int i = 0; i < 8; i++) {
-      const float g = v[2 * i], u = v[2 * i + 1];
-      float a;
-      if (gelu) {
-        const float c = 0.7978845608028654f;  // sqrt(2/pi)
-        a = 0.5f * g * (1.0f + tanhf(c * (g + 0.044715f * g * g * g)));
-      } else {
-        a = g * (1.0f / (1.0f + __expf(-g)));
-      }
-      h[i] = a * u;
+      h[i] = GateAct(v[2 * i], gelu) * v[2 * i + 1];
     }
     if (act) StoreNf<8>(act + (size_t)m * F + (n >> 1), h);
     StoreNbf<8>(actb + (size_t)m * ldb + (n >> 1), h);

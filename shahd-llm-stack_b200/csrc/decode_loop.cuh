@@ -965,13 +965,7 @@ __global__ void __launch_bounds__(kLoopThreads, 1) DecodeLoopKernel(const __grid
                 const float h = (r < nrows && fok) ? fmaxf(v + bfc, 0.f) : 0.f;
                 *reinterpret_cast<bf16*>(actb + (size_t)uu * 2 * kLoopOpBlock + OpOffset(r, fl)) = __float2bfloat16_rn(h);
               } else if ((fl & 1) == 0) {
-                float a;
-                if (D.mlp_kind == 2) {
-                  const float cg = 0.7978845608028654f;  // sqrt(2/pi), Gelu.ts:7-14
-                  a = 0.5f * v * (1.0f + tanhf(cg * (v + 0.044715f * v * v * v)));
-                } else {
-                  a = v * (1.0f / (1.0f + __expf(-v)));  // SiluValue, Silu.ts:8-10
-                }
+                const float a = GateAct(v, D.mlp_kind == 2);  // GeluValue (Gelu.ts:7-14) / SiluValue (Silu.ts:8-10)
                 const float h = (r < nrows && fok) ? a * partner : 0.f;
                 *reinterpret_cast<bf16*>(actb + (size_t)uu * kLoopOpBlock + OpOffset(r, fl >> 1)) = __float2bfloat16_rn(h);
               }
