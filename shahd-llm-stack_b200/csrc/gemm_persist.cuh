@@ -9,8 +9,8 @@
 //     k-block into a ring of stages (128-byte swizzle, K-major);
 //   warp 1 (one thread): tcgen05.mma kind::f16 (M 128, N BN, K 16) into one of two TMEM accumulators, so the
 //     next tile's MMAs run while the epilogue drains the previous one;
-//   warps 2-9: the epilogue, two warps per TMEM lane quadrant (32 rows), each on half of the tile's
-//     columns: tcgen05.ld of 16-column chunks, the row's norm statistics (precomputed by RowStatsKernel from
+//   warps 2..: the epilogue, two or four warps per TMEM lane quadrant (32 rows), each on a part of the
+//     tile's columns: tcgen05.ld of 16-column chunks, the row's norm statistics (precomputed by RowStatsKernel from
 //     the fp32 residual), the fused epilogue functor; the epilogue's global reads (residual, RoPE rows, KV
 //     page lookups) are issued before the accumulator is waited for.
 // Every mbarrier wait is bounded; on timeout the kernel records an error, stops issuing work, frees its
@@ -30,8 +30,14 @@ struct PersistCfg {
   static constexpr int kSmem = kStages * kStageBytes + 1024 /*align*/ + 512 /*barriers*/;
   static constexpr uint32_t kTmemCols = 2 * BN;  // two accumulators
 };
-constexpr int kPersistEpiWarps = 8;
-constexpr int kPersistThreads = 64 + 32 * kPersistEpiWarps;
+// Epilogue warps: sixteen for epilogues that read nothing before the accumulator (the gated MLP, whose
+// activation math is the longest part of a tile), eight for those whose early reads hold registers.
+template <class Epi>
+struct PersistEpi {
+  static constexpr int kWarps = sizeof(typename Epi::Pre) <= 1 ? 16 : 8;
+  static constexpr int kThreads = 64 + 32 * kWarps;
+  static constexpr int kColParts = kWarps / 4;  // epilogue warps per TMEM lane quadrant (column parts)
+};
 
 // fp32 output rows (MatMulNT: out = A.B^T, or out += A.B^T when acc)
 struct EpiF32Out {
@@ -86,14 +92,17 @@ __global__ void __launch_bounds__(256) RowStatsKernel(const float* x, int ldx, i
 }
 
 template <int NORM, class Epi, int BN>
-__global__ void __launch_bounds__(kPersistThreads, 1)
+__global__ void __launch_bounds__(PersistEpi<Epi>::kThreads, 1)
     LinearPersistKernel(LinearArgs la, Epi epi, const __grid_constant__ CUtensorMap tmap_a,
                         const __grid_constant__ CUtensorMap tmap_w) {
   using P = PersistCfg<BN>;
   constexpr int S = P::kStages;
-  constexpr int kChunksW = BN / 32;  // 16-column chunks per epilogue warp (half of the tile's columns)
+  constexpr int kEpiWarps = PersistEpi<Epi>::kWarps;
+  constexpr int kColsW = BN / PersistEpi<Epi>::kColParts;  // columns of the tile per epilogue warp
+  constexpr int kChunksW = kColsW / 16;          // 16-column chunks per epilogue warp
   // chunks whose epilogue reads are in flight together: fewer when they hold many registers
-  constexpr int kGroup = (NORM == kNormLayer || sizeof(typename Epi::Pre) > 64) ? 2 : 4;
+  constexpr int kGroupW = (NORM == kNormLayer || sizeof(typename Epi::Pre) > 64) ? 2 : 4;
+  constexpr int kGroup = kGroupW < kChunksW ? kGroupW : kChunksW;
   static_assert(kChunksW % kGroup == 0, "whole groups per warp");
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -114,7 +123,7 @@ __global__ void __launch_bounds__(kPersistThreads, 1)
     }
     for (int b = 0; b < 2; b++) {
       MbarInit(&tfull[b], 1);
-      MbarInit(&tempty[b], kPersistEpiWarps);
+      MbarInit(&tempty[b], kEpiWarps);
     }
     *s_abort = 0;
     FenceMbarInit();
@@ -187,13 +196,13 @@ __global__ void __launch_bounds__(kPersistThreads, 1)
       }
     }
   } else {
-    // epilogue: warps 2..9, TMEM lane quadrant warp % 4, column half (warp - 2) / 4
-    const int quad = warp & 3, half = (warp - 2) >> 2;
+    // epilogue: warps 2.., TMEM lane quadrant warp % 4, column part (warp - 2) / 4
+    const int quad = warp & 3, part = (warp - 2) >> 2;
     const bool vec = epi.vec_ok(la.N);
     int tc = 0;
     for (int t = blockIdx.x; t < tiles; t += gridDim.x, tc++) {
       const int buf = tc & 1;
-      const int m0 = (t / tiles_n) * kUmmaBM, n0 = (t % tiles_n) * BN + half * (BN / 2);
+      const int m0 = (t / tiles_n) * kUmmaBM, n0 = (t % tiles_n) * BN + part * kColsW;
       const int row = m0 + quad * 32 + lane;
       const bool row_ok = row < la.M;
       float mu = 0.f, is = 1.f;
@@ -215,7 +224,7 @@ __global__ void __launch_bounds__(kPersistThreads, 1)
         break;
       }
       TcgenFenceAfter();
-      const uint32_t trow = tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)(buf * BN + half * (BN / 2));
+      const uint32_t trow = tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)(buf * BN + part * kColsW);
 #pragma unroll
       for (int g = 0; g < kChunksW; g += kGroup) {
         uint32_t u[kGroup][16];
@@ -305,8 +314,8 @@ bool LaunchPersistLinearBN(const LinearArgs& la, const Epi& epi, cudaStream_t st
   if (!EnsureKernelAttrs((const void*)LinearPersistKernel<NORM, Epi, BN>, PersistCfg<BN>::kSmem)) return false;
   const int tiles = CeilDiv(la.N, BN) * CeilDiv(la.M, kUmmaBM);
   const int grid = std::min(tiles, NumSmsOfCurrentDevice());
-  LaunchPdl(LinearPersistKernel<NORM, Epi, BN>, dim3(grid), dim3(kPersistThreads), PersistCfg<BN>::kSmem, st, la, epi,
-            ta, tw);
+  LaunchPdl(LinearPersistKernel<NORM, Epi, BN>, dim3(grid), dim3(PersistEpi<Epi>::kThreads), PersistCfg<BN>::kSmem, st,
+            la, epi, ta, tw);
   return true;
 }
 
