@@ -90,10 +90,8 @@ void ShahdSetTensorCorePrefillAttention(int enable);
 /* Decode-row attention kernel: 0 automatic (default: page streaming for rows attending >= 384 cached
  * positions on average when rows x kv heads fill the SMs, read-ahead rows otherwise), 1 the read-ahead rows
  * kernel (32-position warp tasks, K/V rows in registers), 2 the page-ring kernel (64-position pages by bulk
- * copies into a three-page ring, block-wide phases), 3 the page-streaming kernel (a producer warp streams
- * pages into a six-page ring, one page per compute warp, no block-wide barrier per page; for head_dim 64 the
- * pages come by TMA in the 128-byte swizzled layout and Q.K^T and P.V run as mma tiles with the kv head's
- * query heads as one 8-wide side), 4 the page-streaming kernel on CUDA cores for every head_dim. Results agree
+ * copies into a three-page ring, block-wide phases), 3 the page-streaming kernel (a producer warp's bulk
+ * copies into a six-page ring, one page per compute warp, no block-wide barrier per page). Results agree
  * within the parity tolerance. Process-wide tuning hook; no counterpart in the reference. */
 void ShahdSetDecodeAttentionKernel(int mode);
 /* Fused decode attention block: for decode rows whose rows x kv heads fill the SMs, and models whose Q/K/V

@@ -325,11 +325,11 @@ int shahd_attention_decode(ShahdAttention* a, const float* q, const float* k, co
                     a->scale, a->max_blocks, a->part_o, a->part_m, a->part_l, a->counter};
   // the decode session's choice: long rows over a grid that fills the SMs stream pages, others read ahead
   const bool long_rows = attended >= (long long)kApMinMeanLen * n && n * a->Hk >= a->num_sms;
-  const bool pages = g_decode_attn_kernel >= 3 || (g_decode_attn_kernel == 0 && long_rows);
+  const bool pages = g_decode_attn_kernel == 3 || (g_decode_attn_kernel == 0 && long_rows);
   if (pages) {
     int nsplit = 1;
     if (n * a->Hk < a->num_sms) nsplit = std::max(1, std::min(a->max_blocks, CeilDiv(3 * a->num_sms, n * a->Hk)));
-    LaunchAttnPages(a->d, a->G, dim3(nsplit, a->Hk, n), st, aa, a->kv_tmap_ok ? &a->kv_tmap : nullptr, 1);
+    LaunchAttnPages(a->d, a->G, dim3(nsplit, a->Hk, n), st, aa);
   } else {
     int rsplit = 1;
     if (n * a->Hk < a->num_sms) rsplit = std::max(1, std::min(a->max_blocks, CeilDiv(2 * a->num_sms, n * a->Hk)));

@@ -20,7 +20,7 @@ int g_umma_min_rows = 17;
 bool g_use_pdl = true;
 int g_decode_chains = 0;  // 0 = automatic
 int g_umma_prefill_attn = 1;
-int g_decode_attn_kernel = 0;  // decode-row attention: 0 automatic, 1 read-ahead rows, 2 page ring, 3 page streaming, 4 page streaming on CUDA cores
+int g_decode_attn_kernel = 0;  // decode-row attention: 0 automatic, 1 read-ahead rows, 2 page ring, 3 page streaming  // causal prefill attention of head_dim 64 on the tensor cores
 int g_persistent_step = 0;  // 1: greedy generate runs its decode steps in the persistent cluster loop
 int g_fused_attn_block = 0;
 int g_persist_linear = 1;  // batched prefill projections on the persistent warp-specialized tcgen05 kernel  // decode rows: norm + QKV + RoPE + attention + O projection in one launch where it fits
@@ -352,7 +352,7 @@ void ShahdSetDecodeChains(int chains) { g_decode_chains = chains < 0 ? 0 : chain
 
 void ShahdSetPersistentStep(int enable) { g_persistent_step = enable != 0; }
 void ShahdSetTensorCorePrefillAttention(int enable) { g_umma_prefill_attn = enable != 0; }
-void ShahdSetDecodeAttentionKernel(int mode) { g_decode_attn_kernel = mode < 0 || mode > 4 ? 0 : mode; }
+void ShahdSetDecodeAttentionKernel(int mode) { g_decode_attn_kernel = mode < 0 || mode > 3 ? 0 : mode; }
 void ShahdSetFusedAttentionBlock(int enable) { g_fused_attn_block = enable != 0; }
 void ShahdSetPersistentPrefillProjections(int enable) { g_persist_linear = enable != 0; }
 

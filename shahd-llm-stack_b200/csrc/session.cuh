@@ -347,18 +347,8 @@ void LaunchAttnPagesD(int G, dim3 grid, cudaStream_t st, const AttnArgs& aa) {
   else LaunchPdl(AttnPagesKernel<D, 8>, grid, dim3(kApThreads), ApSmemBytes(D, 8), st, aa);
 }
 
-// Decode-row attention streaming 64-position pages (head_dim 32, 64 or 128, G <= kMaxGroup). Head_dim 64 with
-// the pool's TMA map (`kvmap`, pages of `L` layers) runs the tensor-core page kernel unless the CUDA-core one is
-// selected (ShahdSetDecodeAttentionKernel(4)).
-void LaunchAttnPages(int d, int G, dim3 grid, cudaStream_t st, const AttnArgs& aa, const CUtensorMap* kvmap, int L) {
-  if (d == 64 && kvmap != nullptr && g_decode_attn_kernel != 4) {
-    const ApMmaArgs am{*kvmap, aa, L};
-    if (G == 1) LaunchPdl(AttnPagesMmaKernel<1>, grid, dim3(kApThreads), ApmSmemBytes(1), st, am);
-    else if (G == 2) LaunchPdl(AttnPagesMmaKernel<2>, grid, dim3(kApThreads), ApmSmemBytes(2), st, am);
-    else if (G <= 4) LaunchPdl(AttnPagesMmaKernel<4>, grid, dim3(kApThreads), ApmSmemBytes(4), st, am);
-    else LaunchPdl(AttnPagesMmaKernel<8>, grid, dim3(kApThreads), ApmSmemBytes(8), st, am);
-    return;
-  }
+// Decode-row attention streaming 64-position pages (head_dim 32, 64 or 128, G <= kMaxGroup).
+void LaunchAttnPages(int d, int G, dim3 grid, cudaStream_t st, const AttnArgs& aa) {
   if (d == 64) LaunchAttnPagesD<64>(G, grid, st, aa);
   else if (d == 32) LaunchAttnPagesD<32>(G, grid, st, aa);
   else LaunchAttnPagesD<128>(G, grid, st, aa);
@@ -366,11 +356,6 @@ void LaunchAttnPages(int d, int G, dim3 grid, cudaStream_t st, const AttnArgs& a
 
 template <int D>
 bool EnsureAttnPagesAttrs() {
-  if (D == 64 && !(EnsureKernelAttrs((const void*)AttnPagesMmaKernel<1>, ApmSmemBytes(1)) &&
-                   EnsureKernelAttrs((const void*)AttnPagesMmaKernel<2>, ApmSmemBytes(2)) &&
-                   EnsureKernelAttrs((const void*)AttnPagesMmaKernel<4>, ApmSmemBytes(4)) &&
-                   EnsureKernelAttrs((const void*)AttnPagesMmaKernel<8>, ApmSmemBytes(8))))
-    return false;
   return EnsureKernelAttrs((const void*)AttnPagesKernel<D, 1>, ApSmemBytes(D, 1)) &&
          EnsureKernelAttrs((const void*)AttnPagesKernel<D, 2>, ApSmemBytes(D, 2)) &&
          EnsureKernelAttrs((const void*)AttnPagesKernel<D, 4>, ApSmemBytes(D, 4)) &&
@@ -508,8 +493,7 @@ int EnqueueStep(ShahdSession* s, const StepPlan& p, cudaStream_t st, int r0 = 0,
     // the page-streaming kernel, the rest to the read-ahead rows kernel
     const bool dec_rows = p.pos_in == nullptr && s->G <= kMaxGroup && (s->d == 32 || s->d == 64 || s->d == 128);
     const bool long_rows = (double)p.attended >= (double)kApMinMeanLen * M && M * s->Hk >= s->num_sms;
-    const bool pages_kernel =
-        dec_rows && (g_decode_attn_kernel >= 3 || (g_decode_attn_kernel == 0 && long_rows));
+    const bool pages_kernel = dec_rows && (g_decode_attn_kernel == 3 || (g_decode_attn_kernel == 0 && long_rows));
     const bool rows_kernel = dec_rows && !pages_kernel && g_decode_attn_kernel != 2;
     const int rsplit = RowSplits(s, M, r0);
     // batched prefill rows: norm-consuming projections on the persistent kernel after a row-statistics pass
@@ -550,7 +534,7 @@ int EnqueueStep(ShahdSession* s, const StepPlan& p, cudaStream_t st, int r0 = 0,
         const dim3 pg(p.plan_qblocks, s->Hk, p.plan_n);
         Timed(s, st, pk + kProfAttention, attn_fixed, [&] {
           if (pages_kernel) {
-            LaunchAttnPages(s->d, s->G, ag, st, aa, s->kv_tmap_ok ? &s->kv_tmap : nullptr, s->L);
+            LaunchAttnPages(s->d, s->G, ag, st, aa);
           } else if (rows_kernel) {
             LaunchAttnRows(s->d, s->G, dim3(rsplit, s->Hk, M), s->num_sms, st, aa);
           } else if (tiled && s->d == kFaD && g_umma_prefill_attn && s->kv_tmap_ok) {

@@ -1,5 +1,5 @@
 """Decode-row attention launch shapes against the oracle (CachedForward.ts:76-84 per row), on each of the
-decode attention kernels.
+three decode attention kernels.
 
 The decode attention picks its launch from the step's rows and kv heads: one CTA per (row, kv head) when
 they fill the GPU, position splits merged through partials when they leave SMs idle. Each case below
@@ -24,9 +24,8 @@ CASES = [
 
 
 # 0: the automatic choice (read-ahead rows kernel at these lengths), 2: the page-ring kernel, 3: the
-# page-streaming kernel (producer warp, one page per compute warp; for head_dim 64 TMA pages and mma tiles),
-# 4: the page-streaming kernel on CUDA cores
-KERNELS = {"auto": 0, "page ring": 2, "page streaming": 3, "page streaming cuda cores": 4}
+# page-streaming kernel (producer warp, one page per compute warp)
+KERNELS = {"auto": 0, "page ring": 2, "page streaming": 3}
 
 
 @pytest.fixture
